@@ -1,0 +1,157 @@
+// Python bindings of the native sm_100a kernels (module tempname_5090_b200._C).
+// Every entry validates dtype/device/contiguity, takes the current CUDA stream
+// and raises on a failed launch; no entry point falls back to another backend.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "gemm/gemm_api.h"
+#include "kernels/kernels_api.h"
+#include "comm/comm_api.h"
+
+namespace {
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_bf16(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+}
+void check_rows(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with unit inner stride");
+}
+void raise_if(int code, const char* what) {
+  if (code == 0) return;
+  if (code < 0) TORCH_CHECK(false, what, ": ", tn5b::gemm::last_error());
+  TORCH_CHECK(false, what, ": ", cudaGetErrorString(cudaError_t(code)));
+}
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+int* status_ptr(const at::Tensor& s) {
+  check_cuda(s, "status");
+  TORCH_CHECK(s.scalar_type() == at::kInt && s.numel() >= 1, "status must be int32");
+  return s.data_ptr<int>();
+}
+
+// out = epilogue(A * B^T).  a_mn / b_mn select MN-major storage ([K,M] / [K,N]).
+void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor& out,
+          int64_t epi, const c10::optional<at::Tensor>& bias,
+          const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& residual,
+          const at::Tensor& status, int64_t bn, int64_t max_ctas,
+          const c10::optional<at::Tensor>& tile_order) {
+  check_bf16(A, "A"); check_bf16(B, "B"); check_bf16(out, "out");
+  check_rows(A, "A"); check_rows(B, "B"); check_rows(out, "out");
+  const c10::cuda::CUDAGuard guard(A.device());
+  tn5b::gemm::GemmCall c;
+  c.A = A.data_ptr(); c.lda = A.stride(0); c.a_mn = a_mn;
+  c.B = B.data_ptr(); c.ldb = B.stride(0); c.b_mn = b_mn;
+  c.M = int(a_mn ? A.size(1) : A.size(0));
+  const int64_t ka = a_mn ? A.size(0) : A.size(1);
+  c.N = int(b_mn ? B.size(1) : B.size(0));
+  const int64_t kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(ka == kb, "gemm: K mismatch ", ka, " vs ", kb);
+  c.K = int(ka);
+  TORCH_CHECK(out.size(0) == c.M && out.size(1) == c.N, "gemm: out must be [M, N]");
+  c.out = out.data_ptr(); c.ldo = out.stride(0);
+  c.epi = int(epi);
+  if (bias) { check_bf16(*bias, "bias"); TORCH_CHECK(bias->numel() == c.N && bias->is_contiguous()); c.bias = bias->data_ptr(); }
+  if (aux) { check_bf16(*aux, "aux"); check_rows(*aux, "aux"); c.aux = aux->data_ptr(); c.ld_aux = aux->stride(0); }
+  if (residual) { check_bf16(*residual, "residual"); check_rows(*residual, "residual"); c.residual = residual->data_ptr(); c.ld_res = residual->stride(0); }
+  if (tile_order) { check_cuda(*tile_order, "tile_order"); TORCH_CHECK(tile_order->scalar_type() == at::kInt); c.tile_order = tile_order->data_ptr<int>(); }
+  c.bn = int(bn);
+  c.max_ctas = int(max_ctas);
+  c.status = status_ptr(status);
+  raise_if(tn5b::gemm::run(c, stream()), "gemm");
+}
+
+// GEMM -> reduce-scatter push: tiles of A*B^T go to their owner rank's slot.
+void gemm_rs_push(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_t mode,
+                  int64_t recv_ptrs, int64_t flag_ptrs, int64_t rank, int64_t world,
+                  int64_t chunk_rows, int64_t epoch, int64_t slot_bytes,
+                  const at::Tensor& tile_order, const at::Tensor& status, int64_t timeout_ns,
+                  int64_t max_ctas) {
+  check_bf16(A, "A"); check_bf16(B, "B"); check_rows(A, "A"); check_rows(B, "B");
+  const c10::cuda::CUDAGuard guard(A.device());
+  tn5b::gemm::GemmCall c;
+  c.A = A.data_ptr(); c.lda = A.stride(0); c.a_mn = a_mn;
+  c.B = B.data_ptr(); c.ldb = B.stride(0); c.b_mn = b_mn;
+  c.M = int(a_mn ? A.size(1) : A.size(0));
+  c.N = int(b_mn ? B.size(1) : B.size(0));
+  const int64_t ka = a_mn ? A.size(0) : A.size(1);
+  const int64_t kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(ka == kb, "gemm_rs: K mismatch");
+  c.K = int(ka);
+  c.mode = int(mode);
+  c.rs_recv = reinterpret_cast<uint8_t* const*>(recv_ptrs);
+  c.rs_flags = reinterpret_cast<uint32_t* const*>(flag_ptrs);
+  c.rank = int(rank); c.world = int(world); c.chunk_rows = int(chunk_rows);
+  c.epoch = uint32_t(epoch); c.slot_bytes = slot_bytes;
+  check_cuda(tile_order, "tile_order");
+  TORCH_CHECK(tile_order.scalar_type() == at::kInt);
+  c.tile_order = tile_order.data_ptr<int>();
+  c.status = status_ptr(status);
+  c.timeout_ns = uint64_t(timeout_ns);
+  c.max_ctas = int(max_ctas);
+  raise_if(tn5b::gemm::run(c, stream()), "gemm_rs_push");
+}
+
+// All-gather -> GEMM: out = epilogue(gather(shards) * B^T); `gather` is this
+// rank's symmetric gather buffer [M, K] that peers push their shards into.
+void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor& B, bool b_mn,
+             at::Tensor& out, int64_t epi, const c10::optional<at::Tensor>& bias,
+             const c10::optional<at::Tensor>& aux, int64_t gather_ptrs, int64_t flag_ptrs,
+             int64_t local_flags, int64_t rank, int64_t world, int64_t target,
+             const at::Tensor& tile_order, const at::Tensor& status, int64_t timeout_ns,
+             int64_t bn) {
+  check_bf16(shard, "shard"); check_bf16(gather, "gather"); check_bf16(B, "B"); check_bf16(out, "out");
+  TORCH_CHECK(shard.is_contiguous() && gather.is_contiguous(), "shard/gather must be contiguous");
+  check_rows(B, "B"); check_rows(out, "out");
+  const c10::cuda::CUDAGuard guard(gather.device());
+  tn5b::gemm::GemmCall c;
+  c.A = gather.data_ptr(); c.lda = gather.stride(0); c.a_mn = 0;
+  c.B = B.data_ptr(); c.ldb = B.stride(0); c.b_mn = b_mn;
+  c.M = int(gather.size(0)); c.K = int(gather.size(1));
+  c.N = int(b_mn ? B.size(1) : B.size(0));
+  TORCH_CHECK((b_mn ? B.size(0) : B.size(1)) == c.K, "ag_gemm: K mismatch");
+  TORCH_CHECK(out.size(0) == c.M && out.size(1) == c.N, "ag_gemm: out must be [M, N]");
+  TORCH_CHECK(shard.numel() * world == gather.numel(), "ag_gemm: shard size mismatch");
+  c.out = out.data_ptr(); c.ldo = out.stride(0);
+  c.epi = int(epi);
+  if (bias) { check_bf16(*bias, "bias"); c.bias = bias->data_ptr(); }
+  if (aux) { check_bf16(*aux, "aux"); check_rows(*aux, "aux"); c.aux = aux->data_ptr(); c.ld_aux = aux->stride(0); }
+  c.ag = 1;
+  c.rank = int(rank); c.world = int(world);
+  c.ag_chunk_flags = reinterpret_cast<const uint32_t*>(local_flags);
+  c.ag_target = uint32_t(target);
+  c.ag_shard = shard.data_ptr();
+  c.ag_shard_bytes = shard.numel() * 2;
+  c.ag_gather = reinterpret_cast<uint8_t* const*>(gather_ptrs);
+  c.ag_peer_flags = reinterpret_cast<uint32_t* const*>(flag_ptrs);
+  check_cuda(tile_order, "tile_order");
+  c.tile_order = tile_order.data_ptr<int>();
+  c.status = status_ptr(status);
+  c.timeout_ns = uint64_t(timeout_ns);
+  c.bn = int(bn);
+  raise_if(tn5b::gemm::run(c, stream()), "ag_gemm");
+}
+
+int64_t gemm_grid(int64_t M, int64_t N, int64_t bn, int64_t mode) {
+  tn5b::gemm::GemmCall c;
+  c.M = int(M); c.N = int(N); c.bn = int(bn); c.mode = int(mode);
+  return tn5b::gemm::grid_ctas(c);
+}
+
+}  // namespace
+
+void register_kernels(pybind11::module& m);
+void register_comm(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "tempname_5090_b200 native sm_100a kernels";
+  m.def("gemm", &gemm, "tcgen05 BF16 GEMM with fused epilogue");
+  m.def("gemm_rs_push", &gemm_rs_push, "tcgen05 GEMM whose epilogue pushes tiles to owners");
+  m.def("ag_gemm", &ag_gemm, "all-gather fused into a tcgen05 GEMM");
+  m.def("gemm_grid", &gemm_grid, "persistent grid size of a GEMM call");
+  register_kernels(m);
+  register_comm(m);
+}

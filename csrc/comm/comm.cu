@@ -1,0 +1,222 @@
+// Receiver side of the fused GEMM -> reduce-scatter and the bounded-wait probe.
+//
+// Each rank's producer GEMM pushes tile (source=s) of destination d into d's
+// slot region and release-stores flag[s][tile] = epoch on d.  This kernel runs
+// on d after its own GEMM (same stream), waits (bounded) for every source's
+// tile flag and reduces in the fixed source order 0..W-1, rounding to BF16
+// after every source ("bf16_after_each_source", src/taco/codec.cu:155-196 of
+// TempName-5090).  Remote TACO packets are decoded in the same pass with the
+// reference decoder's FP32 operation sequence, so the output is bit-identical
+// to the reference's decode_reduce / reduce kernels.
+//
+// Consumption policies:
+//   ordered   CTA c takes tiles order[c], order[c+grid], ... and blocks on each.
+//   arrival   CTAs are split over two lanes (block-within-destination parity);
+//             each scans its lane's tiles and claims whichever is fully ready
+//             first (per-tile claim words tagged with the epoch).
+#include "comm_api.h"
+#include "../common/ptx.cuh"
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+namespace tn5b {
+namespace comm {
+
+namespace {
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr float kNorm = 0.08838834764831844055f;
+
+__device__ __forceinline__ uint2 ld_cg_v2(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_cg_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ld_cg_f32(const void* p) {
+  return __uint_as_float(ld_cg_u32(p));
+}
+
+// Reference decoder arithmetic for lane l's four coefficients 4l..4l+3.
+__device__ __forceinline__ void decode4(uint32_t raw, float quant, float adaptive, float (&o)[4]) {
+  const int lane = threadIdx.x & 31;
+  const __half2 lo(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(raw & 0xFFFFu), __NV_E4M3));
+  const __half2 hi(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(raw >> 16), __NV_E4M3));
+  float x[4] = {__fmul_rn(__low2float(lo), quant), __fmul_rn(__high2float(lo), quant),
+                __fmul_rn(__low2float(hi), quant), __fmul_rn(__high2float(hi), quant)};
+  float a = x[0], b = x[1], c = x[2], d = x[3];
+  x[0] = __fadd_rn(a, b); x[1] = __fsub_rn(a, b); x[2] = __fadd_rn(c, d); x[3] = __fsub_rn(c, d);
+  a = x[0]; b = x[1]; c = x[2]; d = x[3];
+  x[0] = __fadd_rn(a, c); x[1] = __fadd_rn(b, d); x[2] = __fsub_rn(a, c); x[3] = __fsub_rn(b, d);
+#pragma unroll
+  for (int stride = 1; stride < 32; stride *= 2) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float other = __shfl_xor_sync(0xffffffffu, x[j], stride);
+      x[j] = (lane & stride) ? __fsub_rn(other, x[j]) : __fadd_rn(x[j], other);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[j] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(x[j], kNorm) / adaptive));
+}
+
+__device__ __forceinline__ bool tile_ready(const RsReduceCall& c, int tile, int tiles) {
+  for (int s = 0; s < c.world; ++s)
+    if (int32_t(ld_acquire_sys(c.flags + int64_t(s) * tiles + tile) - c.epoch) < 0) return false;
+  return true;
+}
+
+// Reduce one producer tile (128 rows x tile_n cols) of the local output.
+__device__ void reduce_tile(const RsReduceCall& c, int tile, int tiles_n) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int tm = tile / tiles_n, tn = tile % tiles_n;
+  const int cols = min(c.tile_n, c.n - tn * c.tile_n);
+  const int groups_per_row = cols / 128;  // n, tile_n multiples of 128
+  const int total = 128 * groups_per_row;
+  const int64_t elems = int64_t(c.chunk_rows) * c.n;
+  const int64_t block_groups = elems / 128;
+  for (int gi = warp; gi < total; gi += kWarps) {
+    const int r = tm * 128 + gi / groups_per_row;
+    const int col = tn * c.tile_n + (gi % groups_per_row) * 128 + lane * 4;
+    const int64_t idx = int64_t(r) * c.n + col;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < c.world; ++s) {
+      float v[4];
+      const uint8_t* slot = c.recv + int64_t(s) * c.slot_bytes;
+      if (s == c.rank || !c.quantized) {
+        const uint2 raw = ld_cg_v2(slot + idx * 2);
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = __bfloat162float(h[j]);
+      } else {
+        const int blk = r / c.chunk_rows;
+        const int64_t g = (int64_t(r % c.chunk_rows) * c.n + (col - lane * 4)) / 128;
+        const uint8_t* pkt = slot + int64_t(blk) * (elems + 8 * block_groups);
+        const uint32_t raw = ld_cg_u32(pkt + g * 128 + lane * 4);
+        const float quant = ld_cg_f32(pkt + elems + 4 * g);
+        const float adaptive = ld_cg_f32(pkt + elems + 4 * block_groups + 4 * g);
+        decode4(raw, quant, adaptive, v);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(acc[j], v[j])));
+    }
+    if (c.residual) {
+      const uint2 rr = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(c.residual) + idx);
+      const __nv_bfloat16* rh = reinterpret_cast<const __nv_bfloat16*>(&rr);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float t = __bfloat162float(__float2bfloat16_rn(__fadd_rn(__bfloat162float(rh[j]), acc[j])));
+        if (c.bias) t = __fadd_rn(t, __bfloat162float(static_cast<const __nv_bfloat16*>(c.bias)[col + j]));
+        acc[j] = t;
+      }
+    } else if (c.bias) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        acc[j] = __fadd_rn(acc[j], __bfloat162float(static_cast<const __nv_bfloat16*>(c.bias)[col + j]));
+    }
+    __nv_bfloat162 o0 = __floats2bfloat162_rn(acc[0], acc[1]);
+    __nv_bfloat162 o1 = __floats2bfloat162_rn(acc[2], acc[3]);
+    uint2 ov;
+    ov.x = *reinterpret_cast<uint32_t*>(&o0);
+    ov.y = *reinterpret_cast<uint32_t*>(&o1);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(c.out) + idx) = ov;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_constant__ RsReduceCall c) {
+  const int tiles_n = (c.n + c.tile_n - 1) / c.tile_n;
+  const int tiles = (c.rows / 128) * tiles_n;
+  __shared__ int s_tile;
+  __shared__ int s_ok;
+  if (!c.arrival) {
+    for (int i = blockIdx.x; i < tiles; i += gridDim.x) {
+      const int tile = c.tile_order ? c.tile_order[i] : i;
+      if (threadIdx.x == 0) {
+        int ok = 1;
+        for (int s = 0; s < c.world && ok; ++s)
+          ok = wait_flag_geq(c.flags + int64_t(s) * tiles + tile, c.epoch, c.timeout_ns, c.status,
+                             kTimeoutPeerFlag);
+        s_ok = ok;
+      }
+      __syncthreads();
+      if (!s_ok) return;
+      reduce_tile(c, tile, tiles_n);
+      __syncthreads();
+    }
+    return;
+  }
+  // Arrival-first: lane = parity of the tile's block-within-destination.
+  const int lane_id = blockIdx.x & 1;
+  const uint64_t start = globaltimer_ns();
+  for (;;) {
+    if (threadIdx.x == 0) {
+      int found = -1, remaining = 0;
+      for (int i = 0; i < tiles; ++i) {
+        const int tile = c.tile_order ? c.tile_order[i] : i;
+        const int blk = (tile / tiles_n) * 128 / c.chunk_rows;
+        if ((blk & 1) != lane_id) continue;
+        const int old = *reinterpret_cast<volatile int*>(c.claims + tile);
+        if (int32_t(uint32_t(old) - c.epoch) >= 0) continue;  // already taken this epoch
+        ++remaining;
+        if (tile_ready(c, tile, tiles) && atomicCAS(c.claims + tile, old, int(c.epoch)) == old) {
+          found = tile;
+          break;
+        }
+      }
+      if (found < 0 && remaining == 0) found = -2;  // lane drained
+      if (found == -1 && globaltimer_ns() - start > c.timeout_ns) {
+        record_status(c.status, kTimeoutPeerFlag);
+        found = -2;
+      }
+      s_tile = found;
+    }
+    __syncthreads();
+    const int tile = s_tile;
+    __syncthreads();
+    if (tile == -2) return;
+    if (tile == -1) {
+      __nanosleep(200);
+      continue;
+    }
+    reduce_tile(c, tile, tiles_n);
+  }
+}
+
+// Bounded wait on a flag that nothing sets: lets tests check the timeout path
+// (status code returned, context still usable) without faulting a GPU.
+__global__ void wait_probe_kernel(const uint32_t* flag, uint32_t target, uint64_t timeout_ns,
+                                  int* status) {
+  if (threadIdx.x == 0 && blockIdx.x == 0)
+    wait_flag_geq(flag, target, timeout_ns, status, kTimeoutPeerFlag);
+}
+}  // namespace
+
+int rs_reduce(const RsReduceCall& c, cudaStream_t stream) {
+  if (c.rows % 128 || c.n % 128 || c.tile_n % 128 || !c.recv || !c.flags || !c.out) return -1;
+  if (c.quantized && (c.rows % c.chunk_rows)) return -1;
+  if (c.arrival && !c.claims) return -1;
+  const int tiles = (c.rows / 128) * ((c.n + c.tile_n - 1) / c.tile_n);
+  int sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int grid = c.arrival ? (tiles < 2 * sms ? tiles : 2 * sms) : tiles;
+  if (c.arrival && grid < 2) grid = 2;
+  if (c.max_ctas > 0 && grid > c.max_ctas) grid = c.max_ctas;
+  rs_reduce_kernel<<<grid, kThreads, 0, stream>>>(c);
+  return int(cudaGetLastError());
+}
+
+int wait_probe(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status,
+               cudaStream_t stream) {
+  wait_probe_kernel<<<1, 32, 0, stream>>>(flag, target, timeout_ns, status);
+  return int(cudaGetLastError());
+}
+
+}  // namespace comm
+}  // namespace tn5b

@@ -1,0 +1,42 @@
+// Symmetric-memory plumbing: CUDA IPC export/import of device allocations so
+// every rank can address every peer's buffer over NVLink, plus the receiver
+// kernels of the fused reduce-scatter (ordered BF16 reduce, fused TACO
+// decode + ordered reduce) with bounded per-tile readiness waits.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace tn5b {
+namespace comm {
+
+struct RsReduceCall {
+  const uint8_t* recv = nullptr;   // this rank's slot region [world][slot_bytes]
+  const uint32_t* flags = nullptr; // this rank's flags [world][tiles]
+  int64_t slot_bytes = 0;
+  int rank = 0, world = 1;
+  int rows = 0, n = 0;             // output [rows, n] (rows = M / world)
+  int tile_n = 256;                // producer tile width (flag granularity)
+  int chunk_rows = 128;            // TACO block rows
+  int quantized = 0;               // remote slots hold TACO packets
+  uint32_t epoch = 0;
+  void* out = nullptr;             // bf16 [rows, n]
+  const void* residual = nullptr;  // optional bf16 [rows, n]: out = bf16(bf16(res + y) + bias)
+  const void* bias = nullptr;      // optional bf16 [n]
+  const int* tile_order = nullptr; // optional consumption order of local tiles
+  int arrival = 0;                 // 1: per-lane any-ready consumption (arrival-first)
+  int* claims = nullptr;           // arrival mode: per-tile claim words [tiles]
+  int* status = nullptr;
+  uint64_t timeout_ns = 0;
+  int max_ctas = 0;
+};
+int rs_reduce(const RsReduceCall& c, cudaStream_t stream);
+
+}  // namespace comm
+}  // namespace tn5b
+
+namespace tn5b {
+namespace comm {
+int wait_probe(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status,
+               cudaStream_t stream);
+}  // namespace comm
+}  // namespace tn5b

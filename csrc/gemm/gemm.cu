@@ -1,0 +1,186 @@
+// Host launcher for the tcgen05 GEMM family: TMA descriptor encoding, kernel
+// instantiation selection, argument validation and persistent-grid sizing.
+#include "gemm_api.h"
+#include "gemm_kernel.cuh"
+
+#include <mutex>
+#include <cstdio>
+
+namespace tn5b {
+namespace gemm {
+
+namespace {
+thread_local std::string g_last_error;
+
+int fail(const char* msg) {
+  g_last_error = msg;
+  return -1;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map, 128-byte swizzle. `inner` is the contiguous extent.
+bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+              uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && n[dev]) return n[dev];
+  int v = 0;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) n[dev] = v;
+  return v;
+}
+
+template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG>
+int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUtensorMap& mb,
+           int grid, cudaStream_t stream) {
+  using L = SmemLayout<BN, STAGES, EPI_COLS>;
+  auto kern = gemm_kernel<BN, STAGES, EPI_COLS, MODE, AG>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !configured[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    if (e != cudaSuccess) return int(e);
+    if (dev < 64) configured[dev] = true;
+  }
+  const int threads = kThreads + (AG ? 32 : 0);
+  kern<<<grid, threads, L::kTotal, stream>>>(ma, mb, p, c.a_mn, c.b_mn);
+  return int(cudaGetLastError());
+}
+
+int pick_bn(const GemmCall& c) {
+  if (c.bn == 128 || c.bn == 256) return c.bn;
+  if (c.mode != 0) return 256;
+  if (c.N <= 128) return 128;
+  // Prefer the wider tile unless it leaves too few tiles to fill the machine.
+  const int sms = sm_count();
+  const long tiles256 = long((c.M + 127) / 128) * ((c.N + 255) / 256);
+  if (tiles256 < sms) return 128;
+  return 256;
+}
+}  // namespace
+
+std::string last_error() { return g_last_error; }
+
+int grid_ctas(const GemmCall& c) {
+  const int bn = pick_bn(c);
+  const long tiles = long((c.M + kBM - 1) / kBM) * ((c.N + bn - 1) / bn);
+  int g = sm_count();
+  if (c.max_ctas > 0 && c.max_ctas < g) g = c.max_ctas;
+  return int(tiles < g ? tiles : g);
+}
+
+int run(const GemmCall& c, cudaStream_t stream) {
+  if (c.M <= 0 || c.N <= 0 || c.K <= 0) return fail("gemm: non-positive M/N/K");
+  if (!c.A || !c.B) return fail("gemm: null operand");
+  if ((reinterpret_cast<uintptr_t>(c.A) | reinterpret_cast<uintptr_t>(c.B)) & 15)
+    return fail("gemm: operands must be 16-byte aligned");
+  if ((c.lda * 2) % 16 || (c.ldb * 2) % 16) return fail("gemm: leading dims must be 16-byte multiples");
+  if (c.N % 8) return fail("gemm: N must be a multiple of 8");
+  if (c.mode == 0) {
+    if (!c.out) return fail("gemm: null output");
+    if ((reinterpret_cast<uintptr_t>(c.out) & 15) || (c.ldo % 8))
+      return fail("gemm: output must be 16-byte aligned with ldo % 8 == 0");
+    if ((c.epi & kEpiGelu) && (!c.aux || (reinterpret_cast<uintptr_t>(c.aux) & 15) || c.ld_aux % 8))
+      return fail("gemm: gelu epilogue needs an aligned aux output");
+    if ((c.epi & kEpiResidual) && (!c.residual || (reinterpret_cast<uintptr_t>(c.residual) & 15) || c.ld_res % 8))
+      return fail("gemm: residual epilogue needs an aligned residual");
+  }
+  const int bn = pick_bn(c);
+  Params p{};
+  p.M = c.M; p.N = c.N; p.K = c.K;
+  p.tiles_m = (c.M + kBM - 1) / kBM;
+  p.tiles_n = (c.N + bn - 1) / bn;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.k_blocks = (c.K + kBK - 1) / kBK;
+  p.group_m = c.group_m > 0 ? c.group_m : 8;
+  p.tile_order = c.tile_order;
+  p.epi = c.epi;
+  p.out = static_cast<__nv_bfloat16*>(c.out); p.ldo = c.ldo;
+  p.aux = static_cast<__nv_bfloat16*>(c.aux); p.ld_aux = c.ld_aux;
+  p.bias = static_cast<const __nv_bfloat16*>(c.bias);
+  p.residual = static_cast<const __nv_bfloat16*>(c.residual); p.ld_res = c.ld_res;
+  p.status = c.status;
+  p.timeout_ns = c.timeout_ns;
+  if (c.mode != 0) {
+    if (!c.rs_recv || !c.rs_flags || c.world < 1 || c.M % c.world) return fail("gemm-rs: bad args");
+    const int rows = c.M / c.world;
+    if (rows % kBM) return fail("gemm-rs: rows per destination must be a multiple of 128");
+    if (c.mode == 2 && (rows % c.chunk_rows || c.chunk_rows % kBM || c.N % 128))
+      return fail("gemm-rs: TACO needs chunk_rows | rows, 128 | chunk_rows, 128 | N");
+    p.rs.recv = c.rs_recv; p.rs.flags = c.rs_flags;
+    p.rs.rank = c.rank; p.rs.world = c.world;
+    p.rs.rows_per_dest = rows; p.rs.chunk_rows = c.chunk_rows;
+    p.rs.epoch = c.epoch; p.rs.slot_bytes = c.slot_bytes;
+  }
+  if (c.ag) {
+    if (!c.ag_chunk_flags || !c.ag_gather || !c.ag_peer_flags || !c.ag_shard || c.M % c.world)
+      return fail("ag-gemm: bad args");
+    if ((c.M / c.world) % kBM) return fail("ag-gemm: rows per source must be a multiple of 128");
+    if (c.ag_shard_bytes % 16 || reinterpret_cast<uintptr_t>(c.ag_shard) & 15)
+      return fail("ag-gemm: shard must be 16-byte aligned and sized");
+    p.ag.chunk_flags = c.ag_chunk_flags; p.ag.target = c.ag_target;
+    p.ag.rank = c.rank; p.ag.world = c.world; p.ag.rows_per_src = c.M / c.world;
+    p.ag.shard = static_cast<const uint8_t*>(c.ag_shard);
+    p.ag.shard_bytes = c.ag_shard_bytes;
+    p.ag.gather = c.ag_gather; p.ag.peer_flags = c.ag_peer_flags;
+  }
+  CUtensorMap ma, mb;
+  const bool ok_a = c.a_mn ? make_map(&ma, c.A, c.M, c.K, c.lda, 64, 64)
+                           : make_map(&ma, c.A, c.K, c.M, c.lda, 64, kBM);
+  const bool ok_b = c.b_mn ? make_map(&mb, c.B, c.N, c.K, c.ldb, 64, 64)
+                           : make_map(&mb, c.B, c.K, c.N, c.ldb, 64, bn);
+  if (!ok_a || !ok_b) return fail("gemm: cuTensorMapEncodeTiled failed");
+  const int grid = grid_ctas(c);
+  if (c.ag) {
+    if (bn == 256) return launch<256, 4, 64, kModeLocal, true>(c, p, ma, mb, grid, stream);
+    return launch<128, 6, 64, kModeLocal, true>(c, p, ma, mb, grid, stream);
+  }
+  switch (c.mode) {
+    case 0:
+      if (bn == 256) return launch<256, 4, 64, kModeLocal, false>(c, p, ma, mb, grid, stream);
+      return launch<128, 6, 64, kModeLocal, false>(c, p, ma, mb, grid, stream);
+    case 1:
+      return launch<256, 4, 64, kModeRsPush, false>(c, p, ma, mb, grid, stream);
+    case 2:
+      return launch<256, 3, 128, kModeRsTaco, false>(c, p, ma, mb, grid, stream);
+    default:
+      return fail("gemm: unknown mode");
+  }
+}
+
+}  // namespace gemm
+}  // namespace tn5b

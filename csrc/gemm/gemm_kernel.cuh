@@ -1,0 +1,641 @@
+// Persistent, warp-specialised BF16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   C[M, N] = A[M, K] * B[N, K]^T          (fp32 accumulation in tensor memory)
+//
+// A and B may each be K-major (row-major [rows, K]) or MN-major (row-major
+// [K, rows]); the operand major is carried by the TMA box shape and the UMMA
+// descriptors, so forward (TN), dgrad (TT) and wgrad (NT) GEMMs all run here.
+//
+// CTA roles (192 threads):
+//   warp 0      TMA producer: one elected lane streams A/B k-blocks into a
+//               STAGES-deep shared-memory ring (128-byte swizzle).
+//   warp 1      MMA issuer: allocates TMEM (2 accumulators x BN columns), one
+//               lane issues tcgen05.mma (M=128, N=BN, K=16) and commits to
+//               mbarriers that free smem stages / publish accumulators.
+//   warps 2..5  epilogue: tcgen05.ld accumulator rows (warp w owns TMEM lanes
+//               32*(w%4)..+31), apply the fused epilogue, stage through a
+//               swizzled smem buffer and write coalesced 16-byte stores.
+//
+// The grid is persistent (<= one CTA per SM); CTA c walks tiles c, c+grid, ...
+// of a tile order that is either a grouped raster (plain GEMMs) or an explicit
+// table (reduce-scatter schedules: destination-major / interleaved / arrival).
+//
+// Every wait is bounded (see ptx.cuh); on a timeout the CTA records a status
+// code, drains its in-flight TMA loads and MMAs, frees TMEM and returns.
+//
+// Reference parity: this replaces the CUTLASS Sm80 mma.sync GEMM with the
+// OrderedDPSwizzle tile order of src/gemm/native.cu:33-114 (TempName-5090).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cstdint>
+#include "../common/ptx.cuh"
+
+namespace tn5b {
+namespace gemm {
+
+constexpr int kBM = 128;             // UMMA M (one CTA, cta_group::1)
+constexpr int kBK = 64;              // k-block: 64 bf16 = one 128-byte swizzle row
+constexpr int kUmmaK = 16;           // K per tcgen05.mma for 16-bit inputs
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+constexpr int kEpiFirstWarp = 2;
+
+enum EpiFlags : int {
+  kEpiBias = 1,        // + bias[n] (fp32 add before rounding)
+  kEpiGelu = 2,        // aux = bf16(acc+bias); out = bf16(gelu(aux))
+  kEpiResidual = 4,    // out = bf16(bf16(res + bf16(acc)) + bias)
+  kEpiAccumulate = 8,  // out = bf16(float(out) + acc)
+};
+
+// Modes of the epilogue destination.
+enum Mode : int {
+  kModeLocal = 0,      // plain store into C
+  kModeRsPush = 1,     // GEMM -> reduce-scatter: BF16 tile pushed to its owner rank
+  kModeRsTaco = 2,     // GEMM -> reduce-scatter: remote tiles TACO-encoded, then pushed
+};
+
+struct RsArgs {
+  // Peer base pointers of every rank's receive slots (index = rank), each slot
+  // region laid out [source][M/W rows][N] (bf16) or [source][blocks][packet].
+  uint8_t* const* recv;          // device array [world]
+  uint32_t* const* flags;        // device array [world]; flag[source * tiles_per_dest + t]
+  int rank, world;
+  int rows_per_dest;             // M / world
+  int chunk_rows;                // TACO packet block rows (reference macroblock)
+  uint32_t epoch;
+  int64_t slot_bytes;            // bytes of one source slot on a receiver
+};
+
+struct AgArgs {
+  // AG->GEMM: A rows [c*rows_per_src, (c+1)*rows_per_src) arrive from rank c.
+  const uint32_t* chunk_flags;   // local counters [world]
+  uint32_t target;               // wait until chunk_flags[c] >= target
+  int rank, world, rows_per_src;
+  // push side (comm warp): copy local shard to every rank's gather buffer
+  const uint8_t* shard;          // local [rows_per_src, K] bf16 rows (contiguous)
+  int64_t shard_bytes;
+  uint8_t* const* gather;        // device array [world] of gather buffer bases
+  uint32_t* const* peer_flags;   // device array [world] of chunk_flags bases
+};
+
+struct Params {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles, k_blocks;
+  int group_m;                   // raster group (plain GEMMs)
+  const int* tile_order;         // optional: linear tile ids (tm * tiles_n + tn)
+  // epilogue
+  int epi;
+  __nv_bfloat16* out; int64_t ldo;
+  __nv_bfloat16* aux; int64_t ld_aux;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual; int64_t ld_res;
+  RsArgs rs;
+  AgArgs ag;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+template <int BN, int STAGES, int EPI_COLS>
+struct SmemLayout {
+  static constexpr int kABytes = kBM * kBK * 2;        // 16 KB
+  static constexpr int kBBytes = BN * kBK * 2;         // 32 KB at BN=256
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStagingPerWarp = 32 * EPI_COLS * 2;
+  static constexpr int kStagingBytes = kEpiWarps * kStagingPerWarp;
+  static constexpr int kBarrierBytes = 256;
+  // [align 1024][stages][staging][barriers]
+  static constexpr int kTotal = 1024 + STAGES * kStageBytes + kStagingBytes + kBarrierBytes;
+};
+
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& tm, int& tn) {
+  if (p.tile_order) {
+    const int id = p.tile_order[t];
+    tm = id / p.tiles_n;
+    tn = id % p.tiles_n;
+    return;
+  }
+  const int group_size = p.group_m * p.tiles_n;
+  const int group = t / group_size;
+  const int first_m = group * p.group_m;
+  const int size_m = min(p.tiles_m - first_m, p.group_m);
+  const int r = t % group_size;
+  tm = first_m + r % size_m;
+  tn = r / size_m;
+}
+
+__device__ __forceinline__ float bf16_round_f(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ float gelu_exact(float x) {
+  // 0.5 * x * (1 + erf(x / sqrt(2))), CUDA's erff called directly.
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Swizzled staging: row r (0..31), 16-byte unit u -> byte offset.
+template <int EPI_COLS>
+__device__ __forceinline__ uint32_t staging_offset(int r, int u) {
+  constexpr int kUnits = EPI_COLS / 8;  // 16-byte units per row
+  return uint32_t(r * kUnits + (u ^ (r & 7))) * 16u;
+}
+
+// ===========================================================================
+// TACO H128/E4M3 encode of one 128-element group held entirely by one thread.
+// The FP32 operation sequence equals the warp-cooperative reference encoder
+// (src/taco/codec.cu:69-103 of TempName-5090): the sum of squares follows its
+// shuffle-down tree, the Walsh-Hadamard butterfly runs distances 1..64 in the
+// same order with the same (lo+hi, lo-hi) operands, and every multiply, add,
+// divide, rsqrtf and FP8 conversion is the same correctly-rounded operation,
+// so packets are byte-identical.  Explicit _rn intrinsics forbid contraction.
+// ===========================================================================
+namespace taco {
+constexpr float kNorm = 0.08838834764831844055f;
+
+__device__ __forceinline__ float clampf(float x, float lo, float hi) {
+  return fminf(fmaxf(x, lo), hi);
+}
+
+// Shuffle-down tree of one 32-lane warp_sum, evaluated for lane 0.
+__device__ __forceinline__ float tree32(const float* a) {
+  float b[16], c[8], d[4], e[2];
+#pragma unroll
+  for (int l = 0; l < 16; ++l) b[l] = __fadd_rn(a[l], a[l + 16]);
+#pragma unroll
+  for (int l = 0; l < 8; ++l) c[l] = __fadd_rn(b[l], b[l + 8]);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) d[l] = __fadd_rn(c[l], c[l + 4]);
+#pragma unroll
+  for (int l = 0; l < 2; ++l) e[l] = __fadd_rn(d[l], d[l + 2]);
+  return __fadd_rn(e[0], e[1]);
+}
+
+// x[c] holds element c (c = lane + 32*j in the reference layout).  On return
+// x[c] holds the normalised Walsh coefficient c (natural order); the caller
+// quantises each with e4m3(x[c] / quant) so no 128-byte code array is live.
+__device__ __forceinline__ void encode_group(float (&x)[128], float& quant, float& adaptive) {
+  float part[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float sq[32];
+#pragma unroll
+    for (int l = 0; l < 32; ++l) sq[l] = __fmul_rn(x[32 * j + l], x[32 * j + l]);
+    part[j] = tree32(sq);
+  }
+  const float sum = __fadd_rn(__fadd_rn(part[0], part[2]), __fadd_rn(part[1], part[3]));
+  const float variance = __fadd_rn(sum / 128.f, 1e-6f);
+  adaptive = clampf(__fmul_rn(448.f, rsqrtf(fmaxf(variance, 1e-12f))), 1e-3f, 1e3f);
+#pragma unroll
+  for (int c = 0; c < 128; ++c) x[c] = __fmul_rn(x[c], adaptive);
+#pragma unroll
+  for (int d = 1; d < 128; d *= 2) {
+#pragma unroll
+    for (int c = 0; c < 128; ++c) {
+      if ((c & d) == 0) {
+        const float lo = x[c], hi = x[c + d];
+        x[c] = __fadd_rn(lo, hi);
+        x[c + d] = __fsub_rn(lo, hi);
+      }
+    }
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int c = 0; c < 128; ++c) {
+    x[c] = __fmul_rn(x[c], kNorm);
+    amax = fmaxf(amax, fabsf(x[c]));
+  }
+  quant = clampf(amax / 448.f, 1e-12f, 1e6f);
+}
+__device__ __forceinline__ uint32_t code(float x, float quant) {
+  return uint32_t(__nv_cvt_float_to_fp8(x / quant, __NV_SATFINITE, __NV_E4M3)) & 0xFFu;
+}
+}  // namespace taco
+
+// ===========================================================================
+// The kernel.
+// ===========================================================================
+template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG>
+__global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ Params p,
+                int a_mn, int b_mn) {
+  using L = SmemLayout<BN, STAGES, EPI_COLS>;
+  static_assert(BN % EPI_COLS == 0, "epilogue chunks must tile BN");
+  static_assert(MODE != kModeRsTaco || EPI_COLS == 128, "TACO groups are 128 columns");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint8_t* staging = smem + STAGES * L::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + L::kStagingBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      int last_parity[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
+      bool ok = true;
+      int waited_chunk = -1;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(p, t, tm, tn);
+        if constexpr (AG) {
+          const int chunk = (tm * kBM) / p.ag.rows_per_src;
+          if (chunk != waited_chunk) {
+            if (!wait_flag_geq(p.ag.chunk_flags + chunk, p.ag.target, p.timeout_ns, p.status,
+                               kTimeoutAgChunk)) {
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+            waited_chunk = chunk;
+          }
+        }
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.timeout_ns, p.status, kTimeoutProducerEmpty,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = stage_base + s * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+          const int k0 = kb * kBK;
+          if (!a_mn) {
+            tma_load_2d(sa, &tmap_a, &full[s], k0, tm * kBM);
+          } else {
+#pragma unroll
+            for (int c = 0; c < kBM / 64; ++c)
+              tma_load_2d(sa + c * 8192, &tmap_a, &full[s], tm * kBM + c * 64, k0);
+          }
+          if (!b_mn) {
+            tma_load_2d(sb, &tmap_b, &full[s], k0, tn * BN);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(sb + c * 8192, &tmap_b, &full[s], tn * BN + c * 64, k0);
+          }
+          last_parity[s] = int(ph);
+        }
+      }
+      if (!ok) {
+        // Abort path: let every issued TMA load land before the CTA can exit.
+        for (int s = 0; s < STAGES; ++s)
+          if (last_parity[s] >= 0)
+            mbar_wait(&full[s], uint32_t(last_parity[s]), p.timeout_ns, p.status, kTimeoutDrain,
+                      nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_bf16(kBM, BN, a_mn, b_mn);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+        const int b = local & 1;
+        const uint32_t use = uint32_t(local >> 1);
+        if (!mbar_wait(&tempty[b], (use & 1) ^ 1, p.timeout_ns, p.status, kTimeoutMmaTmemEmpty,
+                       abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(b * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.timeout_ns, p.status, kTimeoutMmaFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(stage_base + s * L::kStageBytes);
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            const uint64_t ad = a_mn ? make_sw128_desc(sa + k * 2048, 8192, 1024)
+                                     : make_sw128_desc(sa + k * 32, 16, 1024);
+            const uint64_t bd = b_mn ? make_sw128_desc(sb + k * 2048, 8192, 1024)
+                                     : make_sw128_desc(sb + k * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[b]);
+      }
+      // All issued MMAs must finish before TMEM is released (normal and abort path).
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.timeout_ns, p.status, kTimeoutDrain, nullptr);
+    }
+  } else if (warp < kEpiFirstWarp + kEpiWarps) {
+    // ------------------------------------------------------------- epilogue
+    const int q = warp & 3;                       // TMEM lane quarter
+    const int ew = warp - kEpiFirstWarp;          // staging buffer
+    uint8_t* stg = staging + ew * L::kStagingPerWarp;
+    const uint32_t stg_addr = smem_u32(stg);
+    int local = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      int tm, tn;
+      tile_coords(p, t, tm, tn);
+      const int b = local & 1;
+      const uint32_t use = uint32_t(local >> 1);
+      int ok = 1;
+      if (lane == 0)
+        ok = mbar_wait(&tfull[b], use & 1, p.timeout_ns, p.status, kTimeoutEpiTmemFull,
+                       abort_flag);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row_w = tm * kBM + q * 32;        // first row owned by this warp
+      const int my_row = row_w + lane;
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * BN);
+
+      // Destination of this tile (reduce-scatter modes).
+      int dest = 0;
+      bool remote_taco = false;
+      if constexpr (MODE != kModeLocal) {
+        dest = (tm * kBM) / p.rs.rows_per_dest;
+        remote_taco = (MODE == kModeRsTaco) && dest != p.rs.rank;
+      }
+
+      for (int c0 = 0; c0 < BN; c0 += EPI_COLS) {
+        const int col0 = tn * BN + c0;
+        float v[EPI_COLS];
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; j += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + uint32_t(c0 + j), r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[j + i] = __uint_as_float(r[i]);
+        }
+        if (c0 + EPI_COLS >= BN) {
+          // Accumulator fully read: hand the TMEM buffer back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[b]);
+        }
+        if (col0 >= p.N) continue;  // whole chunk beyond N (tail tile)
+
+        if constexpr (MODE == kModeLocal) {
+          const bool row_ok = my_row < p.M;
+          // ---- fused elementwise epilogue, result rounded to bf16 in v[]
+          if ((p.epi & (kEpiBias | kEpiGelu)) && !(p.epi & kEpiResidual)) {
+            if (p.bias) {
+#pragma unroll
+              for (int i = 0; i < EPI_COLS; ++i) {
+                const int col = col0 + i;
+                v[i] = __fadd_rn(v[i], col < p.N ? __bfloat162float(p.bias[col]) : 0.f);
+              }
+            }
+          }
+          if (p.epi & kEpiGelu) {
+            // aux = pre-activation (bf16); v = gelu(aux)
+#pragma unroll
+            for (int u = 0; u < EPI_COLS / 8; ++u) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[8 * u + 0], v[8 * u + 1]);
+              pk.y = pack_bf16x2(v[8 * u + 2], v[8 * u + 3]);
+              pk.z = pack_bf16x2(v[8 * u + 4], v[8 * u + 5]);
+              pk.w = pack_bf16x2(v[8 * u + 6], v[8 * u + 7]);
+              asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(
+                               stg_addr + staging_offset<EPI_COLS>(lane, u)),
+                           "r"(pk.x), "r"(pk.y), "r"(pk.z), "r"(pk.w));
+            }
+            __syncwarp();
+            constexpr int kUnits = EPI_COLS / 8;
+#pragma unroll 4
+            for (int idx = lane; idx < 32 * kUnits; idx += 32) {
+              const int r = idx / kUnits, u = idx % kUnits;
+              const int row = row_w + r, col = col0 + u * 8;
+              uint4 val;
+              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                           : "r"(stg_addr + staging_offset<EPI_COLS>(r, u)));
+              if (row < p.M && col < p.N) st_global_v4(p.aux + int64_t(row) * p.ld_aux + col, val);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < EPI_COLS; ++i) v[i] = gelu_exact(bf16_round_f(v[i]));
+          }
+          if (p.epi & kEpiResidual) {
+            // out = bf16(bf16(res + bf16(acc)) + bias)
+#pragma unroll
+            for (int u = 0; u < EPI_COLS / 8; ++u) {
+              const int col = col0 + 8 * u;
+              uint4 rv = make_uint4(0, 0, 0, 0);
+              if (row_ok && col < p.N) rv = ld_global_v4(p.residual + int64_t(my_row) * p.ld_res + col);
+              const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float y = bf16_round_f(v[8 * u + i]);
+                const float s = bf16_round_f(__fadd_rn(__bfloat162float(rb[i]), y));
+                const float bb = (p.bias && col + i < p.N) ? __bfloat162float(p.bias[col + i]) : 0.f;
+                v[8 * u + i] = p.bias ? __fadd_rn(s, bb) : s;
+              }
+            }
+          }
+          if (p.epi & kEpiAccumulate) {
+#pragma unroll
+            for (int u = 0; u < EPI_COLS / 8; ++u) {
+              const int col = col0 + 8 * u;
+              uint4 ov = make_uint4(0, 0, 0, 0);
+              if (row_ok && col < p.N) ov = ld_global_v4(p.out + int64_t(my_row) * p.ldo + col);
+              const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&ov);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[8 * u + i] = __fadd_rn(__bfloat162float(ob[i]), v[8 * u + i]);
+            }
+          }
+        }
+
+        if constexpr (MODE == kModeRsTaco) {
+          if (remote_taco) {
+            // Encode my row's 128-column group (bf16-rounded partial, as the
+            // reference encodes the stored BF16 partial) and stage the payload.
+            // v[] is reused in place as the group (bf16-rounded first).
+#pragma unroll
+            for (int i = 0; i < 128; ++i) v[i] = bf16_round_f(v[i]);
+            float quant, adaptive;
+            taco::encode_group(v, quant, adaptive);
+            // payload: 128 bytes per row = 8 units of 16 B, swizzled like bf16 staging
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              uint32_t w[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int c = 16 * u + 4 * k;
+                w[k] = taco::code(v[c], quant) | (taco::code(v[c + 1], quant) << 8) |
+                       (taco::code(v[c + 2], quant) << 16) | (taco::code(v[c + 3], quant) << 24);
+              }
+              asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(
+                               stg_addr + staging_offset<64>(lane, u)),
+                           "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]));
+            }
+            __syncwarp();
+            // Receiver packet of source `rank`, block = chunk_rows x N (reference SoA layout).
+            const int row_local0 = row_w - dest * p.rs.rows_per_dest;
+            const int blk = row_local0 / p.rs.chunk_rows;
+            const int64_t elems = int64_t(p.rs.chunk_rows) * p.N;
+            const int64_t groups = elems / 128;
+            uint8_t* pkt = p.rs.recv[dest] + int64_t(p.rs.rank) * p.rs.slot_bytes +
+                           int64_t(blk) * (elems + 8 * groups);
+            const int rib0 = row_local0 % p.rs.chunk_rows;  // row in block of lane 0
+#pragma unroll 4
+            for (int idx = lane; idx < 32 * 8; idx += 32) {
+              const int r = idx / 8, u = idx % 8;
+              const int64_t g = (int64_t(rib0 + r) * p.N + col0) / 128;
+              uint4 val;
+              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                           : "r"(stg_addr + staging_offset<64>(r, u)));
+              st_global_v4(pkt + g * 128 + u * 16, val);
+            }
+            {
+              const int64_t g = (int64_t(rib0 + lane) * p.N + col0) / 128;
+              reinterpret_cast<float*>(pkt + elems)[g] = quant;
+              reinterpret_cast<float*>(pkt + elems + 4 * groups)[g] = adaptive;
+            }
+            __syncwarp();
+            continue;
+          }
+        }
+
+        // ---- bf16 staging + coalesced 16-byte stores
+#pragma unroll
+        for (int u = 0; u < EPI_COLS / 8; ++u) {
+          uint4 pk;
+          pk.x = pack_bf16x2(v[8 * u + 0], v[8 * u + 1]);
+          pk.y = pack_bf16x2(v[8 * u + 2], v[8 * u + 3]);
+          pk.z = pack_bf16x2(v[8 * u + 4], v[8 * u + 5]);
+          pk.w = pack_bf16x2(v[8 * u + 6], v[8 * u + 7]);
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(
+                           stg_addr + staging_offset<EPI_COLS>(lane, u)),
+                       "r"(pk.x), "r"(pk.y), "r"(pk.z), "r"(pk.w));
+        }
+        __syncwarp();
+        {
+          constexpr int kUnits = EPI_COLS / 8;
+          __nv_bfloat16* base;
+          int64_t ld;
+          int row_base;
+          if constexpr (MODE == kModeLocal) {
+            base = p.out;
+            ld = p.ldo;
+            row_base = row_w;
+          } else {
+            base = reinterpret_cast<__nv_bfloat16*>(p.rs.recv[dest] +
+                                                    int64_t(p.rs.rank) * p.rs.slot_bytes);
+            ld = p.N;
+            row_base = row_w - dest * p.rs.rows_per_dest;
+          }
+#pragma unroll 4
+          for (int idx = lane; idx < 32 * kUnits; idx += 32) {
+            const int r = idx / kUnits, u = idx % kUnits;
+            const int col = col0 + u * 8;
+            uint4 val;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                         : "r"(stg_addr + staging_offset<EPI_COLS>(r, u)));
+            if (row_w + r < p.M && col < p.N) st_global_v4(base + int64_t(row_base + r) * ld + col, val);
+          }
+        }
+        __syncwarp();
+      }
+
+      if constexpr (MODE != kModeLocal) {
+        // Publish the tile to its owner: all four epilogue warps' stores, then
+        // one system-scope release of flag[source][tile] = epoch on the owner.
+        named_barrier_sync(1, kEpiWarps * 32);
+        if (warp == kEpiFirstWarp && lane == 0) {
+          const int tiles_per_dest_m = p.rs.rows_per_dest / kBM;
+          const int local_tile = (tm - dest * tiles_per_dest_m) * p.tiles_n + tn;
+          fence_acq_rel_sys();
+          st_release_sys(p.rs.flags[dest] + int64_t(p.rs.rank) * tiles_per_dest_m * p.tiles_n +
+                             local_tile,
+                         p.rs.epoch);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------- AG push warp (AG mode only)
+    if constexpr (AG) {
+      // This CTA copies its slice of the local shard into every rank's gather
+      // buffer (peers first, own buffer last), then bumps each owner's counter.
+      const int64_t units = p.ag.shard_bytes / 16;
+      const int64_t per = (units + gridDim.x - 1) / gridDim.x;
+      const int64_t lo = int64_t(blockIdx.x) * per;
+      const int64_t hi = min(units, lo + per);
+      for (int step = 1; step <= p.ag.world; ++step) {
+        const int dst = (p.ag.rank + step) % p.ag.world;
+        uint8_t* out = p.ag.gather[dst] + int64_t(p.ag.rank) * p.ag.shard_bytes;
+        for (int64_t u = lo + lane; u < hi; u += 32)
+          st_global_v4(out + u * 16, ld_global_nc_v4(p.ag.shard + u * 16));
+        __syncwarp();
+        if (lane == 0) {
+          fence_acq_rel_sys();
+          red_release_sys_add(p.ag.peer_flags[dst] + p.ag.rank, 1u);
+        }
+        __syncwarp();
+      }
+    }
+  }
+
+  // ------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+}  // namespace gemm
+}  // namespace tn5b

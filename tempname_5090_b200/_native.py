@@ -1,0 +1,87 @@
+"""Loader for the in-tree native extension (tempname_5090_b200._C).
+
+On a machine with CUDA the extension is mandatory: `lib()` raises if it cannot
+be imported, so no CUDA code path silently runs anything else.  CPU-only hosts
+(unit tests) never call it.
+"""
+from __future__ import annotations
+
+import threading
+
+_LOCK = threading.Lock()
+_LIB = None
+_ERROR: Exception | None = None
+_STATUS: dict = {}
+_LAUNCHES = [0]
+
+STATUS_MESSAGES = {
+    1: "GEMM producer timed out waiting for a free shared-memory stage",
+    2: "GEMM MMA warp timed out waiting for a loaded stage",
+    3: "GEMM MMA warp timed out waiting for the epilogue to drain TMEM",
+    4: "GEMM epilogue timed out waiting for an accumulator",
+    5: "a cross-GPU readiness flag never arrived (peer stalled or failed)",
+    6: "abort drain of in-flight copies timed out",
+    7: "AG->GEMM: a gathered row chunk never arrived",
+    8: "bad kernel argument",
+}
+
+
+def lib():
+    """Return the native module; raise if it is unavailable."""
+    global _LIB, _ERROR
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            try:
+                from . import _C  # type: ignore
+                _LIB = _C
+            except Exception as exc:  # pragma: no cover - depends on build state
+                _ERROR = exc
+                raise RuntimeError(
+                    "tempname_5090_b200 native extension is not built or failed to load; "
+                    "run `python setup.py build_ext --inplace` (sm_100a). "
+                    f"Import error: {exc}") from exc
+    return _LIB
+
+
+def available() -> bool:
+    try:
+        lib()
+        return True
+    except RuntimeError:
+        return False
+
+
+def status_tensor(device):
+    """Per-device int32 status word shared by all kernels' bounded waits."""
+    import torch
+    device = torch.device(device)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STATUS.get(index)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", index))
+        _STATUS[index] = t
+    return t
+
+
+def check_status(device=None, clear: bool = True) -> None:
+    """Synchronise and raise if any kernel recorded a bounded-wait failure."""
+    import torch
+    index = torch.cuda.current_device() if device is None else torch.device(device).index
+    t = _STATUS.get(index)
+    if t is None:
+        return
+    code = int(t[0].item())
+    if code:
+        if clear:
+            t.zero_()
+        raise RuntimeError(f"device status {code}: {STATUS_MESSAGES.get(code, 'unknown')}")
+
+
+def count_launch(n: int = 1) -> None:
+    _LAUNCHES[0] += n
+
+
+def launches() -> int:
+    return _LAUNCHES[0]

@@ -1,0 +1,132 @@
+"""Physical-block schedules and GEMM tile orders of the four GemmRS arms.
+
+Semantics follow TempName-5090 (python/flux_5090/mapping.py:1-55,
+src/gemm/native.cu:33-82):
+
+* The M rows of a row-parallel projection are cut into physical blocks of
+  `chunk_rows`; block p belongs to destination p // per (per = M/W/chunk_rows),
+  `within` = p % per and its transport lane is within % 2.
+* Slot order: `flux` / `flux_taco` emit blocks 0..B-1 (destination-major);
+  `flux_taco_interleaved` rotates destinations, slot s -> (s % W)*per + s // W;
+  `flux_taco_interleaved_arrival` takes a calibrated plan that keeps slot s's
+  destination equal to s % W.
+* Tile order: destination-major visits each slot's block row-tile by row-tile,
+  all column tiles per row-tile; the interleaved arms visit rounds of W slots
+  and rotate the destination at column-tile granularity.
+
+`tile_order(..., tile_n)` expresses the order in tiles of 128 rows x tile_n
+columns.  At tile_n=128 it is exactly the reference's CTA map; the sm_100a
+GEMM uses tile_n=256 tiles with the same traversal.
+"""
+from __future__ import annotations
+
+ARMS = ("flux", "flux_taco", "flux_taco_interleaved", "flux_taco_interleaved_arrival")
+ARRIVAL_ARMS = ARMS[3:]
+INTERLEAVED_ARMS = ARMS[2:]
+QUANTIZED_ARMS = ARMS[1:]
+BACKEND = "b200-tcgen05-nvlink-push-v1"
+TILE_M = 128
+
+
+def validate_shape(m, n, k, world, chunk_rows):
+    if any(type(x) is not int or x <= 0 for x in (m, n, k, world, chunk_rows)):
+        raise ValueError("positive integer dimensions required")
+    if world < 2 or m % (world * chunk_rows) or chunk_rows % 128 or n % 128 or k % 8:
+        raise ValueError("require world >= 2, M divisible by world*chunk_rows, "
+                         "chunk_rows and N by 128, K by 8")
+
+
+def blocks_per_destination(m, world, chunk_rows):
+    return m // world // chunk_rows
+
+
+def slot_order(m, n, k, world, chunk_rows, arm, plan=None):
+    """Physical block emitted at each slot."""
+    validate_shape(m, n, k, world, chunk_rows)
+    if arm not in ARMS:
+        raise ValueError(f"unknown arm: {arm}")
+    count = m // chunk_rows
+    per = count // world
+    if arm in ARRIVAL_ARMS:
+        from .planning import validate_role_plan
+        validate_role_plan(plan, m, n, k, world, chunk_rows)
+        return list(plan["arrival_order"])
+    if plan is not None:
+        raise ValueError("only the arrival arm accepts a role plan")
+    if arm == "flux_taco_interleaved":
+        return [(s % world) * per + s // world for s in range(count)]
+    return list(range(count))
+
+
+def schedule(m, n, k, world, chunk_rows, arm, plan=None):
+    per = blocks_per_destination(m, world, chunk_rows)
+    order = slot_order(m, n, k, world, chunk_rows, arm, plan)
+    result = []
+    for slot, physical in enumerate(order):
+        within = physical % per
+        result.append(dict(slot=slot, physical=physical, destination=physical // per,
+                           within=within, row=physical * chunk_rows, rows=chunk_rows,
+                           lane=within % 2))
+    return result
+
+
+def tile_order(m, n, k, world, chunk_rows, arm, plan=None, tile_n=128):
+    """(row_tile, col_tile) pairs in production order, tiles of 128 x tile_n."""
+    if n % tile_n and tile_n != 128:
+        raise ValueError("N must be a multiple of the tile width")
+    items = schedule(m, n, k, world, chunk_rows, arm, plan)
+    row_tiles = chunk_rows // TILE_M
+    col_tiles = n // tile_n
+    if arm in INTERLEAVED_ARMS:
+        out = []
+        for round_ in range(len(items) // world):
+            for r in range(row_tiles):
+                for c in range(col_tiles):
+                    for d in range(world):
+                        out.append((items[round_ * world + d]["physical"] * row_tiles + r, c))
+        return out
+    return [(it["physical"] * row_tiles + r, c) for it in items
+            for r in range(row_tiles) for c in range(col_tiles)]
+
+
+def cta_mapping(m, n, k, world, chunk_rows, arm, plan=None):
+    """The reference's 128x128 CTA map (mapping.py:34-41)."""
+    return tile_order(m, n, k, world, chunk_rows, arm, plan, tile_n=128)
+
+
+def linear_tile_ids(m, n, k, world, chunk_rows, arm, plan=None, tile_n=256):
+    """Tile order as linear ids tm * tiles_n + tn (the GEMM kernel's table)."""
+    cols = n // tile_n
+    return [tm * cols + tn for tm, tn in tile_order(m, n, k, world, chunk_rows, arm, plan, tile_n)]
+
+
+def consumer_tile_order(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n=256):
+    """Order in which `rank` consumes its own tiles: production order restricted
+    to tiles destined to `rank`, as local tile ids (row tile within the
+    destination) * tiles_n + col tile."""
+    rows_per_dest = m // world
+    tiles_per_dest_m = rows_per_dest // TILE_M
+    cols = n // tile_n
+    out = []
+    for tm, tn in tile_order(m, n, k, world, chunk_rows, arm, plan, tile_n):
+        if tm // tiles_per_dest_m == rank:
+            out.append((tm - rank * tiles_per_dest_m) * cols + tn)
+    return out
+
+
+def wire_bytes(m, n, world, quantized):
+    """Bytes each source sends to remote owners per projection."""
+    elements = (world - 1) * (m // world) * n
+    return elements // 128 * 136 if quantized else elements * 2
+
+
+def split_sizes(world, rank, destination, elements):
+    """Sparse all-to-all splits of one block (only the owner receives)."""
+    if not 0 <= rank < world or not 0 <= destination < world or elements <= 0:
+        raise ValueError("invalid collective dimensions")
+    sends, receives = [0] * world, [0] * world
+    if rank != destination:
+        sends[destination] = elements
+    else:
+        receives = [elements if source != rank else 0 for source in range(world)]
+    return sends, receives

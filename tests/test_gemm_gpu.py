@@ -1,0 +1,73 @@
+"""tcgen05 GEMM numerics against a plain PyTorch fp32 reference of the same op."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, b, a_t, b_t):
+    af = a.float().t() if a_t else a.float()
+    bf = b.float().t() if b_t else b.float()
+    return af @ bf.t()
+
+
+def _rel(x, y):
+    return ((x.float() - y.float()).norm() / y.float().norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 320), (384, 128, 1024),
+                                   (1000, 520, 200), (2048, 6288, 4096)])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, True), (True, False)])
+def test_gemm_matches_fp32(M, N, K, a_t, b_t):
+    from tempname_5090_b200.ops.gemm import matmul
+    from tempname_5090_b200._native import check_status
+    if (a_t and M % 8) or (b_t and N % 8):
+        pytest.skip("MN-major storage needs 16-byte rows")
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+    a = torch.randn((K, M) if a_t else (M, K), generator=g, device="cuda").to(torch.bfloat16)
+    b = torch.randn((K, N) if b_t else (N, K), generator=g, device="cuda").to(torch.bfloat16)
+    out = matmul(a, b, a_t=a_t, b_t=b_t)
+    torch.cuda.synchronize()
+    check_status()
+    ref = _ref(a, b, a_t, b_t)
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_epilogues(bn):
+    from tempname_5090_b200.ops.gemm import matmul
+    M, N, K = 512, 768, 256
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+    b = (torch.randn((N, K), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = torch.randn((N,), generator=g, device="cuda").to(torch.bfloat16)
+    ref = a.float() @ b.float().t()
+    out = matmul(a, b, bias=bias, bn=bn)
+    assert _rel(out, ref + bias.float()) < 1e-2
+    aux = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    out = matmul(a, b, bias=bias, gelu_aux=aux, bn=bn)
+    pre = (ref + bias.float()).to(torch.bfloat16)
+    assert _rel(aux, pre) < 1e-2
+    assert _rel(out, torch.nn.functional.gelu(pre.float())) < 1e-2
+    res = torch.randn((M, N), generator=g, device="cuda").to(torch.bfloat16)
+    out = matmul(a, b, bias=bias, residual=res, bn=bn)
+    expect = ((res.float() + ref.to(torch.bfloat16).float()).to(torch.bfloat16).float() + bias.float())
+    assert _rel(out, expect) < 1e-2
+    base = torch.randn((M, N), generator=g, device="cuda").to(torch.bfloat16)
+    acc = base.clone()
+    matmul(a, b, out=acc, accumulate=True, bn=bn)
+    assert _rel(acc, base.float() + ref) < 1e-2
+
+
+def test_gemm_strided_output_and_tile_order():
+    from tempname_5090_b200.ops.gemm import matmul
+    M, N, K = 256, 512, 128
+    a = torch.randn((M, K), device="cuda").to(torch.bfloat16)
+    b = torch.randn((N, K), device="cuda").to(torch.bfloat16)
+    big = torch.zeros((M, 2 * N), dtype=torch.bfloat16, device="cuda")
+    view = big[:, N:]
+    tiles = (M // 128) * (N // 256)
+    order = torch.arange(tiles - 1, -1, -1, dtype=torch.int32, device="cuda")
+    matmul(a, b, out=view, bn=256, tile_order=order)
+    assert _rel(view, a.float() @ b.float().t()) < 1e-2
+    assert big[:, :N].abs().sum().item() == 0

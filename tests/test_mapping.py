@@ -1,0 +1,85 @@
+"""Schedules and tile orders of the four arms against an independent spec."""
+import pytest
+
+from tempname_5090_b200.parallel import mapping as mp
+from tempname_5090_b200.parallel import planning as pl
+
+
+def spec_map(m, n, world, chunk_rows, order, interleaved):
+    """Independent statement of the reference CTA map (native.py mapping_reference)."""
+    tiles_per_macro = (chunk_rows // 128) * (n // 128)
+    out = []
+    for logical in range((m // 128) * (n // 128)):
+        if interleaved:
+            within_dest, dest = divmod(logical, world)
+            rnd, within = divmod(within_dest, tiles_per_macro)
+            slot = rnd * world + dest
+        else:
+            slot, within = divmod(logical, tiles_per_macro)
+        row, col = divmod(within, n // 128)
+        out.append((order[slot] * (chunk_rows // 128) + row, col))
+    return out
+
+
+@pytest.mark.parametrize("arm", mp.ARMS)
+@pytest.mark.parametrize("m,n,world,chunk", [(2048, 4096, 8, 128), (1024, 512, 2, 256),
+                                             (4096, 1024, 4, 128)])
+def test_cta_map_matches_spec(arm, m, n, world, chunk):
+    plan = pl.make_role(m, n, 64, world, chunk) if arm in mp.ARRIVAL_ARMS else None
+    order = mp.slot_order(m, n, 64, world, chunk, arm, plan)
+    expect = spec_map(m, n, world, chunk, order, arm in mp.INTERLEAVED_ARMS)
+    assert mp.cta_mapping(m, n, 64, world, chunk, arm, plan) == expect
+
+
+def test_interleave_spacing_and_lanes():
+    items = mp.schedule(2048, 4096, 512, 8, 128, "flux_taco_interleaved")
+    assert [it["destination"] for it in items[:8]] == list(range(8))
+    assert all(it["lane"] == it["within"] % 2 for it in items)
+    assert sorted(it["physical"] for it in items) == list(range(16))
+
+
+def test_wire_bytes_budget():
+    assert mp.wire_bytes(2048, 4096, 8, False) == 14680064
+    assert mp.wire_bytes(2048, 4096, 8, True) == 7798784
+
+
+def test_split_sizes_pairwise():
+    for world in (2, 4, 8):
+        for dest in range(world):
+            recv = None
+            for rank in range(world):
+                sends, receives = mp.split_sizes(world, rank, dest, 10)
+                if rank == dest:
+                    assert sum(sends) == 0 and receives[rank] == 0
+                    assert sum(receives) == 10 * (world - 1)
+                else:
+                    assert sends[dest] == 10 and sum(receives) == 0
+
+
+@pytest.mark.parametrize("bad", [(1000, 4096, 64, 8, 128), (2048, 4000, 64, 8, 128),
+                                 (2048, 4096, 63, 8, 128), (2048, 4096, 64, 1, 128),
+                                 (2048, 4096, 64, 8, 100)])
+def test_invalid_shapes(bad):
+    with pytest.raises(ValueError):
+        mp.validate_shape(*bad)
+
+
+def test_tile_order_256_is_bijection_and_consumer_order():
+    m, n, world, chunk = 8192, 4096, 8, 128
+    for arm in mp.ARMS:
+        plan = pl.make_role(m, n, 2048, world, chunk) if arm in mp.ARRIVAL_ARMS else None
+        ids = mp.linear_tile_ids(m, n, 2048, world, chunk, arm, plan, tile_n=256)
+        assert sorted(ids) == list(range((m // 128) * (n // 256)))
+        for rank in (0, 7):
+            local = mp.consumer_tile_order(m, n, 2048, world, chunk, arm, rank, plan, 256)
+            assert sorted(local) == list(range((m // world // 128) * (n // 256)))
+
+
+def test_plan_only_for_arrival_arm():
+    plan = pl.make_role(2048, 4096, 512, 8, 128)
+    with pytest.raises(ValueError):
+        mp.schedule(2048, 4096, 512, 8, 128, "flux", plan)
+    mutated = dict(plan)
+    mutated["arrival_order"] = list(reversed(plan["arrival_order"]))
+    with pytest.raises(ValueError):
+        mp.schedule(2048, 4096, 512, 8, 128, "flux_taco_interleaved_arrival", mutated)
