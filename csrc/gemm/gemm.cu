@@ -114,6 +114,9 @@ int run(const GemmCall& c, cudaStream_t stream) {
     if (!c.out) return fail("gemm: null output");
     if ((reinterpret_cast<uintptr_t>(c.out) & 15) || (c.ldo % 8))
       return fail("gemm: output must be 16-byte aligned with ldo % 8 == 0");
+    if ((c.epi & kEpiGelu) && (c.epi & kEpiGeluBwd)) return fail("gemm: gelu and gelu-backward are exclusive");
+    if ((c.epi & kEpiGeluBwd) && (!c.aux || (reinterpret_cast<uintptr_t>(c.aux) & 15) || c.ld_aux % 8))
+      return fail("gemm: gelu-backward epilogue needs an aligned pre-activation input");
     if ((c.epi & kEpiGelu) && (!c.aux || (reinterpret_cast<uintptr_t>(c.aux) & 15) || c.ld_aux % 8))
       return fail("gemm: gelu epilogue needs an aligned aux output");
     if ((c.epi & kEpiResidual) && (!c.residual || (reinterpret_cast<uintptr_t>(c.residual) & 15) || c.ld_res % 8))

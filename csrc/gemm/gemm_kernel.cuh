@@ -46,6 +46,7 @@ enum EpiFlags : int {
   kEpiGelu = 2,        // aux = bf16(acc+bias); out = bf16(gelu(aux))
   kEpiResidual = 4,    // out = bf16(bf16(res + bf16(acc)) + bias)
   kEpiAccumulate = 8,  // out = bf16(float(out) + acc)
+  kEpiGeluBwd = 16,    // out = bf16(bf16(acc) * gelu'(aux)), aux = saved pre-activation (input)
 };
 
 // Modes of the epilogue destination.
@@ -131,6 +132,13 @@ __device__ __forceinline__ float bf16_round_f(float x) {
 __device__ __forceinline__ float gelu_exact(float x) {
   // 0.5 * x * (1 + erf(x / sqrt(2))), CUDA's erff called directly.
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+__device__ __forceinline__ float gelu_grad(float z) {
+  // d/dz [z * Phi(z)] = Phi(z) + z * phi(z); erff / expf called directly.
+  const float cdf = 0.5f * (1.0f + erff(z * 0.70710678118654752440f));
+  const float pdf = 0.39894228040143267794f * expf(-0.5f * z * z);
+  return cdf + z * pdf;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -481,6 +489,18 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
                 const float bb = (p.bias && col + i < p.N) ? __bfloat162float(p.bias[col + i]) : 0.f;
                 v[8 * u + i] = p.bias ? __fadd_rn(s, bb) : s;
               }
+            }
+          }
+          if (p.epi & kEpiGeluBwd) {
+#pragma unroll
+            for (int u = 0; u < EPI_COLS / 8; ++u) {
+              const int col = col0 + 8 * u;
+              uint4 zv = make_uint4(0, 0, 0, 0);
+              if (row_ok && col < p.N) zv = ld_global_v4(p.aux + int64_t(my_row) * p.ld_aux + col);
+              const __nv_bfloat16* zb = reinterpret_cast<const __nv_bfloat16*>(&zv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                v[8 * u + i] = bf16_round_f(v[8 * u + i]) * gelu_grad(__bfloat162float(zb[i]));
             }
           }
           if (p.epi & kEpiAccumulate) {

@@ -1,0 +1,253 @@
+"""Fused row-parallel GEMM -> reduce-scatter ("GemmRS"), the four arms.
+
+    out[M/W, N] (rank r) = sum_s  A_s[M, K] @ B_s[N, K]^T  restricted to rows of r
+
+Transport `nvlink` (default): ONE persistent tcgen05 GEMM launch whose
+epilogue pushes every finished 128x256 tile straight into its owner's receive
+slot over NVLink (BF16, or a TACO H128/E4M3 packet for remote tiles in the
+quantized arms) and release-stores a per-(source, tile) epoch flag on the
+owner; then the owner's receiver kernel waits (bounded) on each tile's W flags
+and reduces in source order 0..W-1 with BF16 rounding after every source,
+fusing the TACO decode and an optional residual + bias epilogue.
+Arms A/B produce tiles destination-major, C/D interleave destinations at
+column-tile granularity (D in a calibrated arrival order); the arrival arm's
+receiver consumes whichever tile of its lane is fully ready first.  All arms
+share the arithmetic order, so the three TACO arms are bitwise equal.
+
+Transport `nccl` keeps the reference mechanism (TempName-5090
+python/flux_5090/runtime.py:161-241) as the baseline: the same GEMM writes the
+full partial, each physical block is exchanged with a sparse all_to_all on one
+of two lane communicators, and the owner runs the ordered (decode+)reduce.
+
+Receive slots are double-buffered by call parity.  Safety of reuse: the call
+t+2 push from rank s into rank r's parity slot happens after s's call t+1
+reduce, which waited for r's call t+1 GEMM tiles, which r issued after its own
+call t reduce (stream order) -- so r never reads a slot being overwritten.
+"""
+from __future__ import annotations
+
+import contextlib
+
+import torch
+import torch.distributed as dist
+
+from .._native import count_launch, lib, status_tensor
+from . import mapping
+from .symmetric import SymmetricBuffer
+
+TILE_N = 256
+DEFAULT_TIMEOUT_NS = 10_000_000_000
+
+
+class _Lanes:
+    """Two extra NCCL communicators + streams for the NCCL transport (per group)."""
+    _cache: dict = {}
+
+    @classmethod
+    def get(cls, group):
+        key = id(group)
+        if key not in cls._cache:
+            ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+            lanes = tuple(dist.new_group(ranks=ranks, backend="nccl") for _ in range(2))
+            streams = tuple(torch.cuda.Stream() for _ in range(2))
+            cls._cache[key] = (lanes, streams)
+        return cls._cache[key]
+
+
+class RSWorkspace:
+    """Receive slots (2 parities x W sources), tile flags and the epoch sequence
+    shared by every GemmRS operator of one (M, N) on one group.  Any number of
+    operators may share it: each call is a full exchange, so the parity chain
+    argument holds across operators."""
+
+    def __init__(self, m: int, n: int, world: int, group=None, *, recv=None, flags=None):
+        self.rows = m // world
+        self.slot_bytes = self.rows * n * 2
+        self.tiles_per_dest = (self.rows // 128) * (n // TILE_N)
+        if recv is None:
+            recv = [SymmetricBuffer(world * self.slot_bytes, group) for _ in range(2)]
+            flags = SymmetricBuffer(world * self.tiles_per_dest * 4, group)
+        self.recv, self.flags = recv, flags
+        self.claims = torch.zeros(self.tiles_per_dest, dtype=torch.int32,
+                                  device=torch.device("cuda", torch.cuda.current_device()))
+        self.epoch = 0
+
+    def close(self):
+        for b in self.recv:
+            if isinstance(b, SymmetricBuffer) and b._owned:
+                b.close()
+        if isinstance(self.flags, SymmetricBuffer) and self.flags._owned:
+            self.flags.close()
+
+
+class GemmRS:
+    def __init__(self, m: int, n: int, k: int, group=None, arm: str = "flux", chunk_rows: int = 128,
+                 plan=None, transport: str = "nvlink", timeout_ns: int = DEFAULT_TIMEOUT_NS,
+                 b_mn: bool = False, workspace: RSWorkspace | None = None,
+                 _emulate: tuple | None = None):
+        if arm not in mapping.ARMS:
+            raise ValueError(f"unknown arm {arm}")
+        if transport not in ("nvlink", "nccl"):
+            raise ValueError("transport must be 'nvlink' or 'nccl'")
+        if _emulate is not None:
+            self.rank, self.world = _emulate[0], _emulate[1]
+        else:
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        mapping.validate_shape(m, n, k, self.world, chunk_rows)
+        if n % TILE_N:
+            raise ValueError("N must be a multiple of 256 for the fused GemmRS")
+        self.m, self.n, self.k, self.chunk_rows = m, n, k, chunk_rows
+        self.group, self.arm, self.transport, self.b_mn = group, arm, transport, b_mn
+        self.plan = plan
+        self.quantized = arm in mapping.QUANTIZED_ARMS
+        self.arrival = arm in mapping.ARRIVAL_ARMS
+        self.rows = m // self.world
+        self.timeout_ns = int(timeout_ns)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.order = mapping.schedule(m, n, k, self.world, chunk_rows, arm, plan)
+        ids = mapping.linear_tile_ids(m, n, k, self.world, chunk_rows, arm, plan, tile_n=TILE_N)
+        self.tile_order = torch.tensor(ids, dtype=torch.int32, device=self.device)
+        local = mapping.consumer_tile_order(m, n, k, self.world, chunk_rows, arm, self.rank, plan, TILE_N)
+        self.consumer_order = torch.tensor(local, dtype=torch.int32, device=self.device)
+        self.tiles_per_dest = (self.rows // 128) * (n // TILE_N)
+        self.slot_bytes = self.rows * n * 2
+        self._nccl_epoch = 0
+        self.calls = 0
+        self.failed = False
+        self.status = status_tensor(self.device)
+        self.workspace = None
+        if transport == "nvlink":
+            if _emulate is not None:
+                workspace = RSWorkspace(m, n, self.world, recv=_emulate[2], flags=_emulate[3])
+            self.workspace = workspace if workspace is not None else RSWorkspace(m, n, self.world, group)
+        else:
+            self.lanes, self.lane_streams = _Lanes.get(group)
+            self.partial = torch.empty((m, n), dtype=torch.bfloat16, device=self.device)
+            pbytes = chunk_rows * n // 128 * 136
+            self.packet_bytes = pbytes
+            self.send_packets = torch.empty((m // chunk_rows, pbytes), dtype=torch.uint8, device=self.device)
+            self.recv_blocks = torch.empty((m // chunk_rows // self.world, self.world - 1,
+                                            chunk_rows * n * 2), dtype=torch.uint8, device=self.device)
+
+    @property
+    def epoch(self) -> int:
+        return self.workspace.epoch if self.workspace is not None else self._nccl_epoch
+
+    @epoch.setter
+    def epoch(self, value: int) -> None:
+        if self.workspace is not None:
+            self.workspace.epoch = value
+        else:
+            self._nccl_epoch = value
+
+    @property
+    def recv(self):
+        return self.workspace.recv
+
+    @property
+    def flags(self):
+        return self.workspace.flags
+
+    @property
+    def claims(self):
+        return self.workspace.claims
+
+    # ------------------------------------------------------------------ API
+    def forward(self, x: torch.Tensor, w: torch.Tensor, *, b_mn: bool | None = None, residual=None,
+                bias=None, out=None) -> torch.Tensor:
+        """x [M, K] bf16; w [N, K] (or [K, N] when b_mn); returns [M/W, N] bf16."""
+        b_mn = self.b_mn if b_mn is None else b_mn
+        if self.failed:
+            raise RuntimeError("this GemmRS operator previously failed")
+        if self.epoch + 2 >= 2 ** 31:
+            raise RuntimeError("epoch exhausted; create a new operator")
+        out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device) if out is None else out
+        self.epoch += 1
+        try:
+            if self.transport == "nvlink":
+                self.push(x, w, b_mn)
+                self.reduce(out, residual, bias)
+            else:
+                self._forward_nccl(x, w, b_mn, residual, bias, out)
+        except BaseException:
+            self.failed = True
+            raise
+        self.calls += 1
+        return out
+
+    def push(self, x, w, b_mn: bool | None = None):
+        """Producer phase: the GEMM whose epilogue pushes tiles to their owners."""
+        b_mn = self.b_mn if b_mn is None else b_mn
+        parity = self.epoch & 1
+        mode = 2 if self.quantized else 1
+        lib().gemm_rs_push(x, False, w, b_mn, mode, self.recv[parity].ptrs.data_ptr(),
+                           self.flags.ptrs.data_ptr(), self.rank, self.world, self.chunk_rows,
+                           self.epoch, self.slot_bytes, self.tile_order, self.status, self.timeout_ns, 0)
+        count_launch()
+
+    def begin(self):
+        """Emulation only: start a call (epoch + 1) whose phases are launched separately."""
+        self.epoch += 1
+
+    def reduce(self, out, residual=None, bias=None):
+        """Receiver phase: bounded waits on tile flags, ordered (decode +) reduce."""
+        parity = self.epoch & 1
+        count_launch()
+        lib().rs_reduce(self.recv[parity].local, self.flags.local, self.slot_bytes, self.rank, self.world,
+                        self.rows, self.n, TILE_N, self.chunk_rows, self.quantized, self.epoch, out,
+                        residual, bias, self.consumer_order, self.arrival,
+                        self.claims if self.arrival else None, self.status, self.timeout_ns, 0)
+
+    def _forward_nccl(self, x, w, b_mn, residual, bias, out):
+        from ..ops import gemm as G, taco
+        G.matmul(x, w, b_t=b_mn, out=self.partial, tile_order=None)
+        stream = torch.cuda.current_stream()
+        per = self.rows // self.chunk_rows
+        elements = self.chunk_rows * self.n
+        received = torch.cuda.Event()
+        for item in self.order:
+            p, dest, within, lane = item["physical"], item["destination"], item["within"], item["lane"]
+            block = self.partial.narrow(0, p * self.chunk_rows, self.chunk_rows)
+            local = dest == self.rank
+            if self.quantized:
+                send = self.send_packets[p] if not local else self.send_packets[p][:0]
+                if not local:
+                    taco.encode(block, send)
+                count = self.packet_bytes
+            else:
+                send = block.reshape(-1).view(torch.uint8) if not local else block.reshape(-1).view(torch.uint8)[:0]
+                count = elements * 2
+            recv = self.recv_blocks[within].reshape(-1)[: (self.world - 1) * count] if local else \
+                self.recv_blocks[0].reshape(-1)[:0]
+            sends, receives = mapping.split_sizes(self.world, self.rank, dest, count)
+            dist.all_to_all_single(recv, send, output_split_sizes=receives, input_split_sizes=sends,
+                                   group=self.lanes[lane])
+            if local:
+                target = out.narrow(0, within * self.chunk_rows, self.chunk_rows)
+                if self.quantized:
+                    taco.decode_reduce(block, recv.view(self.world - 1, count), self.rank, self.world, out=target)
+                else:
+                    taco.ordered_reduce(block, recv.view(torch.bfloat16), self.rank, self.world, out=target)
+        if residual is not None or bias is not None:
+            y = out.float()
+            if residual is not None:
+                y = (residual.float() + y).to(torch.bfloat16).float()
+            if bias is not None:
+                y = y + bias.float()
+            out.copy_(y.to(torch.bfloat16))
+
+    def state(self) -> dict:
+        return dict(backend=mapping.BACKEND, transport=self.transport, arm=self.arm, rank=self.rank,
+                    world=self.world, calls=self.calls, epoch=self.epoch,
+                    shape=[self.m, self.n, self.k], chunk_rows=self.chunk_rows,
+                    production_schedule=self.order, tile_n=TILE_N,
+                    quantization="all_remote_h128_e4m3" if self.quantized else "none",
+                    remote_wire_bytes_per_source=mapping.wire_bytes(self.m, self.n, self.world, self.quantized),
+                    reduction_order=list(range(self.world)), rounding="bf16_after_each_source",
+                    consumer_policy="per_lane_ready" if self.arrival else "ordered",
+                    transport_lanes=2, producer_launches_per_call=1,
+                    publication="system-release-per-tile-epoch")
+
+    def close(self):
+        if self.workspace is not None:
+            self.workspace.close()

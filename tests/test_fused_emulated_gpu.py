@@ -1,0 +1,155 @@
+"""Fused GEMM->RS and AG->GEMM kernels with W ranks emulated on ONE GPU.
+
+Every rank's buffers are local allocations; each emulated rank's kernels are
+launched in an order where every wait is already satisfied when the kernel
+starts (producers before receivers, peers' pushes pre-filled), so no launch
+ever waits on another launch.
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _gen(seed):
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("arm", ["flux", "flux_taco", "flux_taco_interleaved", "flux_taco_interleaved_arrival"])
+def test_gemm_rs_emulated_bitwise(world, arm):
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    from tempname_5090_b200.parallel import planning
+    from tempname_5090_b200.ops import gemm as G, taco
+    from tempname_5090_b200._native import check_status
+    chunk = 128
+    m, n, k = world * 256, 512, 320
+    rows = m // world
+    slot = rows * n * 2
+    tiles = (rows // 128) * (n // 256)
+    recv = [SymmetricBuffer.emulated(world * slot, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(world * tiles * 4, world)
+    plan = None
+    if arm.endswith("arrival"):
+        order = planning.candidates(m, n, k, world, chunk)[1]["arrival_order"]
+        plan = planning.make_role(m, n, k, world, chunk, order)
+    ops = [GemmRS(m, n, k, arm=arm, chunk_rows=chunk, plan=plan,
+                  _emulate=(r, world, [b.as_rank(r) for b in recv], flags.as_rank(r))) for r in range(world)]
+    xs = [torch.randn((m, k), generator=_gen(r), device="cuda").to(torch.bfloat16) for r in range(world)]
+    ws = [(0.05 * torch.randn((n, k), generator=_gen(100 + r), device="cuda")).to(torch.bfloat16) for r in range(world)]
+    for call in range(3):  # several calls exercise both slot parities and epochs
+        for op in ops:
+            op.begin()
+        for r, op in enumerate(ops):
+            op.push(xs[r], ws[r])
+        outs = []
+        for op in ops:
+            out = torch.empty((rows, n), dtype=torch.bfloat16, device="cuda")
+            op.reduce(out)
+            outs.append(out)
+        torch.cuda.synchronize()
+        check_status()
+        partials = [G.matmul(xs[s], ws[s], bn=256) for s in range(world)]
+        for r in range(world):
+            local = partials[r][r * rows:(r + 1) * rows].contiguous()
+            if op.quantized:
+                blocks = []
+                for b in range(rows // chunk):
+                    pk = [taco.encode(partials[s][r * rows + b * chunk: r * rows + (b + 1) * chunk])
+                          for s in range(world) if s != r]
+                    blocks.append(taco.decode_reduce(local[b * chunk:(b + 1) * chunk].contiguous(),
+                                                     torch.cat(pk), r, world))
+                expect = torch.cat(blocks)
+            else:
+                remote = torch.cat([partials[s][r * rows:(r + 1) * rows] for s in range(world) if s != r])
+                expect = taco.ordered_reduce(local, remote, r, world)
+            assert torch.equal(outs[r], expect), (arm, world, r, call)
+        xs = [(x * 0.5 + 0.25).to(torch.bfloat16) for x in xs]
+
+
+def test_gemm_rs_fused_residual_bias():
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    from tempname_5090_b200.ops import gemm as G, taco
+    world, m, n, k = 2, 512, 256, 128
+    rows = m // world
+    recv = [SymmetricBuffer.emulated(world * rows * n * 2, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(world * (rows // 128) * (n // 256) * 4, world)
+    ops = [GemmRS(m, n, k, _emulate=(r, world, [b.as_rank(r) for b in recv], flags.as_rank(r))) for r in range(world)]
+    xs = [torch.randn((m, k), generator=_gen(r), device="cuda").to(torch.bfloat16) for r in range(world)]
+    ws = [torch.randn((n, k), generator=_gen(9 + r), device="cuda").to(torch.bfloat16) for r in range(world)]
+    res = torch.randn((rows, n), generator=_gen(5), device="cuda").to(torch.bfloat16)
+    bias = torch.randn((n,), generator=_gen(6), device="cuda").to(torch.bfloat16)
+    for op in ops:
+        op.begin()
+    for r, op in enumerate(ops):
+        op.push(xs[r], ws[r])
+    out = torch.empty((rows, n), dtype=torch.bfloat16, device="cuda")
+    ops[0].reduce(out, residual=res, bias=bias)
+    plain = torch.empty_like(out)
+    ops[1].reduce(torch.empty_like(out))
+    parts = [G.matmul(xs[s], ws[s], bn=256) for s in range(world)]
+    y = taco.ordered_reduce(parts[0][:rows].contiguous(), parts[1][:rows].contiguous(), 0, world)
+    expect = ((res.float() + y.float()).to(torch.bfloat16).float() + bias.float()).to(torch.bfloat16)
+    assert torch.equal(out, expect)
+
+
+@pytest.mark.parametrize("world,bn", [(2, 128), (4, 256), (8, 256)])
+@pytest.mark.parametrize("epi", ["plain", "bias_gelu", "mn_major"])
+def test_ag_gemm_emulated(world, bn, epi):
+    from tempname_5090_b200.parallel.ag_gemm import AGGemm
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    from tempname_5090_b200.ops import gemm as G
+    from tempname_5090_b200._native import check_status, lib
+    m, k, n = world * 256, 256, 768
+    rows = m // world
+    gather = SymmetricBuffer.emulated(m * k * 2, world)
+    flags = SymmetricBuffer.emulated(world * 4, world)
+    shards = [torch.randn((rows, k), generator=_gen(r), device="cuda").to(torch.bfloat16) for r in range(world)]
+    full = torch.cat(shards)
+    w = (0.05 * torch.randn((n, k), generator=_gen(77), device="cuda")).to(torch.bfloat16)
+    w_mn = w.t().contiguous()
+    bias = torch.randn((n,), generator=_gen(78), device="cuda").to(torch.bfloat16)
+    grid = lib().gemm_grid(m, n, bn, 0)
+    for r in range(world):
+        op = AGGemm(m, k, _emulate=(r, world, gather.as_rank(r), flags.as_rank(r)))
+        gview = gather.view(r, (m, k), torch.bfloat16)
+        fview = flags.view(r, (world,), torch.int32)
+        for c in range(world):
+            if c != r:
+                gview[c * rows:(c + 1) * rows].copy_(shards[c])
+        fview.fill_(grid)
+        fview[r] = 0
+        aux = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+        if epi == "plain":
+            out = op.forward(shards[r], w, bn=bn)
+            expect = G.matmul(full, w, bn=bn)
+        elif epi == "bias_gelu":
+            out = op.forward(shards[r], w, bias=bias, gelu_aux=aux, bn=bn)
+            aux_ref = torch.empty_like(aux)
+            expect = G.matmul(full, w, bias=bias, gelu_aux=aux_ref, bn=bn)
+        else:
+            out = op.forward(shards[r], w_mn, b_mn=True, bn=bn)
+            expect = G.matmul(full, w_mn, b_t=True, bn=bn)
+        torch.cuda.synchronize()
+        check_status()
+        assert torch.equal(op.gathered, full)
+        assert torch.equal(out, expect)
+        if epi == "bias_gelu":
+            assert torch.equal(aux, aux_ref)
+        assert int(fview[r].item()) == grid
+
+
+def test_bounded_wait_times_out_and_context_survives():
+    from tempname_5090_b200._native import lib, status_tensor, check_status
+    flag = torch.zeros(4, dtype=torch.int32, device="cuda")
+    status = status_tensor("cuda")
+    status.zero_()
+    lib().wait_probe(flag.data_ptr(), 1, 200_000_000, status)  # 0.2 s, nothing ever sets it
+    torch.cuda.synchronize()
+    assert int(status[0].item()) == 5
+    status.zero_()
+    x = torch.ones(8, device="cuda")
+    assert x.sum().item() == 8.0  # context still usable
+    check_status()

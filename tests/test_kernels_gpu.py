@@ -1,0 +1,188 @@
+"""Numerics of the SIMT / warp-MMA kernels against plain PyTorch FP32 references."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(x, y):
+    return ((x.float() - y.float()).norm() / y.float().norm().clamp_min(1e-12)).item()
+
+
+def gen(seed=0):
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+# ----------------------------------------------------------------- TACO codec
+def test_taco_encode_matches_stdlib_oracle():
+    from tempname_5090_b200.ops import taco
+    from tempname_5090_b200.utils import reference as ref
+    x = torch.randn(128 * 6, generator=gen(1), device="cuda").to(torch.bfloat16)
+    x[5] = 120.0
+    x[300] = -96.0
+    packet = taco.encode(x)
+    decoded = taco.decode(packet, x.numel())
+    pbytes = bytes(packet.cpu().tolist())
+    oracle_from_bytes = ref.decode(pbytes)
+    oracle_end_to_end = ref.decode(ref.encode(x.float().cpu().tolist()))
+    assert ref.relative_l2(decoded.float().cpu().tolist(), oracle_from_bytes) <= 0.003
+    assert ref.relative_l2(decoded.float().cpu().tolist(), oracle_end_to_end) <= 0.02
+    assert ref.relative_l2(decoded.float().cpu().tolist(), x.float().cpu().tolist()) <= 0.05
+
+
+def test_taco_device_matches_cpu_statement():
+    from tempname_5090_b200.ops import taco
+    x = torch.randn(128 * 64, generator=gen(2), device="cuda").to(torch.bfloat16)
+    p_dev = taco.encode(x)
+    p_cpu = taco.encode(x.cpu())
+    # Scales may differ by rsqrt ulps; payload codes agree almost everywhere.
+    same = (p_dev[: x.numel()].cpu() == p_cpu[: x.numel()]).float().mean().item()
+    assert same > 0.97
+    assert rel(taco.decode(p_dev, x.numel()), x) < 0.05
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_decode_reduce_is_bitwise_decode_then_ordered_reduce(world):
+    from tempname_5090_b200.ops import taco
+    n = 128 * 32
+    local = torch.randn(n, generator=gen(world), device="cuda").to(torch.bfloat16)
+    sources = [torch.randn(n, generator=gen(10 + s), device="cuda").to(torch.bfloat16) for s in range(world - 1)]
+    packets = torch.cat([taco.encode(s) for s in sources])
+    for rank in range(world):
+        fused = taco.decode_reduce(local, packets, rank, world)
+        decoded = torch.cat([taco.decode(taco.encode(s), n) for s in sources])
+        plain = taco.ordered_reduce(local, decoded, rank, world)
+        assert torch.equal(fused, plain)
+        ordered = [local if s == rank else decoded.view(world - 1, n)[s - (s > rank)] for s in range(world)]
+        assert torch.equal(plain, taco.ordered_sum_cpu([o.cpu() for o in ordered]).cuda())
+
+
+# ---------------------------------------------------------------- LayerNorm
+@pytest.mark.parametrize("H", [256, 1024, 4096])
+def test_layernorm_fwd_bwd(H):
+    from tempname_5090_b200.ops import norm
+    rows = 300
+    x = torch.randn((rows, H), generator=gen(3), device="cuda").to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, generator=gen(4), device="cuda")).to(torch.bfloat16)
+    b = (0.1 * torch.randn(H, generator=gen(5), device="cuda")).to(torch.bfloat16)
+    y, mean, rstd = norm.layer_norm_fwd(x, w, b, 1e-5)
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    bf = b.float().requires_grad_(True)
+    yr = F.layer_norm(xf, (H,), wf, bf, 1e-5)
+    assert rel(y, yr) < 1e-2
+    dy = torch.randn((rows, H), generator=gen(6), device="cuda").to(torch.bfloat16)
+    yr.backward(dy.float())
+    dres = torch.randn((rows, H), generator=gen(7), device="cuda").to(torch.bfloat16)
+    dx, dw, db = norm.layer_norm_bwd(dy, x, w, mean, rstd, dres=dres)
+    assert rel(dx, xf.grad + dres.float()) < 1e-2
+    assert rel(dw, wf.grad) < 1e-2
+    assert rel(db, bf.grad) < 1e-2
+
+
+def test_gelu_bwd_and_column_sum():
+    from tempname_5090_b200.ops import norm
+    z = torch.randn((256, 512), generator=gen(8), device="cuda").to(torch.bfloat16)
+    dy = torch.randn((256, 512), generator=gen(9), device="cuda").to(torch.bfloat16)
+    zf = z.float().requires_grad_(True)
+    F.gelu(zf).backward(dy.float())
+    assert rel(norm.gelu_bwd(dy, z), zf.grad) < 1e-2
+    g = torch.randn((5000, 640), generator=gen(10), device="cuda").to(torch.bfloat16)
+    assert rel(norm.column_sum(g), g.float().sum(0)) < 1e-2
+
+
+# ------------------------------------------------------------ cross-entropy
+def test_cross_entropy_fwd_bwd():
+    from tempname_5090_b200.ops import loss
+    M, V = 512, 6288
+    logits = (3 * torch.randn((M, V), generator=gen(11), device="cuda")).to(torch.bfloat16)
+    targets = torch.randint(0, V, (M,), generator=gen(12), device="cuda")
+    value, state = loss.forward(logits, targets)
+    lf = logits.float().requires_grad_(True)
+    ref = F.cross_entropy(lf, targets)
+    assert abs(value.item() - ref.item()) < 1e-3 * max(1.0, abs(ref.item()))
+    ref.backward()
+    work = logits.clone()
+    loss.backward(work, targets, state, 1.0 / M)
+    assert rel(work, lf.grad) < 1e-2
+
+
+# ---------------------------------------------------------------- optimizer
+def test_adamw_and_norm_match_torch():
+    from tempname_5090_b200.ops import optim
+    n = 4096 + 1024
+    n_decay = 4096
+    master = torch.randn(n, generator=gen(13), device="cuda")
+    grad = (0.01 * torch.randn(n, generator=gen(14), device="cuda")).to(torch.bfloat16)
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    param = master.to(torch.bfloat16)
+    norm2 = torch.zeros((), dtype=torch.float64, device="cuda")
+    optim.sqsum(grad, norm2)
+    assert abs(norm2.item() - grad.float().square().sum(dtype=torch.float64).item()) < 1e-6 * norm2.item()
+    p_ref = torch.nn.Parameter(master.clone())
+    p_ref2 = torch.nn.Parameter(master.clone())
+    opt = torch.optim.AdamW([dict(params=[p_ref], weight_decay=0.01), dict(params=[p_ref2], weight_decay=0.0)],
+                            lr=1e-3, betas=(0.9, 0.95), eps=1e-8, foreach=False)
+    coef = min(1.0 / (math.sqrt(norm2.item()) + 1e-6), 1.0)
+    for step in range(1, 4):
+        optim.adamw(master, m, v, grad, param, n_decay, norm2, max_norm=1.0, lr=1e-3, weight_decay=0.01,
+                    beta1=0.9, beta2=0.95, eps=1e-8, step=step)
+        p_ref.grad = grad.float() * coef
+        p_ref2.grad = grad.float() * coef
+        opt.step()
+    expect = torch.cat([p_ref.detach()[:n_decay], p_ref2.detach()[n_decay:]])
+    assert (master - expect).abs().max().item() < 1e-5
+    assert torch.equal(param, master.to(torch.bfloat16))
+
+
+# --------------------------------------------------------------- embeddings
+def test_embedding_lookup_and_grad():
+    from tempname_5090_b200.ops import embedding
+    V, H, M, start = 1000, 256, 4096, 3000
+    table = torch.randn((V, H), generator=gen(15), device="cuda").to(torch.bfloat16)
+    tokens = torch.randint(2500, 4500, (M,), generator=gen(16), device="cuda")
+    out = embedding.lookup(tokens, table, start)
+    ref = embedding.lookup(tokens.cpu(), table.cpu(), start)
+    assert torch.equal(out.cpu(), ref)
+    g = torch.randn((M, H), generator=gen(17), device="cuda").to(torch.bfloat16)
+    base = torch.randn((V, H), generator=gen(18), device="cuda").to(torch.bfloat16)
+    dev = embedding.lookup_grad(tokens, g, base.clone(), start)
+    cpu = embedding.lookup_grad(tokens.cpu(), g.cpu(), base.cpu().clone(), start)
+    assert rel(dev, cpu.cuda()) < 1e-2
+    again = embedding.lookup_grad(tokens, g, base.clone(), start)
+    assert torch.equal(dev, again)  # deterministic
+    P = torch.randn((512, H), generator=gen(19), device="cuda").to(torch.bfloat16)
+    x = torch.randn((1024, H), generator=gen(20), device="cuda").to(torch.bfloat16)
+    got = embedding.add_position(x.clone(), P, 256)
+    want = embedding.add_position(x.cpu().clone(), P.cpu(), 256)
+    assert rel(got, want.cuda()) < 1e-2
+    dP = embedding.position_grad(g[:1024].contiguous(), 512, 256)
+    dPc = embedding.position_grad(g[:1024].cpu().contiguous(), 512, 256)
+    assert rel(dP, dPc.cuda()) < 1e-2
+
+
+# ---------------------------------------------------------------- attention
+@pytest.mark.parametrize("B,S,H", [(1, 256, 1), (2, 512, 2), (1, 2048, 1)])
+def test_attention_fwd_bwd(B, S, H):
+    from tempname_5090_b200.ops import attention
+    d = 128
+    qkv = torch.randn((B * S, 3 * H * d), generator=gen(21), device="cuda").to(torch.bfloat16)
+    out, lse = attention.forward(qkv, B, S, H)
+    q, k, v = qkv.float().reshape(B, S, 3, H, d).permute(2, 0, 3, 1, 4).unbind(0)
+    q.requires_grad_(True); k.requires_grad_(True); v.requires_grad_(True)
+    o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    ref = o.transpose(1, 2).reshape(B * S, H * d)
+    assert rel(out, ref) < 1e-2
+    dout = torch.randn((B * S, H * d), generator=gen(22), device="cuda").to(torch.bfloat16)
+    ref.backward(dout.float())
+    dqkv = attention.backward(qkv, out, dout, lse, B, S, H)
+    dq, dk, dv = dqkv.float().reshape(B, S, 3, H, d).permute(2, 0, 3, 1, 4).unbind(0)
+    assert rel(dq, q.grad) < 2e-2
+    assert rel(dk, k.grad) < 2e-2
+    assert rel(dv, v.grad) < 2e-2
+    again = attention.backward(qkv, out, dout, lse, B, S, H)
+    assert torch.equal(again, dqkv)  # deterministic
