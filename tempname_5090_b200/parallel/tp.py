@@ -27,10 +27,12 @@ from ..ops import taco
 class TensorParallel:
     def __init__(self, group=None, *, arm: str = "flux", transport: str = "nvlink",
                  chunk_rows: int = 128, plans: dict | None = None, timeout_ns: int = 10_000_000_000):
-        self.group = group
-        self.initialized = dist.is_available() and dist.is_initialized()
-        self.world = dist.get_world_size(group) if self.initialized else 1
-        self.rank = dist.get_rank(group) if self.initialized else 0
+        # group="local": a single-rank context even inside an initialised job.
+        local = isinstance(group, str) and group == "local"
+        self.group = None if local else group
+        self.initialized = (not local) and dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(self.group) if self.initialized else 1
+        self.rank = dist.get_rank(self.group) if self.initialized else 0
         self.arm, self.transport, self.chunk_rows = arm, transport, chunk_rows
         self.plans = plans or {}
         self.timeout_ns = timeout_ns
