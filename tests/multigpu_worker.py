@@ -37,8 +37,11 @@ def case_gemm_rs(rank, world):
     dist.all_to_all_single(gathered, partial)
     sources = gathered.view(world, rows, n)
     outputs = {}
+    from tempname_5090_b200.parallel import planning
+    plan = planning.make_role(m, n, k, world, chunk, planning.candidates(m, n, k, world, chunk)[1]["arrival_order"])
     for arm in ("flux", "flux_taco", "flux_taco_interleaved", "flux_taco_interleaved_arrival"):
-        op = GemmRS(m, n, k, arm=arm, chunk_rows=chunk)
+        p = plan if arm.endswith("arrival") else None
+        op = GemmRS(m, n, k, arm=arm, chunk_rows=chunk, plan=p)
         for _ in range(3):
             out = op.forward(x, w)
         torch.cuda.synchronize()
@@ -55,7 +58,7 @@ def case_gemm_rs(rank, world):
             expect = taco.ordered_reduce(local, remote, rank, world)
         require(torch.equal(out, expect), f"GemmRS {arm} differs from all_to_all + ordered reduce")
         outputs[arm] = out
-        nccl = GemmRS(m, n, k, arm=arm, chunk_rows=chunk, transport="nccl").forward(x, w)
+        nccl = GemmRS(m, n, k, arm=arm, chunk_rows=chunk, plan=p, transport="nccl").forward(x, w)
         torch.cuda.synchronize()
         require(torch.equal(nccl, out), f"NCCL transport differs from NVLink transport for {arm}")
         op.close()
