@@ -47,6 +47,7 @@ def parse():
     ap.add_argument("--transport", default="nvlink", choices=("nvlink", "nccl"))
     ap.add_argument("--config", default="bench", choices=("bench", "small"))
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling only)")
     return ap.parse_args()
 
 
@@ -132,6 +133,8 @@ def main():
     cfg = dict(C.GPT_6P7B_BENCH if args.config == "bench" else C.SMALL)
     if args.config == "small":
         cfg.update(hidden=512, heads=4, ffn=2048, sequence=512, micro_batch=4, vocab=4096)
+    if args.layers:
+        cfg["layers"] = args.layers
     model = GPT(cfg, arm=args.arm, device=dev, transport=args.transport)
     trainer = Trainer(model)
     c = model.config
@@ -202,7 +205,8 @@ def main():
             "impl": "ours",
             "tokens_per_s": round(tokens / (ms / 1000.0), 1),
             "model_tflops_per_gpu": round(flops / (ms / 1000.0) / world / 1e12, 1),
-            "config": {"model": "GPT-6.7B" if args.config == "bench" else "GPT-small",
+            "config": {"model": ("GPT-6.7B" if args.config == "bench" else "GPT-small")
+                       + (f" ({c['layers']} layers: profiling, not the benchmark)" if args.layers else ""),
                        "layers": c["layers"], "hidden": c["hidden"], "heads": c["heads"], "ffn": c["ffn"],
                        "vocab": c["vocab"], "global_batch": c["micro_batch"] * c["accumulation_steps"],
                        "seq_len": c["sequence"], "tokens_per_step": tokens, "parallelism": f"tp{world}-sp",
