@@ -69,7 +69,7 @@ void gemm_rs_push(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn
                   int64_t recv_ptrs, int64_t flag_ptrs, int64_t rank, int64_t world,
                   int64_t chunk_rows, int64_t epoch, int64_t slot_bytes,
                   const at::Tensor& tile_order, const at::Tensor& status, int64_t timeout_ns,
-                  int64_t max_ctas) {
+                  int64_t max_ctas, int64_t delay_tile, int64_t delay_ns) {
   check_bf16(A, "A"); check_bf16(B, "B"); check_rows(A, "A"); check_rows(B, "B");
   const c10::cuda::CUDAGuard guard(A.device());
   tn5b::gemm::GemmCall c;
@@ -92,6 +92,8 @@ void gemm_rs_push(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn
   c.status = status_ptr(status);
   c.timeout_ns = uint64_t(timeout_ns);
   c.max_ctas = int(max_ctas);
+  c.delay_tile = int(delay_tile);
+  c.delay_ns = uint64_t(delay_ns);
   raise_if(tn5b::gemm::run(c, stream()), "gemm_rs_push");
 }
 

@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
       if (!s_ok) return;
       reduce_tile(c, tile, tiles_n);
       __syncthreads();
+      if (c.stamps && threadIdx.x == 0) c.stamps[tile] = globaltimer_ns();
     }
     return;
   }
@@ -184,6 +185,8 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
       continue;
     }
     reduce_tile(c, tile, tiles_n);
+    __syncthreads();
+    if (c.stamps && threadIdx.x == 0) c.stamps[tile] = globaltimer_ns();
   }
 }
 

@@ -25,6 +25,7 @@ struct RsReduceCall {
   const int* tile_order = nullptr; // optional consumption order of local tiles
   int arrival = 0;                 // 1: per-lane any-ready consumption (arrival-first)
   int* claims = nullptr;           // arrival mode: per-tile claim words [tiles]
+  unsigned long long* stamps = nullptr;  // optional: %globaltimer at each tile's completion
   int* status = nullptr;
   uint64_t timeout_ns = 0;
   int max_ctas = 0;

@@ -49,7 +49,7 @@ void rs_reduce(int64_t recv, int64_t flags, int64_t slot_bytes, int64_t rank, in
                int64_t epoch, at::Tensor& out, const c10::optional<at::Tensor>& residual,
                const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& tile_order,
                bool arrival, const c10::optional<at::Tensor>& claims, const at::Tensor& status,
-               int64_t timeout_ns, int64_t max_ctas) {
+               int64_t timeout_ns, int64_t max_ctas, const c10::optional<at::Tensor>& stamps) {
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.is_contiguous());
   TORCH_CHECK(out.size(0) == rows && out.size(1) == n, "rs_reduce: out must be [rows, n]");
   const c10::cuda::CUDAGuard guard(out.device());
@@ -76,6 +76,10 @@ void rs_reduce(int64_t recv, int64_t flags, int64_t slot_bytes, int64_t rank, in
   c.status = status.data_ptr<int>();
   c.timeout_ns = uint64_t(timeout_ns);
   c.max_ctas = int(max_ctas);
+  if (stamps) {
+    TORCH_CHECK(stamps->scalar_type() == at::kLong && stamps->is_cuda());
+    c.stamps = reinterpret_cast<unsigned long long*>(stamps->data_ptr<int64_t>());
+  }
   const int r = tn5b::comm::rs_reduce(c, at::cuda::getCurrentCUDAStream().stream());
   TORCH_CHECK(r == 0, "rs_reduce failed: ", r < 0 ? "bad arguments" : cudaGetErrorString(cudaError_t(r)));
 }

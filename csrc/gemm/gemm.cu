@@ -148,6 +148,8 @@ int run(const GemmCall& c, cudaStream_t stream) {
     p.rs.rank = c.rank; p.rs.world = c.world;
     p.rs.rows_per_dest = rows; p.rs.chunk_rows = c.chunk_rows;
     p.rs.epoch = c.epoch; p.rs.slot_bytes = c.slot_bytes;
+    if (c.delay_ns > 100000000ull) return fail("gemm-rs: diagnostic delay above 100 ms");
+    p.rs.delay_tile = c.delay_tile; p.rs.delay_ns = c.delay_ns;
   }
   if (c.ag) {
     if (!c.ag_chunk_flags || !c.ag_gather || !c.ag_peer_flags || !c.ag_shard || c.M % c.world)

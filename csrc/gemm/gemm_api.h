@@ -35,6 +35,8 @@ struct GemmCall {
   int chunk_rows = 128;
   uint32_t epoch = 0;
   int64_t slot_bytes = 0;
+  int delay_tile = -1;         // diagnostic: bounded publication delay of one tile
+  uint64_t delay_ns = 0;
   // all-gather
   int ag = 0;
   const uint32_t* ag_chunk_flags = nullptr;

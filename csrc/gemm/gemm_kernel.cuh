@@ -66,6 +66,10 @@ struct RsArgs {
   int chunk_rows;                // TACO packet block rows (reference macroblock)
   uint32_t epoch;
   int64_t slot_bytes;            // bytes of one source slot on a receiver
+  // Diagnostic only (never in timed paths): delay the flag publication of one
+  // tile (linear id) by a bounded `delay_ns` to create artificial lane skew.
+  int delay_tile;
+  uint64_t delay_ns;
 };
 
 struct AgArgs {
@@ -617,6 +621,10 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         if (warp == kEpiFirstWarp && lane == 0) {
           const int tiles_per_dest_m = p.rs.rows_per_dest / kBM;
           const int local_tile = (tm - dest * tiles_per_dest_m) * p.tiles_n + tn;
+          if (p.rs.delay_ns && tm * p.tiles_n + tn == p.rs.delay_tile) {
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < p.rs.delay_ns) __nanosleep(1000);
+          }
           fence_acq_rel_sys();
           st_release_sys(p.rs.flags[dest] + int64_t(p.rs.rank) * tiles_per_dest_m * p.tiles_n +
                              local_tile,

@@ -175,28 +175,62 @@ class GemmRS:
         self.calls += 1
         return out
 
-    def push(self, x, w, b_mn: bool | None = None):
+    def push(self, x, w, b_mn: bool | None = None, delay_tile: int = -1, delay_ns: int = 0):
         """Producer phase: the GEMM whose epilogue pushes tiles to their owners."""
         b_mn = self.b_mn if b_mn is None else b_mn
         parity = self.epoch & 1
         mode = 2 if self.quantized else 1
         lib().gemm_rs_push(x, False, w, b_mn, mode, self.recv[parity].ptrs.data_ptr(),
                            self.flags.ptrs.data_ptr(), self.rank, self.world, self.chunk_rows,
-                           self.epoch, self.slot_bytes, self.tile_order, self.status, self.timeout_ns, 0)
+                           self.epoch, self.slot_bytes, self.tile_order, self.status, self.timeout_ns, 0,
+                           delay_tile, delay_ns)
         count_launch()
 
     def begin(self):
         """Emulation only: start a call (epoch + 1) whose phases are launched separately."""
         self.epoch += 1
 
-    def reduce(self, out, residual=None, bias=None):
+    def reduce(self, out, residual=None, bias=None, stamps=None):
         """Receiver phase: bounded waits on tile flags, ordered (decode +) reduce."""
         parity = self.epoch & 1
         count_launch()
         lib().rs_reduce(self.recv[parity].local, self.flags.local, self.slot_bytes, self.rank, self.world,
                         self.rows, self.n, TILE_N, self.chunk_rows, self.quantized, self.epoch, out,
                         residual, bias, self.consumer_order, self.arrival,
-                        self.claims if self.arrival else None, self.status, self.timeout_ns, 0)
+                        self.claims if self.arrival else None, self.status, self.timeout_ns, 0, stamps)
+
+    def profile_call(self, x, w, *, delay_ns: int = 0, delay_rank: int = 0):
+        """Untimed diagnostic call: optionally delays (bounded, <= 100 ms) the flag
+        publication of the first lane-0 tile that `delay_rank` produces, and
+        returns (output, per-local-tile completion times in ns since the first
+        completion, the delayed tile's local id on its owner or None)."""
+        if self.transport != "nvlink":
+            raise RuntimeError("profile_call needs the NVLink transport")
+        if not 0 <= delay_ns <= 100_000_000:
+            raise ValueError("diagnostic delay must be within 100 ms")
+        out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device)
+        stamps = torch.zeros(self.tiles_per_dest, dtype=torch.int64, device=self.device)
+        self.epoch += 1
+        delay_tile, delayed_local = -1, None
+        if delay_ns:
+            tiles_n = self.n // TILE_N
+            per_dest_m = self.rows // 128
+            for tid in self.tile_order.tolist():
+                tm = tid // tiles_n
+                block = (tm * 128 % self.rows) // self.chunk_rows
+                if block % 2 == 0:
+                    delay_tile = tid
+                    dest = tm // per_dest_m
+                    delayed_local = (dest, (tm - dest * per_dest_m) * tiles_n + tid % tiles_n)
+                    break
+        self.push(x, w, delay_tile=delay_tile if self.rank == delay_rank else -1,
+                  delay_ns=delay_ns if self.rank == delay_rank else 0)
+        self.reduce(out, stamps=stamps)
+        self.calls += 1
+        torch.cuda.synchronize()
+        s = stamps.cpu()
+        rel = (s - s.min()).tolist()
+        return out, rel, delayed_local
 
     def _forward_nccl(self, x, w, b_mn, residual, bias, out):
         from ..ops import gemm as G, taco

@@ -1,0 +1,194 @@
+"""Operator benchmarks on one node (one process per GPU; launch with torchrun).
+
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m tempname_5090_b200.runner.opbench --op gemmrs
+    ... --op attention      # AG->GEMM QKV + causal attention + GemmRS out-proj (TP8, SP)
+    ... --op sweep          # GemmRS N=4096, K=16384/TP, M in 2048..32768, bf16 vs TACO
+
+Timing: every iteration is bracketed by CUDA events on the launching stream,
+the L2 is flushed (a 256 MiB write) between iterations outside the events,
+and the reported time is the MAX over ranks of the per-rank median.
+Baselines on the same box: `nccl+cublas` (torch.mm + NCCL reduce_scatter /
+all_gather + SDPA, the path that only calls libraries) and `transport=nccl`
+(this framework's GEMM + the reference's per-block sparse all_to_all mechanism).
+Roofline fraction = max(FLOPs / measured bf16 peak, NVLink bytes / 770 GB/s) / time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[2]
+
+
+def peaks() -> dict:
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return dict(bf16_tflops=float(d["bf16_tflops"]), nvlink_gbs=770.0, source="measured")
+    except (OSError, ValueError, KeyError):
+        return dict(bf16_tflops=1590.0, nvlink_gbs=770.0, source="fallback")
+
+
+class Timer:
+    def __init__(self, world, group=None):
+        import torch
+        self.torch = torch
+        self.world, self.group = world, group
+        self.flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+    def run(self, fn, warmup=5, iterations=20) -> float:
+        """Median microseconds per call, max over ranks."""
+        torch = self.torch
+        import torch.distributed as dist
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(iterations):
+            self.flush.fill_(1.0)
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e) * 1000.0)
+        med = torch.tensor(statistics.median(times), dtype=torch.float64, device="cuda")
+        if self.world > 1:
+            dist.all_reduce(med, op=dist.ReduceOp.MAX, group=self.group)
+        return float(med.item())
+
+
+def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True, chunk_rows=128):
+    import torch
+    import torch.distributed as dist
+    from ..parallel.gemm_rs import GemmRS
+    from ..parallel import planning
+    from ..ops import gemm as G
+    pk = peaks()
+    g = torch.Generator(device="cuda").manual_seed(17 + rank)
+    x = torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16)
+    w = (0.02 * torch.randn((n, k), generator=g, device="cuda")).to(torch.bfloat16)
+    flops = 2.0 * m * n * k
+    rows = []
+    for arm in arms:
+        plan = None
+        if arm.endswith("arrival"):
+            plan = planning.make_role(m, n, k, world, chunk_rows)
+        for transport in transports:
+            op = GemmRS(m, n, k, arm=arm, chunk_rows=chunk_rows, plan=plan, transport=transport)
+            us = timer.run(lambda: op.forward(x, w))
+            wire = (world - 1) * (m // world) * n * (136 / 128 if arm != "flux" else 2.0)
+            roof = max(flops / (pk["bf16_tflops"] * 1e12), wire / (pk["nvlink_gbs"] * 1e9)) * 1e6
+            rows.append(dict(op="gemmrs", arm=arm, transport=transport, m=m, n=n, k=k, world=world, us=us,
+                             roofline_us=roof, roofline_fraction=roof / us, tflops=flops / us / 1e6,
+                             nvlink_bytes_per_rank=wire, peaks=pk["source"]))
+            op.close()
+    # GEMM alone (no communication) and the library-only baseline
+    out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    rows.append(dict(op="gemm_only", m=m, n=n, k=k, us=timer.run(lambda: G.matmul(x, w, out=out))))
+    if with_library and world > 1:
+        rs = torch.empty((m // world, n), dtype=torch.bfloat16, device="cuda")
+
+        def library():
+            full = torch.mm(x, w.t())
+            dist.reduce_scatter_tensor(rs, full)
+        rows.append(dict(op="gemmrs", arm="flux", transport="nccl+cublas", m=m, n=n, k=k, world=world,
+                         us=timer.run(library)))
+        rows.append(dict(op="cublas_gemm_only", m=m, n=n, k=k, us=timer.run(lambda: torch.mm(x, w.t(), out=out))))
+    return rows
+
+
+def attention_case(rank, world, timer, heads=32, hidden=4096, seq=2048, batch=4):
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    from ..parallel.tp import TensorParallel
+    from ..ops import attention as A
+    tp = TensorParallel(None)
+    m = seq * batch
+    lh = heads // world
+    g = torch.Generator(device="cuda").manual_seed(5 + rank)
+    xs = torch.randn((m // world, hidden), generator=g, device="cuda").to(torch.bfloat16)
+    wqkv = (0.02 * torch.randn((3 * hidden // world, hidden), generator=g, device="cuda")).to(torch.bfloat16)
+    bqkv = torch.zeros(3 * hidden // world, dtype=torch.bfloat16, device="cuda")
+    wo = (0.02 * torch.randn((hidden, hidden // world), generator=g, device="cuda")).to(torch.bfloat16)
+    bo = torch.zeros(hidden, dtype=torch.bfloat16, device="cuda")
+
+    def ours():
+        qkv, _ = tp.ag_linear(("bench_qkv", 0), xs, wqkv, bias=bqkv)
+        attn, _ = A.forward(qkv, batch, seq, lh)
+        return tp.linear_rs(attn, wo, residual=xs, bias=bo, role="attn")
+
+    full = torch.empty((m, hidden), dtype=torch.bfloat16, device="cuda")
+    rs = torch.empty((m // world, hidden), dtype=torch.bfloat16, device="cuda")
+
+    def library():
+        dist.all_gather_into_tensor(full, xs)
+        qkv = F.linear(full, wqkv, bqkv)
+        q, k, v = qkv.view(batch, seq, 3, lh, 128).permute(2, 0, 3, 1, 4).unbind(0)
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(m, lh * 128)
+        dist.reduce_scatter_tensor(rs, torch.mm(a, wo.t()))
+        return rs
+
+    flops = 2 * m * hidden * 3 * hidden / world + 4 * batch * lh * seq * seq * 128 / 2 + 2 * m * hidden * hidden / world
+    rows = [dict(op="attention_block", impl="ours", world=world, us=timer.run(ours), flops=flops)]
+    if world > 1:
+        rows.append(dict(op="attention_block", impl="nccl+cublas+sdpa", world=world, us=timer.run(library), flops=flops))
+    tp.close()
+    return rows
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep"), default="gemmrs")
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--arms", default="all")
+    ap.add_argument("--transports", default="nvlink,nccl")
+    ap.add_argument("--out", type=Path)
+    args = ap.parse_args(argv)
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    timer = Timer(world)
+    from ..config import ARMS
+    arms = ARMS if args.arms == "all" else tuple(args.arms.split(","))
+    transports = tuple(args.transports.split(","))
+    rows = []
+    if args.op == "gemmrs":
+        rows += gemmrs_case(args.m, args.n, args.k, rank, world, timer, arms, transports)
+    elif args.op == "attention":
+        rows += attention_case(rank, world, timer)
+    else:
+        for m in (2048, 4096, 8192, 16384, 32768):
+            chunk = 128 if m // world >= 128 else None
+            if chunk is None:
+                continue
+            rows += gemmrs_case(m, 4096, 16384 // world, rank, world, timer, ("flux", "flux_taco"), ("nvlink",),
+                                with_library=(m == 8192))
+    if rank == 0:
+        for r in rows:
+            print(json.dumps(r), flush=True)
+        if args.out:
+            args.out.parent.mkdir(parents=True, exist_ok=True)
+            args.out.write_text("\n".join(json.dumps(r) for r in rows) + "\n")
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())
