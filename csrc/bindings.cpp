@@ -38,7 +38,8 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
           int64_t epi, const c10::optional<at::Tensor>& bias,
           const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& residual,
           const at::Tensor& status, int64_t bn, int64_t max_ctas,
-          const c10::optional<at::Tensor>& tile_order) {
+          const c10::optional<at::Tensor>& tile_order, int64_t pair, int64_t group_m,
+          const c10::optional<at::Tensor>& debug) {
   check_bf16(A, "A"); check_bf16(B, "B"); check_bf16(out, "out");
   check_rows(A, "A"); check_rows(B, "B"); check_rows(out, "out");
   const c10::cuda::CUDAGuard guard(A.device());
@@ -60,6 +61,9 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
   if (tile_order) { check_cuda(*tile_order, "tile_order"); TORCH_CHECK(tile_order->scalar_type() == at::kInt); c.tile_order = tile_order->data_ptr<int>(); }
   c.bn = int(bn);
   c.max_ctas = int(max_ctas);
+  c.pair = int(pair);
+  if (group_m > 0) c.group_m = int(group_m);
+  if (debug) c.debug = reinterpret_cast<unsigned long long*>(debug->data_ptr<int64_t>());
   c.status = status_ptr(status);
   raise_if(tn5b::gemm::run(c, stream()), "gemm");
 }
@@ -140,6 +144,7 @@ void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor
 int64_t gemm_grid(int64_t M, int64_t N, int64_t bn, int64_t mode) {
   tn5b::gemm::GemmCall c;
   c.M = int(M); c.N = int(N); c.bn = int(bn); c.mode = int(mode);
+  // same pair decision as ag_gemm's launch (auto)
   return tn5b::gemm::grid_ctas(c);
 }
 

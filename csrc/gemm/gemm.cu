@@ -62,11 +62,11 @@ int sm_count() {
   return v;
 }
 
-template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG>
+template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false>
 int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUtensorMap& mb,
            int grid, cudaStream_t stream) {
-  using L = SmemLayout<BN, STAGES, EPI_COLS>;
-  auto kern = gemm_kernel<BN, STAGES, EPI_COLS, MODE, AG>;
+  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR>;
+  auto kern = gemm_kernel<BN, STAGES, EPI_COLS, MODE, AG, PAIR>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -77,8 +77,33 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
     if (dev < 64) configured[dev] = true;
   }
   const int threads = kThreads + (AG ? 32 : 0);
-  kern<<<grid, threads, L::kTotal, stream>>>(ma, mb, p, c.a_mn, c.b_mn);
-  return int(cudaGetLastError());
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid), 1, 1);
+    cfg.blockDim = dim3(unsigned(threads), 1, 1);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return int(cudaLaunchKernelEx(&cfg, kern, ma, mb, p, c.a_mn, c.b_mn));
+  } else {
+    kern<<<grid, threads, L::kTotal, stream>>>(ma, mb, p, c.a_mn, c.b_mn);
+    return int(cudaGetLastError());
+  }
+}
+
+// CTA pairs (256 x 256 cluster tiles) for local / all-gather GEMMs with enough tiles.
+bool use_pair(const GemmCall& c, int bn) {
+  if (c.mode != 0 || bn != 256) return false;
+  if (c.pair == 0) return false;
+  if (c.pair == 1) return true;
+  const long pair_tiles = long((c.M + 255) / 256) * ((c.N + 255) / 256);
+  return pair_tiles >= sm_count() / 2;
 }
 
 int pick_bn(const GemmCall& c) {
@@ -97,9 +122,15 @@ std::string last_error() { return g_last_error; }
 
 int grid_ctas(const GemmCall& c) {
   const int bn = pick_bn(c);
-  const long tiles = long((c.M + kBM - 1) / kBM) * ((c.N + bn - 1) / bn);
+  const bool pair = use_pair(c, bn);
+  const int tile_m = pair ? 2 * kBM : kBM;
+  const long tiles = long((c.M + tile_m - 1) / tile_m) * ((c.N + bn - 1) / bn);
   int g = sm_count();
   if (c.max_ctas > 0 && c.max_ctas < g) g = c.max_ctas;
+  if (pair) {
+    const long clusters = tiles < g / 2 ? tiles : g / 2;
+    return int(2 * clusters);
+  }
   return int(tiles < g ? tiles : g);
 }
 
@@ -123,9 +154,10 @@ int run(const GemmCall& c, cudaStream_t stream) {
       return fail("gemm: residual epilogue needs an aligned residual");
   }
   const int bn = pick_bn(c);
+  const bool pair = use_pair(c, bn);
   Params p{};
   p.M = c.M; p.N = c.N; p.K = c.K;
-  p.tiles_m = (c.M + kBM - 1) / kBM;
+  p.tiles_m = (c.M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.tiles_n = (c.N + bn - 1) / bn;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_blocks = (c.K + kBK - 1) / kBK;
@@ -138,6 +170,7 @@ int run(const GemmCall& c, cudaStream_t stream) {
   p.residual = static_cast<const __nv_bfloat16*>(c.residual); p.ld_res = c.ld_res;
   p.status = c.status;
   p.timeout_ns = c.timeout_ns;
+  p.debug = c.debug;
   if (c.mode != 0) {
     if (!c.rs_recv || !c.rs_flags || c.world < 1 || c.M % c.world) return fail("gemm-rs: bad args");
     const int rows = c.M / c.world;
@@ -167,15 +200,17 @@ int run(const GemmCall& c, cudaStream_t stream) {
   const bool ok_a = c.a_mn ? make_map(&ma, c.A, c.M, c.K, c.lda, 64, 64)
                            : make_map(&ma, c.A, c.K, c.M, c.lda, 64, kBM);
   const bool ok_b = c.b_mn ? make_map(&mb, c.B, c.N, c.K, c.ldb, 64, 64)
-                           : make_map(&mb, c.B, c.K, c.N, c.ldb, 64, bn);
+                           : make_map(&mb, c.B, c.K, c.N, c.ldb, 64, pair ? bn / 2 : bn);
   if (!ok_a || !ok_b) return fail("gemm: cuTensorMapEncodeTiled failed");
   const int grid = grid_ctas(c);
   if (c.ag) {
+    if (pair) return launch<256, 6, 64, kModeLocal, true, true>(c, p, ma, mb, grid, stream);
     if (bn == 256) return launch<256, 4, 64, kModeLocal, true>(c, p, ma, mb, grid, stream);
     return launch<128, 6, 64, kModeLocal, true>(c, p, ma, mb, grid, stream);
   }
   switch (c.mode) {
     case 0:
+      if (pair) return launch<256, 6, 64, kModeLocal, false, true>(c, p, ma, mb, grid, stream);
       if (bn == 256) return launch<256, 4, 64, kModeLocal, false>(c, p, ma, mb, grid, stream);
       return launch<128, 6, 64, kModeLocal, false>(c, p, ma, mb, grid, stream);
     case 1:

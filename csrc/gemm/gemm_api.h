@@ -25,6 +25,7 @@ struct GemmCall {
   const int* tile_order = nullptr;
   int group_m = 8;
   int bn = 0;            // 0 = auto, else 128 / 256
+  int pair = -1;         // CTA-pair (cta_group::2) tiles: -1 auto, 0 off, 1 on
   int max_ctas = 0;      // 0 = all SMs
   // mode 0 local, 1 RS push bf16, 2 RS push TACO
   int mode = 0;
@@ -48,6 +49,7 @@ struct GemmCall {
   // status / bounded waits
   int* status = nullptr;
   uint64_t timeout_ns = 10ull * 1000 * 1000 * 1000;
+  unsigned long long* debug = nullptr;  // optional per-CTA cycle counters (4 per CTA)
 };
 
 // Number of CTAs the persistent kernel will launch for this call.

@@ -99,12 +99,16 @@ struct Params {
   AgArgs ag;
   int* status;
   uint64_t timeout_ns;
+  // Optional per-CTA cycle counters (profiling): [mma wait-full, mma total,
+  // producer wait-empty, epilogue wait-tmem-full].
+  unsigned long long* debug;
 };
 
-template <int BN, int STAGES, int EPI_COLS>
+template <int BN, int STAGES, int EPI_COLS, bool PAIR = false>
 struct SmemLayout {
   static constexpr int kABytes = kBM * kBK * 2;        // 16 KB
-  static constexpr int kBBytes = BN * kBK * 2;         // 32 KB at BN=256
+  // In a CTA pair each CTA holds half of B's N rows.
+  static constexpr int kBBytes = (PAIR ? BN / 2 : BN) * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStagingPerWarp = 32 * EPI_COLS * 2;
   static constexpr int kStagingBytes = kEpiWarps * kStagingPerWarp;
@@ -231,12 +235,22 @@ __device__ __forceinline__ uint32_t code(float x, float quant) {
 // ===========================================================================
 // The kernel.
 // ===========================================================================
-template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG>
+// PAIR: a cluster of two CTAs computes one 256 x BN tile with
+// tcgen05.mma.cta_group::2 issued by the leader (cluster rank 0).  Each CTA
+// TMA-loads its own 128 rows of A and its own BN/2 rows of B from this GPU's
+// memory (no multicast); both CTAs' loads complete on the leader's "full"
+// barrier, the leader's commits arrive on both CTAs' "empty" / "tmem full"
+// barriers, and both CTAs' epilogues release the accumulator on the leader's
+// "tmem empty" barrier.  Each CTA's TMEM holds its 128 rows x BN fp32.
+template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ Params p,
                 int a_mn, int b_mn) {
-  using L = SmemLayout<BN, STAGES, EPI_COLS>;
+  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR>;
+  static_assert(!PAIR || MODE == kModeLocal, "CTA pairs serve the local-store epilogue");
+  constexpr int kTileM = PAIR ? 2 * kBM : kBM;
+  constexpr int kBRows = PAIR ? BN / 2 : BN;
   static_assert(BN % EPI_COLS == 0, "epilogue chunks must tile BN");
   static_assert(MODE != kModeRsTaco || EPI_COLS == 128, "TACO groups are 128 columns");
   extern __shared__ uint8_t smem_raw[];
@@ -255,6 +269,10 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const uint32_t cta_rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = cta_rank == 0;
+  const int cluster_id = PAIR ? int(blockIdx.x / 2) : int(blockIdx.x);
+  const int clusters = PAIR ? int(gridDim.x / 2) : int(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -263,7 +281,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps);
+      mbar_init(&tempty[b], kEpiWarps * (PAIR ? 2 : 1));
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -274,11 +292,17 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     tma_prefetch_desc(&tmap_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * BN);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, 2 * BN);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 2 * BN);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // peer barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -286,16 +310,19 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int it = 0;
+      long long dbg_empty = 0;
       int last_parity[STAGES];
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
       bool ok = true;
       int waited_chunk = -1;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int t = cluster_id; t < p.num_tiles && ok; t += clusters) {
         int tm, tn;
         tile_coords(p, t, tm, tn);
+        const int row_a = tm * kTileM + int(cta_rank) * kBM;   // this CTA's A rows
+        const int row_b = tn * BN + int(cta_rank) * kBRows;    // this CTA's B rows
         if constexpr (AG) {
-          const int chunk = (tm * kBM) / p.ag.rows_per_src;
+          const int chunk = row_a / p.ag.rows_per_src;
           if (chunk != waited_chunk) {
             if (!wait_flag_geq(p.ag.chunk_flags + chunk, p.ag.target, p.timeout_ns, p.status,
                                kTimeoutAgChunk)) {
@@ -310,47 +337,77 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          const long long w0 = p.debug ? clock64() : 0;
           if (!mbar_wait(&empty[s], ph ^ 1, p.timeout_ns, p.status, kTimeoutProducerEmpty,
                          abort_flag)) {
             ok = false;
             break;
           }
+          if (p.debug) dbg_empty += clock64() - w0;
           uint8_t* sa = stage_base + s * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
-          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
           const int k0 = kb * kBK;
-          if (!a_mn) {
-            tma_load_2d(sa, &tmap_a, &full[s], k0, tm * kBM);
-          } else {
+          if constexpr (PAIR) {
+            // Both CTAs' bytes land on the leader's full barrier.
+            const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+            if (!a_mn) {
+              tma_load_2d_pair(sa, &tmap_a, fb, k0, row_a);
+            } else {
 #pragma unroll
-            for (int c = 0; c < kBM / 64; ++c)
-              tma_load_2d(sa + c * 8192, &tmap_a, &full[s], tm * kBM + c * 64, k0);
-          }
-          if (!b_mn) {
-            tma_load_2d(sb, &tmap_b, &full[s], k0, tn * BN);
-          } else {
+              for (int c = 0; c < kBM / 64; ++c) tma_load_2d_pair(sa + c * 8192, &tmap_a, fb, row_a + c * 64, k0);
+            }
+            if (!b_mn) {
+              tma_load_2d_pair(sb, &tmap_b, fb, k0, row_b);
+            } else {
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c)
-              tma_load_2d(sb + c * 8192, &tmap_b, &full[s], tn * BN + c * 64, k0);
+              for (int c = 0; c < kBRows / 64; ++c) tma_load_2d_pair(sb + c * 8192, &tmap_b, fb, row_b + c * 64, k0);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+            if (!a_mn) {
+              tma_load_2d(sa, &tmap_a, &full[s], k0, row_a);
+            } else {
+#pragma unroll
+              for (int c = 0; c < kBM / 64; ++c)
+                tma_load_2d(sa + c * 8192, &tmap_a, &full[s], row_a + c * 64, k0);
+            }
+            if (!b_mn) {
+              tma_load_2d(sb, &tmap_b, &full[s], k0, row_b);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c)
+                tma_load_2d(sb + c * 8192, &tmap_b, &full[s], row_b + c * 64, k0);
+            }
           }
           last_parity[s] = int(ph);
         }
       }
+      if (p.debug) p.debug[blockIdx.x * 4 + 2] = (unsigned long long)dbg_empty;
       if (!ok) {
         // Abort path: let every issued TMA load land before the CTA can exit.
-        for (int s = 0; s < STAGES; ++s)
-          if (last_parity[s] >= 0)
-            mbar_wait(&full[s], uint32_t(last_parity[s]), p.timeout_ns, p.status, kTimeoutDrain,
-                      nullptr);
+        if (!PAIR) {
+          for (int s = 0; s < STAGES; ++s)
+            if (last_parity[s] >= 0)
+              mbar_wait(&full[s], uint32_t(last_parity[s]), p.timeout_ns, p.status, kTimeoutDrain,
+                        nullptr);
+        } else {
+          // The pair's full barriers live in the leader; loads are long complete
+          // when a multi-second wait expires -- wait out their latency once more.
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 100000) __nanosleep(1000);
+        }
       }
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_bf16(kBM, BN, a_mn, b_mn);
+    if (lane == 0 && leader) {
+      long long dbg_full = 0;
+      const long long dbg_t0 = clock64();
+      const uint32_t idesc = make_idesc_bf16(kTileM, BN, a_mn, b_mn);
       int it = 0, local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+      for (int t = cluster_id; t < p.num_tiles && ok; t += clusters, ++local) {
         const int b = local & 1;
         const uint32_t use = uint32_t(local >> 1);
         if (!mbar_wait(&tempty[b], (use & 1) ^ 1, p.timeout_ns, p.status, kTimeoutMmaTmemEmpty,
@@ -363,10 +420,12 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          const long long w0 = p.debug ? clock64() : 0;
           if (!mbar_wait(&full[s], ph, p.timeout_ns, p.status, kTimeoutMmaFull, abort_flag)) {
             ok = false;
             break;
           }
+          if (p.debug) dbg_full += clock64() - w0;
           tc_fence_after();
           const uint32_t sa = smem_u32(stage_base + s * L::kStageBytes);
           const uint32_t sb = sa + L::kABytes;
@@ -376,16 +435,36 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
                                      : make_sw128_desc(sa + k * 32, 16, 1024);
             const uint64_t bd = b_mn ? make_sw128_desc(sb + k * 2048, 8192, 1024)
                                      : make_sw128_desc(sb + k * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          if constexpr (PAIR) {
+            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 0));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+          } else {
+            umma_commit(&empty[s]);
+          }
         }
         if (!ok) break;
-        umma_commit(&tfull[b]);
+        if constexpr (PAIR) {
+          umma_commit_pair(mapa_shared(smem_u32(&tfull[b]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&tfull[b]), 1));
+        } else {
+          umma_commit(&tfull[b]);
+        }
       }
       // All issued MMAs must finish before TMEM is released (normal and abort path).
-      umma_commit(drain);
+      if constexpr (PAIR)
+        umma_commit_pair(mapa_shared(smem_u32(drain), 0));
+      else
+        umma_commit(drain);
       mbar_wait(drain, 0, p.timeout_ns, p.status, kTimeoutDrain, nullptr);
+      if (p.debug) {
+        p.debug[blockIdx.x * 4 + 0] = (unsigned long long)dbg_full;
+        p.debug[blockIdx.x * 4 + 1] = (unsigned long long)(clock64() - dbg_t0);
+      }
     }
   } else if (warp < kEpiFirstWarp + kEpiWarps) {
     // ------------------------------------------------------------- epilogue
@@ -394,7 +473,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     uint8_t* stg = staging + ew * L::kStagingPerWarp;
     const uint32_t stg_addr = smem_u32(stg);
     int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+    for (int t = cluster_id; t < p.num_tiles; t += clusters, ++local) {
       int tm, tn;
       tile_coords(p, t, tm, tn);
       const int b = local & 1;
@@ -406,7 +485,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const int row_w = tm * kBM + q * 32;        // first row owned by this warp
+      const int row_w = tm * kTileM + int(cta_rank) * kBM + q * 32;  // first row of this warp
       const int my_row = row_w + lane;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * BN);
 
@@ -433,7 +512,12 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
           // Accumulator fully read: hand the TMEM buffer back to the MMA warp.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[b]);
+          if (lane == 0) {
+            if constexpr (PAIR)
+              mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
+            else
+              mbar_arrive(&tempty[b]);
+          }
         }
         if (col0 >= p.N) continue;  // whole chunk beyond N (tail tile)
 
@@ -659,9 +743,13 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
   // ------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the leader's MMAs into this CTA's TMEM are done
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, 2 * BN);
+    else
+      tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 

@@ -1,0 +1,744 @@
+// Causal attention forward on the sm_100a tensor cores (tcgen05 + TMEM + TMA),
+// head_dim 128, BF16 in/out, FP32 softmax statistics.
+//
+// One CTA per (128-query tile, batch*head); heavy (late) query tiles first.
+//   warp 0     TMA producer: the Q tile once, then K_j and V_j (128 keys each)
+//              through a 2-stage ring.  Q/K/V are read in place from the fused
+//              QKV buffer [tokens, 3*heads*128] with one 2-D tensor map.
+//   warp 1     MMA issuer: S_j = Q K_j^T into one of two TMEM buffers
+//              (M=128, N=128, K=16 x 8), then O += P_{j-1} V_{j-1} with the
+//              A operand (P, BF16) read from TMEM and V as an MN-major smem
+//              operand -- S_{j} is issued before PV_{j-1} so the softmax of
+//              block j overlaps the tensor work of block j-1.
+//   warps 2-5  softmax: thread = query row = TMEM lane; loads its 128 scores,
+//              applies the causal mask on the diagonal block, keeps a running
+//              max in the log2 domain and rescales O in TMEM only when the
+//              max grows by more than 2^8 (otherwise the stale max is exact:
+//              numerator and denominator share it), writes P = exp2(s - m) as
+//              packed BF16 over the same TMEM columns, and finally normalises O
+//              and writes O (BF16) and the row LSE (natural log).
+// TMEM: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+// Every wait is bounded; on a timeout the status word is set and the CTA exits.
+// Semantics: causal scaled_dot_product_attention (TempName-5090 model.py:255).
+#include "kernels_api.h"
+#include "../common/ptx.cuh"
+
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <mutex>
+
+namespace tn5b {
+namespace kernels {
+namespace {
+constexpr int kD = 128;
+constexpr int kBlk = 128;
+constexpr int kThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescale = 8.0f;
+
+constexpr int kSmQ = 0;               // 2 x 16 KB (d chunks)
+constexpr int kSmK = 32768;           // 2 stages x 32 KB
+constexpr int kSmV = 32768 * 3;       // 2 stages x 32 KB
+constexpr int kSmBar = 32768 * 5;
+constexpr int kSmTotal = kSmBar + 256 + 1024;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+// [rows, cols] bf16 row-major (ld elements), box 64 columns x 128 rows, 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// K-major operand tile [128 rows][128 d] stored as two 64-column SW128 chunks.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
+  return make_sw128_desc(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+// MN-major operand (V: rows = keys = K dim, columns = d = N dim), two 64-column chunks.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
+  return make_sw128_desc(base + kk * 2048, 16384, 1024);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, __nv_bfloat16* __restrict__ out,
+                       int64_t ld_out, float* __restrict__ lse, int S, int H, float scale, int* status,
+                       uint64_t timeout_ns) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kSmBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = bars + 3;
+  uint64_t* k_empty = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;
+  uint64_t* p_full = bars + 11;
+  uint64_t* o_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int qt = int(gridDim.x) - 1 - int(blockIdx.x);
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int q0 = qt * kBlk;
+  const int row0 = b * S;
+  const int nkb = qt + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(k_full + i, 1);
+      mbar_init(v_full + i, 1);
+      mbar_init(k_empty + i, 1);
+      mbar_init(v_empty + i, 1);
+      mbar_init(s_full + i, 1);
+      mbar_init(p_full + i, 4);
+    }
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tq);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = smem_u32(sm + kSmQ);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 32768);
+      tma_load_2d(sm + kSmQ, &tq, q_full, h * kD, row0 + q0);
+      tma_load_2d(sm + kSmQ + 16384, &tq, q_full, h * kD + 64, row0 + q0);
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(k_empty + st, ph ^ 1, timeout_ns, status, kTimeoutProducerEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(k_full + st, 32768);
+        uint8_t* kdst = sm + kSmK + st * 32768;
+        tma_load_2d(kdst, &tq, k_full + st, (H + h) * kD, row0 + j * kBlk);
+        tma_load_2d(kdst + 16384, &tq, k_full + st, (H + h) * kD + 64, row0 + j * kBlk);
+        if (!mbar_wait(v_empty + st, ph ^ 1, timeout_ns, status, kTimeoutProducerEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full + st, 32768);
+        uint8_t* vdst = sm + kSmV + st * 32768;
+        tma_load_2d(vdst, &tq, v_full + st, (2 * H + h) * kD, row0 + j * kBlk);
+        tma_load_2d(vdst + 16384, &tq, v_full + st, (2 * H + h) * kD + 64, row0 + j * kBlk);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      const uint32_t idesc_o = make_idesc_bf16(128, 128, 0, 1);
+      bool ok = mbar_wait(q_full, 0, timeout_ns, status, kTimeoutMmaFull, abort_flag);
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(p_full + (i & 1), (i >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) return false;
+        if (!mbar_wait(v_full + (i & 1), (i >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t vb = smem_u32(sm + kSmV + (i & 1) * 32768);
+        const uint32_t p_tmem = tmem + uint32_t((i & 1) * 128);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_tmem_a(tmem + 256, p_tmem + uint32_t(kk * 8), mnmajor_desc(vb, kk), idesc_o,
+                          (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(v_empty + (i & 1));
+        umma_commit(o_done);
+        return true;
+      };
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(k_full + st, (j >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = smem_u32(sm + kSmK + st * 32768);
+        const uint32_t d = tmem + uint32_t(st * 128);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(d, kmajor_desc(sQ, kk), kmajor_desc(kb, kk), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(k_empty + st);
+        umma_commit(s_full + st);
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok) issue_pv(nkb - 1);
+      // Drain: all MMAs (including the last PV) done before TMEM is freed.
+      mbar_wait(o_done, (nkb - 1) & 1, timeout_ns, status, kTimeoutDrain, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = uint32_t(q * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    float m_run = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      if (!mbar_wait(s_full + (j & 1), (j >> 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[128];
+      {
+        // All four 32-column loads in flight, one wait.
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        const uint32_t sb = tmem + lane_base + uint32_t((j & 1) * 128);
+        tmem_ld_32x32b_x32(sb, r0);
+        tmem_ld_32x32b_x32(sb + 32, r1);
+        tmem_ld_32x32b_x32(sb + 64, r2);
+        tmem_ld_32x32b_x32(sb + 96, r3);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          x[i] = __uint_as_float(r0[i]);
+          x[32 + i] = __uint_as_float(r1[i]);
+          x[64 + i] = __uint_as_float(r2[i]);
+          x[96 + i] = __uint_as_float(r3[i]);
+        }
+      }
+      const bool diag = j == nkb - 1;
+      // Eight independent max chains (no 128-long serial dependency).
+      float mxa[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mxa[a] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float v = x[c] * sl2;
+        if (diag && c > row) v = -INFINITY;
+        x[c] = v;
+        mxa[c & 7] = fmaxf(mxa[c & 7], v);
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+      if (mx > m_run + kRescale) {
+        if (j > 0) {
+          const float factor = exp2f(m_run - mx);
+          l *= factor;
+          // O holds PV up to block j-2 plus PV(j-1) in flight: wait for it, then rescale.
+          if (!mbar_wait(o_done, (j - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t r[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t addr = tmem + lane_base + uint32_t(256 + c * 32);
+            tmem_ld_32x32b_x32(addr, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+            tmem_st_32x32b_x32(addr, r);
+          }
+          tmem_wait_st();
+        }
+        m_run = mx;
+      }
+      float suma[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) suma[a] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float p = exp2f(x[c] - m_run);
+        x[c] = p;
+        suma[c & 7] += p;
+      }
+      const float sum = ((suma[0] + suma[1]) + (suma[2] + suma[3])) + ((suma[4] + suma[5]) + (suma[6] + suma[7]));
+      l += sum;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = pack2(x[half * 64 + 2 * i], x[half * 64 + 2 * i + 1]);
+        tmem_st_32x32b_x32(tmem + lane_base + uint32_t((j & 1) * 128 + half * 32), w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full + (j & 1));
+    }
+    if (ok && mbar_wait(o_done, (nkb - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const int qidx = q0 + row;
+      lse[int64_t(blockIdx.y) * S + qidx] = (m_run + log2f(l)) / kLog2e;
+      // Stage this warp's 32 rows (256 B each) through smem (the Q tile is dead).
+      uint8_t* stg = sm + kSmQ + q * 8192;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + uint32_t(256 + c * 32), r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 pk;
+          pk.x = pack2(__uint_as_float(r[8 * u + 0]) * inv, __uint_as_float(r[8 * u + 1]) * inv);
+          pk.y = pack2(__uint_as_float(r[8 * u + 2]) * inv, __uint_as_float(r[8 * u + 3]) * inv);
+          pk.z = pack2(__uint_as_float(r[8 * u + 4]) * inv, __uint_as_float(r[8 * u + 5]) * inv);
+          pk.w = pack2(__uint_as_float(r[8 * u + 6]) * inv, __uint_as_float(r[8 * u + 7]) * inv);
+          const int unit = c * 4 + u;  // 16 units of 16 B per row
+          *reinterpret_cast<uint4*>(stg + lane * 256 + ((unit ^ (lane & 7)) << 4)) = pk;
+        }
+      }
+      __syncwarp();
+      __nv_bfloat16* og = out + int64_t(row0 + q0 + q * 32) * ld_out + h * kD;
+#pragma unroll 4
+      for (int i = lane; i < 32 * 16; i += 32) {
+        const int r = i / 16, unit = i % 16;
+        *reinterpret_cast<uint4*>(og + int64_t(r) * ld_out + unit * 8) =
+            *reinterpret_cast<const uint4*>(stg + r * 256 + ((unit ^ (r & 7)) << 4));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================
+// Backward.  D = rowsum(dO * O) comes from a small pre-pass.  Two kernels, no
+// float atomics (deterministic):
+//   dK/dV: CTA per 128-key block; for each query block i >= the key block:
+//          S^T = K Q_i^T and dP^T = V dO_i^T into TMEM; the elementwise warps
+//          write P^T = exp2(S^T*scale*log2e - LSE_i*log2e) and
+//          dS^T = P^T (dP^T - D_i) back as packed BF16; then
+//          dV += P^T dO_i and dK += dS^T Q_i (A from TMEM; Q_i / dO_i reused as
+//          MN-major operands from the same 128-byte-swizzled smem tiles).
+//   dQ:    CTA per 128-query block; for each key block j <= the query block:
+//          S = Q K_j^T, dP = dO V_j^T; dS = P (dP - D); dQ += dS K_j.
+// ============================================================================
+constexpr int kBwdSmTotal = 6 * 32768 + 2048 + 256 + 1024;
+
+// cp.async.bulk (non-tensor) global -> shared, completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Elementwise pass over one 128-column score row pair held in TMEM:
+// reads S (cols s_col..+128) and dP (cols dp_col..+128), writes P (packed BF16)
+// over S's first 64 columns and dS over dP's first 64 columns.
+// column_mode: per-column LSE/D from smem (dK/dV kernel) or per-row values.
+template <bool kColumnStats>
+__device__ __forceinline__ void softmax_grad_row(uint32_t tmem, uint32_t lane_base, uint32_t s_col, uint32_t dp_col,
+                                                 float sl2, const float* lse_s, const float* d_s, float lse_row2,
+                                                 float d_row, int row, bool diag, bool write_p) {
+#pragma unroll 1
+  for (int quarter = 0; quarter < 4; ++quarter) {
+    uint32_t rs[32], rd[32];
+    tmem_ld_32x32b_x32(tmem + lane_base + s_col + quarter * 32, rs);
+    tmem_ld_32x32b_x32(tmem + lane_base + dp_col + quarter * 32, rd);
+    tmem_wait_ld();
+    uint32_t wp[16], wd[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      float pp[2], dd[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = quarter * 32 + i + e;
+        const float l2 = kColumnStats ? lse_s[c] : lse_row2;
+        const float dv = kColumnStats ? d_s[c] : d_row;
+        // dK/dV: rows are keys, columns queries -> masked when query < key.
+        // dQ:    rows are queries, columns keys -> masked when key > query.
+        const bool masked = diag && (kColumnStats ? (c < row) : (c > row));
+        const float p = masked ? 0.f : exp2f(__uint_as_float(rs[i + e]) * sl2 - l2);
+        pp[e] = p;
+        dd[e] = p * (__uint_as_float(rd[i + e]) - dv);
+      }
+      wp[i / 2] = pack2(pp[0], pp[1]);
+      wd[i / 2] = pack2(dd[0], dd[1]);
+    }
+    if (write_p) tmem_st_32x32b_x16(tmem + lane_base + s_col + quarter * 16, wp);
+    tmem_st_32x32b_x16(tmem + lane_base + dp_col + quarter * 16, wd);
+  }
+  tmem_wait_st();
+}
+
+// Write 32 rows x 128 columns (fp32 in TMEM, scaled) of this warp as BF16.
+__device__ __forceinline__ void store_tmem_rows(uint32_t tmem_row, float mul, uint8_t* stg, __nv_bfloat16* g,
+                                                int64_t ld, int lane) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tmem_row + c * 32, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      uint4 pk;
+      pk.x = pack2(__uint_as_float(r[8 * u + 0]) * mul, __uint_as_float(r[8 * u + 1]) * mul);
+      pk.y = pack2(__uint_as_float(r[8 * u + 2]) * mul, __uint_as_float(r[8 * u + 3]) * mul);
+      pk.z = pack2(__uint_as_float(r[8 * u + 4]) * mul, __uint_as_float(r[8 * u + 5]) * mul);
+      pk.w = pack2(__uint_as_float(r[8 * u + 6]) * mul, __uint_as_float(r[8 * u + 7]) * mul);
+      const int unit = c * 4 + u;
+      *reinterpret_cast<uint4*>(stg + lane * 256 + ((unit ^ (lane & 7)) << 4)) = pk;
+    }
+  }
+  __syncwarp();
+#pragma unroll 4
+  for (int i = lane; i < 32 * 16; i += 32) {
+    const int r = i / 16, unit = i % 16;
+    *reinterpret_cast<uint4*>(g + int64_t(r) * ld + unit * 8) =
+        *reinterpret_cast<const uint4*>(stg + r * 256 + ((unit ^ (r & 7)) << 4));
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                            const float* __restrict__ lse, const float* __restrict__ Dvec,
+                            __nv_bfloat16* __restrict__ dqkv, int64_t ld_dqkv, int S, int H, float scale,
+                            int* status, uint64_t timeout_ns) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // [K 32K][V 32K][Q st0 32K][Q st1 32K][dO st0 32K][dO st1 32K][LSE/D 2 x 1K][bars]
+  uint8_t* sK = sm;
+  uint8_t* sV = sm + 32768;
+  uint8_t* sQ = sm + 65536;
+  uint8_t* sO = sm + 65536 + 65536;
+  float* sStat = reinterpret_cast<float*>(sm + 6 * 32768);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 6 * 32768 + 2048);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int kb = blockIdx.x;  // small key blocks carry the most query blocks: run them first
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int row0 = b * S;
+  const int k0 = kb * kBlk;
+  const int nqb = S / kBlk;
+  const int nblk = nqb - kb;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(q_full + i, 1);
+      mbar_init(q_empty + i, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tdo);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 65536);
+      tma_load_2d(sK, &tq, kv_full, (H + h) * kD, row0 + k0);
+      tma_load_2d(sK + 16384, &tq, kv_full, (H + h) * kD + 64, row0 + k0);
+      tma_load_2d(sV, &tq, kv_full, (2 * H + h) * kD, row0 + k0);
+      tma_load_2d(sV + 16384, &tq, kv_full, (2 * H + h) * kD + 64, row0 + k0);
+      for (int t = 0; t < nblk; ++t) {
+        const int i = kb + t, st = t & 1;
+        if (!mbar_wait(q_empty + st, ((t >> 1) & 1) ^ 1, timeout_ns, status, kTimeoutProducerEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full + st, 65536 + 1024);
+        tma_load_2d(sQ + st * 32768, &tq, q_full + st, h * kD, row0 + i * kBlk);
+        tma_load_2d(sQ + st * 32768 + 16384, &tq, q_full + st, h * kD + 64, row0 + i * kBlk);
+        tma_load_2d(sO + st * 32768, &tdo, q_full + st, h * kD, row0 + i * kBlk);
+        tma_load_2d(sO + st * 32768 + 16384, &tdo, q_full + st, h * kD + 64, row0 + i * kBlk);
+        bulk_load(sStat + st * 256, lse + int64_t(blockIdx.y) * S + i * kBlk, 512, q_full + st);
+        bulk_load(sStat + st * 256 + 128, Dvec + int64_t(blockIdx.y) * S + i * kBlk, 512, q_full + st);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
+      const uint32_t idesc_tm = make_idesc_bf16(128, 128, 0, 1);
+      bool ok = mbar_wait(kv_full, 0, timeout_ns, status, kTimeoutMmaFull, abort_flag);
+      tc_fence_after();
+      const uint32_t kbase = smem_u32(sK), vbase = smem_u32(sV);
+      for (int t = 0; t < nblk && ok; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(q_full + st, (t >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qb = smem_u32(sQ + st * 32768), ob = smem_u32(sO + st * 32768);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_f16(tmem, kmajor_desc(kbase, kk), kmajor_desc(qb, kk), idesc_kk, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tmem + 128, kmajor_desc(vbase, kk), kmajor_desc(ob, kk), idesc_kk, kk > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, t & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_tmem_a(tmem + 256, tmem + uint32_t(kk * 8), mnmajor_desc(ob, kk), idesc_tm, (t > 0 || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_tmem_a(tmem + 384, tmem + 128 + uint32_t(kk * 8), mnmajor_desc(qb, kk), idesc_tm, (t > 0 || kk > 0));
+        umma_commit(q_empty + st);
+      }
+      umma_commit(done);
+      mbar_wait(done, 0, timeout_ns, status, kTimeoutDrain, nullptr);
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // key row within the block
+    const uint32_t lane_base = uint32_t(q * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    bool ok = true;
+    for (int t = 0; t < nblk; ++t) {
+      const int st = t & 1;
+      if (!mbar_wait(s_full, t & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
+      // q_full(t) has completed before the MMA warp issued S^T(t): the stats are in smem.
+      tc_fence_after();
+      float lse2[1];
+      (void)lse2;
+      const float* ls = sStat + st * 256;
+      const float* ds = sStat + st * 256 + 128;
+      // Per-column LSE in log2 units computed on the fly (ls[c] * log2e).
+      __shared__ float lse_l2[4][128];
+      // Each warp converts its own copy (no cross-warp sync needed).
+#pragma unroll
+      for (int c = lane; c < 128; c += 32) lse_l2[q][c] = ls[c] * kLog2e;
+      __syncwarp();
+      softmax_grad_row<true>(tmem, lane_base, 0, 128, sl2, lse_l2[q], ds, 0.f, 0.f, row, t == 0, true);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+      tc_fence_after();
+      uint8_t* stg = sQ + q * 8192;  // Q stage 0 is dead after the last MMA
+      __nv_bfloat16* dK = dqkv + int64_t(row0 + k0 + q * 32) * ld_dqkv + (H + h) * kD;
+      __nv_bfloat16* dV = dqkv + int64_t(row0 + k0 + q * 32) * ld_dqkv + (2 * H + h) * kD;
+      store_tmem_rows(tmem + lane_base + 256, 1.f, stg, dV, ld_dqkv, lane);
+      store_tmem_rows(tmem + lane_base + 384, scale, stg, dK, ld_dqkv, lane);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                          const float* __restrict__ lse, const float* __restrict__ Dvec,
+                          __nv_bfloat16* __restrict__ dqkv, int64_t ld_dqkv, int S, int H, float scale,
+                          int* status, uint64_t timeout_ns) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // [Q 32K][dO 32K][K st0 32K][K st1 32K][V st0 32K][V st1 32K][bars]
+  uint8_t* sQ = sm;
+  uint8_t* sO = sm + 32768;
+  uint8_t* sK = sm + 65536;
+  uint8_t* sV = sm + 65536 + 65536;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 6 * 32768 + 2048);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int qt = int(gridDim.x) - 1 - int(blockIdx.x);  // heavy first
+  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int row0 = b * S;
+  const int q0 = qt * kBlk;
+  const int nkb = qt + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(kv_full + i, 1);
+      mbar_init(kv_empty + i, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tdo);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 65536);
+      tma_load_2d(sQ, &tq, q_full, h * kD, row0 + q0);
+      tma_load_2d(sQ + 16384, &tq, q_full, h * kD + 64, row0 + q0);
+      tma_load_2d(sO, &tdo, q_full, h * kD, row0 + q0);
+      tma_load_2d(sO + 16384, &tdo, q_full, h * kD + 64, row0 + q0);
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_empty + st, ((j >> 1) & 1) ^ 1, timeout_ns, status, kTimeoutProducerEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(kv_full + st, 65536);
+        tma_load_2d(sK + st * 32768, &tq, kv_full + st, (H + h) * kD, row0 + j * kBlk);
+        tma_load_2d(sK + st * 32768 + 16384, &tq, kv_full + st, (H + h) * kD + 64, row0 + j * kBlk);
+        tma_load_2d(sV + st * 32768, &tq, kv_full + st, (2 * H + h) * kD, row0 + j * kBlk);
+        tma_load_2d(sV + st * 32768 + 16384, &tq, kv_full + st, (2 * H + h) * kD + 64, row0 + j * kBlk);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
+      const uint32_t idesc_tm = make_idesc_bf16(128, 128, 0, 1);
+      bool ok = mbar_wait(q_full, 0, timeout_ns, status, kTimeoutMmaFull, abort_flag);
+      tc_fence_after();
+      const uint32_t qbase = smem_u32(sQ), obase = smem_u32(sO);
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_full + st, (j >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t kbase = smem_u32(sK + st * 32768), vbase = smem_u32(sV + st * 32768);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_f16(tmem, kmajor_desc(qbase, kk), kmajor_desc(kbase, kk), idesc_kk, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tmem + 128, kmajor_desc(obase, kk), kmajor_desc(vbase, kk), idesc_kk, kk > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, j & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_tmem_a(tmem + 256, tmem + 128 + uint32_t(kk * 8), mnmajor_desc(kbase, kk), idesc_tm,
+                          (j > 0 || kk > 0));
+        umma_commit(kv_empty + st);
+      }
+      umma_commit(done);
+      mbar_wait(done, 0, timeout_ns, status, kTimeoutDrain, nullptr);
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = uint32_t(q * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    const float lse2 = lse[int64_t(blockIdx.y) * S + q0 + row] * kLog2e;
+    const float drow = Dvec[int64_t(blockIdx.y) * S + q0 + row];
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      if (!mbar_wait(s_full, j & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      softmax_grad_row<false>(tmem, lane_base, 0, 128, sl2, nullptr, nullptr, lse2, drow, row, j == nkb - 1, false);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+      tc_fence_after();
+      uint8_t* stg = sK + q * 8192;
+      __nv_bfloat16* dQ = dqkv + int64_t(row0 + q0 + q * 32) * ld_dqkv + h * kD;
+      store_tmem_rows(tmem + lane_base + 256, scale, stg, dQ, ld_dqkv, lane);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+}  // namespace
+
+int attention_fwd_tc(const void* qkv, int64_t ld_qkv, void* out, int64_t ld_out, float* lse, int B, int S,
+                     int H, float scale, int* status, uint64_t timeout_ns, cudaStream_t s) {
+  if (S % kBlk || ld_qkv % 8 || ld_out % 8 || (reinterpret_cast<uintptr_t>(qkv) & 15)) return -1;
+  CUtensorMap map;
+  if (!make_map(&map, qkv, uint64_t(3) * H * kD, uint64_t(B) * S, uint64_t(ld_qkv))) return -1;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmTotal);
+    configured[dev] = true;
+  }
+  dim3 grid(S / kBlk, B * H);
+  attn_fwd_tc_kernel<<<grid, kThreads, kSmTotal, s>>>(map, static_cast<__nv_bfloat16*>(out), ld_out, lse, S, H,
+                                                      scale, status, timeout_ns);
+  return int(cudaGetLastError());
+}
+
+int attention_bwd_tc(const void* qkv, int64_t ld_qkv, const void* dout, int64_t ld_dout, const float* lse,
+                     const float* Dvec, void* dqkv, int64_t ld_dqkv, int B, int S, int H, float scale, int* status,
+                     uint64_t timeout_ns, cudaStream_t s) {
+  if (S % kBlk || ld_qkv % 8 || ld_dout % 8 || ld_dqkv % 8) return -1;
+  CUtensorMap mq, mo;
+  if (!make_map(&mq, qkv, uint64_t(3) * H * kD, uint64_t(B) * S, uint64_t(ld_qkv))) return -1;
+  if (!make_map(&mo, dout, uint64_t(H) * kD, uint64_t(B) * S, uint64_t(ld_dout))) return -1;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
+    cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
+    configured[dev] = true;
+  }
+  dim3 grid(S / kBlk, B * H);
+  attn_bwd_dkdv_tc_kernel<<<grid, kThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
+                                                             ld_dqkv, S, H, scale, status, timeout_ns);
+  attn_bwd_dq_tc_kernel<<<grid, kThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
+                                                           ld_dqkv, S, H, scale, status, timeout_ns);
+  return int(cudaGetLastError());
+}
+
+}  // namespace kernels
+}  // namespace tn5b

@@ -171,24 +171,29 @@ void embed_bwd(const at::Tensor& tok, const at::Tensor& gr, at::Tensor& dE, int6
                   start, dE.size(0), ws.data_ptr<int>(), accumulate, cur()), "embed_bwd");
 }
 
-void attention_fwd(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B, int64_t S, int64_t H,
-                   double scale) {
+void attention_fwd_tc(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B, int64_t S, int64_t H,
+                      double scale, const at::Tensor& status, int64_t timeout_ns) {
   need(qkv, at::kBFloat16, "qkv", false); need(out, at::kBFloat16, "out", false); need(lse, at::kFloat, "lse");
   TORCH_CHECK(qkv.stride(1) == 1 && out.stride(1) == 1);
   TORCH_CHECK(qkv.size(0) == B * S && qkv.size(1) == 3 * H * 128 && out.size(1) == H * 128);
   const c10::cuda::CUDAGuard g(qkv.device());
-  ok(k::attention_fwd(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), lse.data_ptr<float>(),
-                      int(B), int(S), int(H), float(scale), cur()), "attention_fwd");
+  ok(k::attention_fwd_tc(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), lse.data_ptr<float>(),
+                         int(B), int(S), int(H), float(scale), status.data_ptr<int>(), uint64_t(timeout_ns), cur()),
+     "attention_fwd_tc");
 }
-void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
-                   at::Tensor& Dvec, at::Tensor& dqkv, int64_t B, int64_t S, int64_t H, double scale) {
+void attention_bwd_tc(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
+                      at::Tensor& Dvec, at::Tensor& dqkv, int64_t B, int64_t S, int64_t H, double scale,
+                      const at::Tensor& status, int64_t timeout_ns) {
   need(qkv, at::kBFloat16, "qkv", false); need(out, at::kBFloat16, "out", false);
   need(dout, at::kBFloat16, "dout", false); need(dqkv, at::kBFloat16, "dqkv", false);
   need(lse, at::kFloat, "lse"); need(Dvec, at::kFloat, "D");
+  TORCH_CHECK(qkv.stride(1) == 1 && dout.stride(1) == 1 && dqkv.stride(1) == 1 && out.stride(1) == 1);
   const c10::cuda::CUDAGuard g(qkv.device());
-  ok(k::attention_bwd(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), dout.data_ptr(),
-                      dout.stride(0), lse.data_ptr<float>(), Dvec.data_ptr<float>(), dqkv.data_ptr(),
-                      dqkv.stride(0), int(B), int(S), int(H), float(scale), cur()), "attention_bwd");
+  ok(k::attention_bwd_pre(out.data_ptr(), out.stride(0), dout.data_ptr(), dout.stride(0), Dvec.data_ptr<float>(),
+                          int(B), int(S), int(H), cur()), "attention_bwd_pre");
+  ok(k::attention_bwd_tc(qkv.data_ptr(), qkv.stride(0), dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(),
+                         Dvec.data_ptr<float>(), dqkv.data_ptr(), dqkv.stride(0), int(B), int(S), int(H), float(scale),
+                         status.data_ptr<int>(), uint64_t(timeout_ns), cur()), "attention_bwd_tc");
 }
 }  // namespace
 
@@ -215,6 +220,6 @@ void register_kernels(pybind11::module& m) {
   m.def("position_bwd", &position_bwd);
   m.def("embed_bwd_workspace", &embed_bwd_workspace);
   m.def("embed_bwd", &embed_bwd);
-  m.def("attention_fwd", &attention_fwd);
-  m.def("attention_bwd", &attention_bwd);
+  m.def("attention_fwd_tc", &attention_fwd_tc);
+  m.def("attention_bwd_tc", &attention_bwd_tc);
 }

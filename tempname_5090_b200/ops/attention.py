@@ -1,7 +1,9 @@
 """Causal attention over a fused QKV buffer [tokens, 3*heads*128] (per-token
 layout [3][heads][head_dim], TempName-5090 model.py:254); output
-[tokens, heads*128].  CUDA: hand-written sm_100a kernels (forward with saved
-LSE, deterministic two-kernel backward).  CPU: torch math reference.
+[tokens, heads*128].  CUDA: hand-written sm_100a tcgen05 kernels (TMA-fed,
+scores/probabilities/accumulators in tensor memory; forward saves the row
+LSE; the backward is two deterministic kernels, dK/dV per key block and dQ per
+query block).  CPU: torch math reference (test oracle).
 """
 from __future__ import annotations
 
@@ -10,7 +12,9 @@ import math
 import torch
 import torch.nn.functional as F
 
-from .._native import count_launch, lib
+from .._native import count_launch, lib, status_tensor
+
+TIMEOUT_NS = 10_000_000_000
 
 HEAD_DIM = 128
 
@@ -29,7 +33,7 @@ def forward(qkv: torch.Tensor, B: int, S: int, H: int, out: torch.Tensor | None 
             raise ValueError("the CUDA attention kernel is specialised for head_dim 128")
         out = torch.empty((B * S, H * d), dtype=torch.bfloat16, device=qkv.device) if out is None else out
         lse = torch.empty((B * H, S), dtype=torch.float32, device=qkv.device)
-        lib().attention_fwd(qkv, out, lse, B, S, H, scale)
+        lib().attention_fwd_tc(qkv, out, lse, B, S, H, scale, status_tensor(qkv.device), TIMEOUT_NS)
         count_launch()
         return out, lse
     q, k, v = _split(qkv, B, S, H, d)
@@ -51,7 +55,8 @@ def backward(qkv, out, dout, lse, B: int, S: int, H: int, dqkv: torch.Tensor | N
     if qkv.is_cuda:
         dqkv = torch.empty_like(qkv) if dqkv is None else dqkv
         Dvec = torch.empty((B * H, S), dtype=torch.float32, device=qkv.device)
-        lib().attention_bwd(qkv, out, dout, lse, Dvec, dqkv, B, S, H, scale)
+        lib().attention_bwd_tc(qkv, out, dout, lse, Dvec, dqkv, B, S, H, scale, status_tensor(qkv.device),
+                               TIMEOUT_NS)
         count_launch(3)
         return dqkv
     q, k, v = _split(qkv, B, S, H, d)

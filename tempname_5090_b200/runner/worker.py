@@ -175,6 +175,7 @@ def operators(config: dict, arm: str, rank: int, world: int, group) -> dict:
             bitwise = bool(torch.equal(sibling.forward(x, w), retained))
             require_all(bitwise, f"{role}: order-only sibling arm output differs", group)
             sibling.close()
+        diagnostic = arrival_diagnostic(op, x, w, retained, group) if arm == P.ARRIVAL else None
         seconds = _timed(lambda: op.forward(x, w), timing["operator_warmup"], timing["operator_iterations"], group)
         full = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
         gemm_only = _timed(lambda: G.matmul(x, w, out=full), 5, timing["operator_iterations"], group)
@@ -185,9 +186,35 @@ def operators(config: dict, arm: str, rank: int, world: int, group) -> dict:
                             correctness_passed=True, bf16_relative_l2=e_plain, codec_reference_relative_l2=e_codec,
                             order_bitwise_equal=bitwise, gemm_only_us=gemm_only * 1e6,
                             roofline_us=roof * 1e6, roofline_fraction=roof / seconds, peaks=peaks,
-                            execution=op.state()))
+                            arrival_diagnostic=diagnostic, execution=op.state()))
         op.close()
     return dict(operator_results=results)
+
+
+def arrival_diagnostic(op, x, w, expected, group, delay_ns: int = 20_000_000) -> dict:
+    """Artificial lane skew (never timed): rank 0 delays the flag of its first
+    lane-0 tile by a bounded 20 ms; each owner records per-tile completion
+    times of its arrival-first receiver.  Evidence of bypass = tiles of the
+    other lane, later in the consumption order, finished before the delayed tile.
+    Output must stay bitwise equal (arithmetic order never depends on arrival)."""
+    import torch
+    import torch.distributed as dist
+    from .validation import require_all
+    out, stamps, delayed = op.profile_call(x, w, delay_ns=delay_ns, delay_rank=0)
+    require_all(bool(torch.equal(out, expected)), "artificial lane skew changed the output", group)
+    result = dict(passed=True, artificial=True, delayed_rank=0, delay_ns=delay_ns, ordinary_speedup_claim=False)
+    if delayed is not None and delayed[0] == op.rank:
+        tile = delayed[1]
+        order = op.consumer_order.tolist()
+        pos = order.index(tile)
+        tiles_n = op.n // 256
+        lane_of = lambda t: ((t // tiles_n) * 128 // op.chunk_rows) % 2
+        overtakes = [t for t in order[pos + 1:] if lane_of(t) != lane_of(tile) and stamps[t] < stamps[tile]]
+        result.update(owner=True, delayed_tile=tile, later_other_lane_tiles_completed_before=overtakes,
+                      ready_bypass_observed=bool(overtakes))
+    else:
+        result.update(owner=False)
+    return result
 
 
 # ---------------------------------------------------------------------- train
