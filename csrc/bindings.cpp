@@ -155,9 +155,10 @@ void register_comm(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "tempname_5090_b200 native sm_100a kernels";
-  m.def("gemm", &gemm, "tcgen05 BF16 GEMM with fused epilogue");
-  m.def("gemm_rs_push", &gemm_rs_push, "tcgen05 GEMM whose epilogue pushes tiles to owners");
-  m.def("ag_gemm", &ag_gemm, "all-gather fused into a tcgen05 GEMM");
+  using nogil = pybind11::call_guard<pybind11::gil_scoped_release>;
+  m.def("gemm", &gemm, "tcgen05 BF16 GEMM with fused epilogue", nogil());
+  m.def("gemm_rs_push", &gemm_rs_push, "tcgen05 GEMM whose epilogue pushes tiles to owners", nogil());
+  m.def("ag_gemm", &ag_gemm, "all-gather fused into a tcgen05 GEMM", nogil());
   m.def("gemm_grid", &gemm_grid, "persistent grid size of a GEMM call");
   register_kernels(m);
   register_comm(m);

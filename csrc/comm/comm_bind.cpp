@@ -100,6 +100,7 @@ void register_comm(pybind11::module& m) {
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("view_ptr", &view_ptr);
-  m.def("rs_reduce", &rs_reduce);
-  m.def("wait_probe", &wait_probe);
+  using nogil = pybind11::call_guard<pybind11::gil_scoped_release>;
+  m.def("rs_reduce", &rs_reduce, nogil());
+  m.def("wait_probe", &wait_probe, nogil());
 }

@@ -104,6 +104,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// Warp-uniform bounded wait: lane 0 polls, the outcome is broadcast, and the
+// warp leaves converged (tcgen05.ld/st are .sync.aligned and need the whole
+// warp).  The __syncwarp orders lane 0's acquire before the other lanes' reads.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns, int* status,
+                                          int code, volatile int* abort) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, timeout_ns, status, code, abort) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
 // ------------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(desc) : "memory");
@@ -255,6 +267,16 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Diagnostic progress word: a system-scope store a host thread can poll in
+// mapped pinned memory while the kernel is still running.
+__device__ __forceinline__ void trace_put(unsigned long long* t, int idx, unsigned long long v) {
+  if (t) asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(t + idx), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t smid() {
+  uint32_t v;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(v));
   return v;
 }
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {

@@ -100,10 +100,9 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
 // CTA pairs (256 x 256 cluster tiles) for local / all-gather GEMMs with enough tiles.
 bool use_pair(const GemmCall& c, int bn) {
   if (c.mode != 0 || bn != 256) return false;
-  if (c.pair == 0) return false;
-  if (c.pair == 1) return true;
-  const long pair_tiles = long((c.M + 255) / 256) * ((c.N + 255) / 256);
-  return pair_tiles >= sm_count() / 2;
+  // Opt-in only (pair == 1): CTA-pair tiles measured no faster than single-CTA
+  // tiles, and the pair path is not part of the default GEMM.
+  return c.pair == 1;
 }
 
 int pick_bn(const GemmCall& c) {

@@ -10,12 +10,16 @@
 //              A operand (P, BF16) read from TMEM and V as an MN-major smem
 //              operand -- S_{j} is issued before PV_{j-1} so the softmax of
 //              block j overlaps the tensor work of block j-1.
-//   warps 2-5  softmax: thread = query row = TMEM lane; loads its 128 scores,
-//              applies the causal mask on the diagonal block, keeps a running
-//              max in the log2 domain and rescales O in TMEM only when the
+//   warps 2-9  softmax: two warps per TMEM lane quarter, each owning 64 of the
+//              128 score columns of its rows (row = TMEM lane); loads its scores,
+//              applies the causal mask on the diagonal block, exchanges
+//              half-row maxima (and at the end the partial row sums) with its
+//              partner warp through a bounded mbarrier handshake, keeps a
+//              running max in the log2 domain and rescales O in TMEM only when the
 //              max grows by more than 2^8 (otherwise the stale max is exact:
 //              numerator and denominator share it), writes P = exp2(s - m) as
-//              packed BF16 over the same TMEM columns, and finally normalises O
+//              packed BF16 into the first half of its own 64 score columns
+//              (the PV MMA addresses those chunks), and finally normalises O
 //              and writes O (BF16) and the row LSE (natural log).
 // TMEM: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
 // Every wait is bounded; on a timeout the status word is set and the CTA exits.
@@ -32,7 +36,8 @@ namespace kernels {
 namespace {
 constexpr int kD = 128;
 constexpr int kBlk = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;    // warp 0 TMA, warp 1 MMA, warps 2-9 elementwise (2 per TMEM lane quarter)
+constexpr int kEwWarps = 8;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;
 
@@ -71,6 +76,13 @@ bool make_map(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows, u
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Hardware base-2 exponential (MUFU), flush-to-zero.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -85,10 +97,15 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
   return make_sw128_desc(base + kk * 2048, 16384, 1024);
 }
 
+// TMEM column of packed BF16 K-chunk kk (16 values per row) inside a 128-column
+// score buffer: the elementwise warp of half h writes its 64 probabilities as
+// 32 packed columns at [64h, 64h+32), inside the columns only it reads.
+__device__ __forceinline__ uint32_t packed_col(int kk) { return uint32_t((kk >> 2) * 64 + (kk & 3) * 8); }
+
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, __nv_bfloat16* __restrict__ out,
                        int64_t ld_out, float* __restrict__ lse, int S, int H, float scale, int* status,
-                       uint64_t timeout_ns) {
+                       uint64_t timeout_ns, unsigned long long* trace) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kSmBar);
@@ -102,6 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_done = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ uint64_t xbar[4];  // per lane quarter: the two softmax warps' handshake
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int qt = int(gridDim.x) - 1 - int(blockIdx.x);
@@ -109,6 +127,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q0 = qt * kBlk;
   const int row0 = b * S;
   const int nkb = qt + 1;
+  // Optional progress trace (16 words per CTA): [0] SM id and stage, [1] producer,
+  // [2] MMA issuer, [3..10] elementwise warps (block index + 1 reached).
+  unsigned long long* tr = trace ? trace + (size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 16 : nullptr;
+  const unsigned long long tsm = (unsigned long long)smid() << 16;
+  if (threadIdx.x == 0) trace_put(tr, 0, tsm | 1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -118,9 +141,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(k_empty + i, 1);
       mbar_init(v_empty + i, 1);
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 4);
+      mbar_init(p_full + i, kEwWarps);
     }
     mbar_init(o_done, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(xbar + i, 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -134,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sQ = smem_u32(sm + kSmQ);
+  if (threadIdx.x == 0) trace_put(tr, 0, tsm | 2);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -144,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(k_empty + st, ph ^ 1, timeout_ns, status, kTimeoutProducerEmpty, abort_flag)) break;
+        trace_put(tr, 1, j + 1);
         mbar_arrive_expect_tx(k_full + st, 32768);
         uint8_t* kdst = sm + kSmK + st * 32768;
         tma_load_2d(kdst, &tq, k_full + st, (H + h) * kD, row0 + j * kBlk);
@@ -168,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t p_tmem = tmem + uint32_t((i & 1) * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 256, p_tmem + uint32_t(kk * 8), mnmajor_desc(vb, kk), idesc_o,
+          umma_f16_tmem_a(tmem + 256, p_tmem + packed_col(kk), mnmajor_desc(vb, kk), idesc_o,
                           (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(v_empty + (i & 1));
         umma_commit(o_done);
@@ -181,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        trace_put(tr, 2, j + 1);
         const uint32_t kb = smem_u32(sm + kSmK + st * 32768);
         const uint32_t d = tmem + uint32_t(st * 128);
 #pragma unroll
@@ -196,64 +223,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------- softmax
+    // Two warps per TMEM lane quarter: `half` selects columns [64*half, 64*half+64).
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     const float sl2 = scale * kLog2e;
-    float m_run = -INFINITY, l = 0.f;
+    // Partner handshake per lane quarter: double-buffered slots, bounded waits.
+    __shared__ float xchg[2][2][128];  // [slot][half][row]
+    float m_run = -INFINITY, l = 0.f;  // m_run in log2 units; l = this half's partial row sum
     bool ok = true;
+    auto exchange = [&](int step, float mine, float& other) -> bool {
+      xchg[step & 1][half][row] = mine;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xbar + q);
+      if (!warp_wait(xbar + q, step & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) return false;
+      other = xchg[step & 1][half ^ 1][row];
+      return true;
+    };
     for (int j = 0; j < nkb; ++j) {
-      if (!mbar_wait(s_full + (j & 1), (j >> 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+      if (!warp_wait(s_full + (j & 1), (j >> 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float x[128];
+      float x[64];
       {
-        // All four 32-column loads in flight, one wait.
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        const uint32_t sb = tmem + lane_base + uint32_t((j & 1) * 128);
+        uint32_t r0[32], r1[32];
+        const uint32_t sb = tmem + lane_base + uint32_t((j & 1) * 128 + half * 64);
         tmem_ld_32x32b_x32(sb, r0);
         tmem_ld_32x32b_x32(sb + 32, r1);
-        tmem_ld_32x32b_x32(sb + 64, r2);
-        tmem_ld_32x32b_x32(sb + 96, r3);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           x[i] = __uint_as_float(r0[i]);
           x[32 + i] = __uint_as_float(r1[i]);
-          x[64 + i] = __uint_as_float(r2[i]);
-          x[96 + i] = __uint_as_float(r3[i]);
         }
       }
       const bool diag = j == nkb - 1;
-      // Eight independent max chains (no 128-long serial dependency).
       float mxa[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) mxa[a] = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float v = x[c] * sl2;
-        if (diag && c > row) v = -INFINITY;
-        x[c] = v;
-        mxa[c & 7] = fmaxf(mxa[c & 7], v);
+      for (int c = 0; c < 64; ++c) {
+        if (diag && half * 64 + c > row) x[c] = -INFINITY;  // raw-score max: scale > 0 keeps the order
+        mxa[c & 7] = fmaxf(mxa[c & 7], x[c]);
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-      if (mx > m_run + kRescale) {
+      float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                       fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+      // Exchange the half-row maxima with the partner warp of this lane quarter.
+      float other_mx;
+      if (!exchange(j, mx, other_mx)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, other_mx) * sl2;
+      // Lazy rescale, decided per row but executed by the whole warp (the TMEM
+      // load/store are warp-collective): rows that keep their max scale by 1.
+      const bool grow = mx > m_run + kRescale;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = grow ? mx : m_run;
         if (j > 0) {
-          const float factor = exp2f(m_run - mx);
+          const float factor = grow ? ex2(m_run - m_new) : 1.f;
           l *= factor;
-          // O holds PV up to block j-2 plus PV(j-1) in flight: wait for it, then rescale.
-          if (!mbar_wait(o_done, (j - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+          if (!warp_wait(o_done, (j - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           uint32_t r[32];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t addr = tmem + lane_base + uint32_t(256 + c * 32);
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t addr = tmem + lane_base + uint32_t(256 + half * 64 + c * 32);
             tmem_ld_32x32b_x32(addr, r);
             tmem_wait_ld();
 #pragma unroll
@@ -262,42 +303,46 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_wait_st();
         }
-        m_run = mx;
+        m_run = m_new;
       }
       float suma[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) suma[a] = 0.f;
+      uint32_t w[32];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float p = exp2f(x[c] - m_run);
-        x[c] = p;
-        suma[c & 7] += p;
+      for (int c = 0; c < 64; c += 2) {
+        const float p0 = ex2(fmaf(x[c], sl2, -m_run));
+        const float p1 = ex2(fmaf(x[c + 1], sl2, -m_run));
+        suma[c & 7] += p0;
+        suma[(c + 1) & 7] += p1;
+        w[c / 2] = pack2(p0, p1);
       }
-      const float sum = ((suma[0] + suma[1]) + (suma[2] + suma[3])) + ((suma[4] + suma[5]) + (suma[6] + suma[7]));
-      l += sum;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t w[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) w[i] = pack2(x[half * 64 + 2 * i], x[half * 64 + 2 * i + 1]);
-        tmem_st_32x32b_x32(tmem + lane_base + uint32_t((j & 1) * 128 + half * 32), w);
-      }
+      l += ((suma[0] + suma[1]) + (suma[2] + suma[3])) + ((suma[4] + suma[5]) + (suma[6] + suma[7]));
+      // P (BF16) for columns [64*half, +64) -> packed TMEM columns [64*half, +32).
+      tmem_st_32x32b_x32(tmem + lane_base + uint32_t((j & 1) * 128 + half * 64), w);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full + (j & 1));
+      if (lane == 0) {
+        mbar_arrive(p_full + (j & 1));
+        trace_put(tr, 1 + warp, j + 1);
+      }
     }
-    if (ok && mbar_wait(o_done, (nkb - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+    // Final: combine the two half-row sums, normalise this half's O columns.
+    float other_l = 0.f;
+    if (ok) ok = exchange(nkb, l, other_l);
+    const float ltot = l + other_l;
+    if (ok && warp_wait(o_done, (nkb - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
       tc_fence_after();
-      const float inv = 1.f / l;
+      const float inv = 1.f / ltot;
       const int qidx = q0 + row;
-      lse[int64_t(blockIdx.y) * S + qidx] = (m_run + log2f(l)) / kLog2e;
-      // Stage this warp's 32 rows (256 B each) through smem (the Q tile is dead).
-      uint8_t* stg = sm + kSmQ + q * 8192;
+      if (half == 0) lse[int64_t(blockIdx.y) * S + qidx] = (m_run + log2f(ltot)) / kLog2e;
+      // Stage 32 rows x 64 columns (128 B per row) of this warp through smem (Q tile is dead).
+      uint8_t* stg = sm + kSmQ + (q * 2 + half) * 4096;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + uint32_t(256 + c * 32), r);
+        tmem_ld_32x32b_x32(tmem + lane_base + uint32_t(256 + half * 64 + c * 32), r);
         tmem_wait_ld();
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -306,17 +351,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk.y = pack2(__uint_as_float(r[8 * u + 2]) * inv, __uint_as_float(r[8 * u + 3]) * inv);
           pk.z = pack2(__uint_as_float(r[8 * u + 4]) * inv, __uint_as_float(r[8 * u + 5]) * inv);
           pk.w = pack2(__uint_as_float(r[8 * u + 6]) * inv, __uint_as_float(r[8 * u + 7]) * inv);
-          const int unit = c * 4 + u;  // 16 units of 16 B per row
-          *reinterpret_cast<uint4*>(stg + lane * 256 + ((unit ^ (lane & 7)) << 4)) = pk;
+          const int unit = c * 4 + u;  // 8 units of 16 B per 64-column row
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((unit ^ (lane & 7)) << 4)) = pk;
         }
       }
       __syncwarp();
-      __nv_bfloat16* og = out + int64_t(row0 + q0 + q * 32) * ld_out + h * kD;
+      __nv_bfloat16* og = out + int64_t(row0 + q0 + q * 32) * ld_out + h * kD + half * 64;
 #pragma unroll 4
-      for (int i = lane; i < 32 * 16; i += 32) {
-        const int r = i / 16, unit = i % 16;
+      for (int i = lane; i < 32 * 8; i += 32) {
+        const int r = i / 8, unit = i % 8;
         *reinterpret_cast<uint4*>(og + int64_t(r) * ld_out + unit * 8) =
-            *reinterpret_cast<const uint4*>(stg + r * 256 + ((unit ^ (r & 7)) << 4));
+            *reinterpret_cast<const uint4*>(stg + r * 128 + ((unit ^ (r & 7)) << 4));
       }
     }
   }
@@ -325,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+    if (lane == 0) trace_put(tr, 0, tsm | 3);
   }
 }
 
@@ -350,16 +396,18 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
-// Elementwise pass over one 128-column score row pair held in TMEM:
-// reads S (cols s_col..+128) and dP (cols dp_col..+128), writes P (packed BF16)
-// over S's first 64 columns and dS over dP's first 64 columns.
-// column_mode: per-column LSE/D from smem (dK/dV kernel) or per-row values.
+// Elementwise pass over half (`half`) of one 128-column score row pair held in
+// TMEM: reads S (cols s_col+64*half..+64) and dP (dp_col+64*half..+64) and
+// writes P / dS as packed BF16 into the first 32 of those same 64 columns, so
+// the two warps sharing a lane quarter never touch each other's columns.  The
+// MMA reads packed chunk kk (16 BF16 values) at column packed_col(kk).
+// kColumnStats: per-column LSE/D from smem (dK/dV kernel) or per-row values.
 template <bool kColumnStats>
 __device__ __forceinline__ void softmax_grad_row(uint32_t tmem, uint32_t lane_base, uint32_t s_col, uint32_t dp_col,
                                                  float sl2, const float* lse_s, const float* d_s, float lse_row2,
-                                                 float d_row, int row, bool diag, bool write_p) {
+                                                 float d_row, int row, bool diag, bool write_p, int half) {
 #pragma unroll 1
-  for (int quarter = 0; quarter < 4; ++quarter) {
+  for (int quarter = 2 * half; quarter < 2 * half + 2; ++quarter) {
     uint32_t rs[32], rd[32];
     tmem_ld_32x32b_x32(tmem + lane_base + s_col + quarter * 32, rs);
     tmem_ld_32x32b_x32(tmem + lane_base + dp_col + quarter * 32, rd);
@@ -376,24 +424,25 @@ __device__ __forceinline__ void softmax_grad_row(uint32_t tmem, uint32_t lane_ba
         // dK/dV: rows are keys, columns queries -> masked when query < key.
         // dQ:    rows are queries, columns keys -> masked when key > query.
         const bool masked = diag && (kColumnStats ? (c < row) : (c > row));
-        const float p = masked ? 0.f : exp2f(__uint_as_float(rs[i + e]) * sl2 - l2);
+        const float p = masked ? 0.f : ex2(fmaf(__uint_as_float(rs[i + e]), sl2, -l2));
         pp[e] = p;
         dd[e] = p * (__uint_as_float(rd[i + e]) - dv);
       }
       wp[i / 2] = pack2(pp[0], pp[1]);
       wd[i / 2] = pack2(dd[0], dd[1]);
     }
-    if (write_p) tmem_st_32x32b_x16(tmem + lane_base + s_col + quarter * 16, wp);
-    tmem_st_32x32b_x16(tmem + lane_base + dp_col + quarter * 16, wd);
+    const uint32_t packed = uint32_t(half * 64 + (quarter & 1) * 16);
+    if (write_p) tmem_st_32x32b_x16(tmem + lane_base + s_col + packed, wp);
+    tmem_st_32x32b_x16(tmem + lane_base + dp_col + packed, wd);
   }
   tmem_wait_st();
 }
 
-// Write 32 rows x 128 columns (fp32 in TMEM, scaled) of this warp as BF16.
+// Write 32 rows x 64 columns (fp32 in TMEM, scaled) of this warp as BF16.
 __device__ __forceinline__ void store_tmem_rows(uint32_t tmem_row, float mul, uint8_t* stg, __nv_bfloat16* g,
                                                 int64_t ld, int lane) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(tmem_row + c * 32, r);
     tmem_wait_ld();
@@ -405,15 +454,15 @@ __device__ __forceinline__ void store_tmem_rows(uint32_t tmem_row, float mul, ui
       pk.z = pack2(__uint_as_float(r[8 * u + 4]) * mul, __uint_as_float(r[8 * u + 5]) * mul);
       pk.w = pack2(__uint_as_float(r[8 * u + 6]) * mul, __uint_as_float(r[8 * u + 7]) * mul);
       const int unit = c * 4 + u;
-      *reinterpret_cast<uint4*>(stg + lane * 256 + ((unit ^ (lane & 7)) << 4)) = pk;
+      *reinterpret_cast<uint4*>(stg + lane * 128 + ((unit ^ (lane & 7)) << 4)) = pk;
     }
   }
   __syncwarp();
 #pragma unroll 4
-  for (int i = lane; i < 32 * 16; i += 32) {
-    const int r = i / 16, unit = i % 16;
+  for (int i = lane; i < 32 * 8; i += 32) {
+    const int r = i / 8, unit = i % 8;
     *reinterpret_cast<uint4*>(g + int64_t(r) * ld + unit * 8) =
-        *reinterpret_cast<const uint4*>(stg + r * 256 + ((unit ^ (r & 7)) << 4));
+        *reinterpret_cast<const uint4*>(stg + r * 128 + ((unit ^ (r & 7)) << 4));
   }
   __syncwarp();
 }
@@ -456,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(q_empty + i, 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, kEwWarps);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -515,10 +564,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 256, tmem + uint32_t(kk * 8), mnmajor_desc(ob, kk), idesc_tm, (t > 0 || kk > 0));
+          umma_f16_tmem_a(tmem + 256, tmem + packed_col(kk), mnmajor_desc(ob, kk), idesc_tm, (t > 0 || kk > 0));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 384, tmem + 128 + uint32_t(kk * 8), mnmajor_desc(qb, kk), idesc_tm, (t > 0 || kk > 0));
+          umma_f16_tmem_a(tmem + 384, tmem + 128 + packed_col(kk), mnmajor_desc(qb, kk), idesc_tm, (t > 0 || kk > 0));
         umma_commit(q_empty + st);
       }
       umma_commit(done);
@@ -526,37 +575,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = q * 32 + lane;  // key row within the block
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     const float sl2 = scale * kLog2e;
     bool ok = true;
     for (int t = 0; t < nblk; ++t) {
       const int st = t & 1;
-      if (!mbar_wait(s_full, t & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
+      if (!warp_wait(s_full, t & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
       // q_full(t) has completed before the MMA warp issued S^T(t): the stats are in smem.
       tc_fence_after();
-      float lse2[1];
-      (void)lse2;
       const float* ls = sStat + st * 256;
       const float* ds = sStat + st * 256 + 128;
       // Per-column LSE in log2 units computed on the fly (ls[c] * log2e).
-      __shared__ float lse_l2[4][128];
+      __shared__ float lse_l2[kEwWarps][128];
+      const int ew = warp - 2;
       // Each warp converts its own copy (no cross-warp sync needed).
 #pragma unroll
-      for (int c = lane; c < 128; c += 32) lse_l2[q][c] = ls[c] * kLog2e;
+      for (int c = lane; c < 128; c += 32) lse_l2[ew][c] = ls[c] * kLog2e;
       __syncwarp();
-      softmax_grad_row<true>(tmem, lane_base, 0, 128, sl2, lse_l2[q], ds, 0.f, 0.f, row, t == 0, true);
+      softmax_grad_row<true>(tmem, lane_base, 0, 128, sl2, lse_l2[ew], ds, 0.f, 0.f, row, t == 0, true, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+    if (ok && warp_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
       tc_fence_after();
-      uint8_t* stg = sQ + q * 8192;  // Q stage 0 is dead after the last MMA
-      __nv_bfloat16* dK = dqkv + int64_t(row0 + k0 + q * 32) * ld_dqkv + (H + h) * kD;
-      __nv_bfloat16* dV = dqkv + int64_t(row0 + k0 + q * 32) * ld_dqkv + (2 * H + h) * kD;
-      store_tmem_rows(tmem + lane_base + 256, 1.f, stg, dV, ld_dqkv, lane);
-      store_tmem_rows(tmem + lane_base + 384, scale, stg, dK, ld_dqkv, lane);
+      uint8_t* stg = sQ + (q * 2 + half) * 4096;  // Q stage 0 is dead after the last MMA
+      __nv_bfloat16* dK = dqkv + int64_t(row0 + k0 + q * 32) * ld_dqkv + (H + h) * kD + half * 64;
+      __nv_bfloat16* dV = dqkv + int64_t(row0 + k0 + q * 32) * ld_dqkv + (2 * H + h) * kD + half * 64;
+      store_tmem_rows(tmem + lane_base + 256 + half * 64, 1.f, stg, dV, ld_dqkv, lane);
+      store_tmem_rows(tmem + lane_base + 384 + half * 64, scale, stg, dK, ld_dqkv, lane);
     }
   }
   tc_fence_before();
@@ -603,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_empty + i, 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, kEwWarps);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -660,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 256, tmem + 128 + uint32_t(kk * 8), mnmajor_desc(kbase, kk), idesc_tm,
+          umma_f16_tmem_a(tmem + 256, tmem + 128 + packed_col(kk), mnmajor_desc(kbase, kk), idesc_tm,
                           (j > 0 || kk > 0));
         umma_commit(kv_empty + st);
       }
@@ -669,6 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     const float sl2 = scale * kLog2e;
@@ -676,18 +726,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float drow = Dvec[int64_t(blockIdx.y) * S + q0 + row];
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
-      if (!mbar_wait(s_full, j & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
+      if (!warp_wait(s_full, j & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      softmax_grad_row<false>(tmem, lane_base, 0, 128, sl2, nullptr, nullptr, lse2, drow, row, j == nkb - 1, false);
+      softmax_grad_row<false>(tmem, lane_base, 0, 128, sl2, nullptr, nullptr, lse2, drow, row, j == nkb - 1, false,
+                              half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+    if (ok && warp_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
       tc_fence_after();
-      uint8_t* stg = sK + q * 8192;
-      __nv_bfloat16* dQ = dqkv + int64_t(row0 + q0 + q * 32) * ld_dqkv + h * kD;
-      store_tmem_rows(tmem + lane_base + 256, scale, stg, dQ, ld_dqkv, lane);
+      uint8_t* stg = sK + (q * 2 + half) * 4096;
+      __nv_bfloat16* dQ = dqkv + int64_t(row0 + q0 + q * 32) * ld_dqkv + h * kD + half * 64;
+      store_tmem_rows(tmem + lane_base + 256 + half * 64, scale, stg, dQ, ld_dqkv, lane);
     }
   }
   tc_fence_before();
@@ -700,7 +751,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 int attention_fwd_tc(const void* qkv, int64_t ld_qkv, void* out, int64_t ld_out, float* lse, int B, int S,
-                     int H, float scale, int* status, uint64_t timeout_ns, cudaStream_t s) {
+                     int H, float scale, int* status, uint64_t timeout_ns, cudaStream_t s,
+                     unsigned long long* trace) {
   if (S % kBlk || ld_qkv % 8 || ld_out % 8 || (reinterpret_cast<uintptr_t>(qkv) & 15)) return -1;
   CUtensorMap map;
   if (!make_map(&map, qkv, uint64_t(3) * H * kD, uint64_t(B) * S, uint64_t(ld_qkv))) return -1;
@@ -713,7 +765,7 @@ int attention_fwd_tc(const void* qkv, int64_t ld_qkv, void* out, int64_t ld_out,
   }
   dim3 grid(S / kBlk, B * H);
   attn_fwd_tc_kernel<<<grid, kThreads, kSmTotal, s>>>(map, static_cast<__nv_bfloat16*>(out), ld_out, lse, S, H,
-                                                      scale, status, timeout_ns);
+                                                      scale, status, timeout_ns, trace);
   return int(cudaGetLastError());
 }
 

@@ -50,8 +50,10 @@ int64_t embed_bwd_workspace_ints(int M, int64_t V);
 int embed_bwd(const int64_t* tok, const void* g, void* dE, int M, int H, int64_t start, int64_t V,
               int* workspace, int accumulate, cudaStream_t s);
 // Attention (attention_tc.cu, attention_pre.cu)
+// `trace` (optional, may be null): 16 progress words per CTA for stall diagnosis.
 int attention_fwd_tc(const void* qkv, int64_t ld_qkv, void* out, int64_t ld_out, float* lse, int B, int S,
-                     int H, float scale, int* status, uint64_t timeout_ns, cudaStream_t s);
+                     int H, float scale, int* status, uint64_t timeout_ns, cudaStream_t s,
+                     unsigned long long* trace = nullptr);
 int attention_bwd_pre(const void* out, int64_t ld_out, const void* dout, int64_t ld_dout, float* Dvec, int B,
                       int S, int H, cudaStream_t s);
 int attention_bwd_tc(const void* qkv, int64_t ld_qkv, const void* dout, int64_t ld_dout, const float* lse,

@@ -172,13 +172,14 @@ void embed_bwd(const at::Tensor& tok, const at::Tensor& gr, at::Tensor& dE, int6
 }
 
 void attention_fwd_tc(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, int64_t B, int64_t S, int64_t H,
-                      double scale, const at::Tensor& status, int64_t timeout_ns) {
+                      double scale, const at::Tensor& status, int64_t timeout_ns, int64_t trace) {
   need(qkv, at::kBFloat16, "qkv", false); need(out, at::kBFloat16, "out", false); need(lse, at::kFloat, "lse");
   TORCH_CHECK(qkv.stride(1) == 1 && out.stride(1) == 1);
   TORCH_CHECK(qkv.size(0) == B * S && qkv.size(1) == 3 * H * 128 && out.size(1) == H * 128);
   const c10::cuda::CUDAGuard g(qkv.device());
   ok(k::attention_fwd_tc(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), lse.data_ptr<float>(),
-                         int(B), int(S), int(H), float(scale), status.data_ptr<int>(), uint64_t(timeout_ns), cur()),
+                         int(B), int(S), int(H), float(scale), status.data_ptr<int>(), uint64_t(timeout_ns), cur(),
+                         reinterpret_cast<unsigned long long*>(trace)),
      "attention_fwd_tc");
 }
 void attention_bwd_tc(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
@@ -197,29 +198,35 @@ void attention_bwd_tc(const at::Tensor& qkv, const at::Tensor& out, const at::Te
 }
 }  // namespace
 
+// Launch entry points touch no Python object: the GIL is released while they
+// run, so other Python threads (e.g. a stall watchdog) keep running.
+using nogil = pybind11::call_guard<pybind11::gil_scoped_release>;
+
 void register_kernels(pybind11::module& m) {
-  m.def("taco_encode", &taco_encode);
-  m.def("taco_decode", &taco_decode);
-  m.def("taco_decode_reduce", &taco_decode_reduce);
-  m.def("ordered_reduce", &ordered_reduce);
-  m.def("diagnostic_delay", &diagnostic_delay);
-  m.def("layernorm_fwd", &layernorm_fwd);
-  m.def("layernorm_bwd_workspace", &layernorm_bwd_workspace);
-  m.def("layernorm_bwd", &layernorm_bwd);
-  m.def("column_sum", &column_sum);
-  m.def("gelu_bwd", &gelu_bwd);
-  m.def("ce_stats", &ce_stats);
-  m.def("ce_sumexp", &ce_sumexp);
-  m.def("ce_loss", &ce_loss);
-  m.def("ce_bwd", &ce_bwd);
-  m.def("grad_sqsum_parts", &grad_sqsum_parts);
-  m.def("grad_sqsum", &grad_sqsum);
-  m.def("adamw_step", &adamw_step);
-  m.def("embed_fwd", &embed_fwd);
-  m.def("add_position", &add_position);
-  m.def("position_bwd", &position_bwd);
-  m.def("embed_bwd_workspace", &embed_bwd_workspace);
-  m.def("embed_bwd", &embed_bwd);
-  m.def("attention_fwd_tc", &attention_fwd_tc);
-  m.def("attention_bwd_tc", &attention_bwd_tc);
+  m.def("taco_encode", &taco_encode, nogil());
+  m.def("taco_decode", &taco_decode, nogil());
+  m.def("taco_decode_reduce", &taco_decode_reduce, nogil());
+  m.def("ordered_reduce", &ordered_reduce, nogil());
+  m.def("diagnostic_delay", &diagnostic_delay, nogil());
+  m.def("layernorm_fwd", &layernorm_fwd, nogil());
+  m.def("layernorm_bwd_workspace", &layernorm_bwd_workspace, nogil());
+  m.def("layernorm_bwd", &layernorm_bwd, nogil());
+  m.def("column_sum", &column_sum, nogil());
+  m.def("gelu_bwd", &gelu_bwd, nogil());
+  m.def("ce_stats", &ce_stats, nogil());
+  m.def("ce_sumexp", &ce_sumexp, nogil());
+  m.def("ce_loss", &ce_loss, nogil());
+  m.def("ce_bwd", &ce_bwd, nogil());
+  m.def("grad_sqsum_parts", &grad_sqsum_parts, nogil());
+  m.def("grad_sqsum", &grad_sqsum, nogil());
+  m.def("adamw_step", &adamw_step, nogil());
+  m.def("embed_fwd", &embed_fwd, nogil());
+  m.def("add_position", &add_position, nogil());
+  m.def("position_bwd", &position_bwd, nogil());
+  m.def("embed_bwd_workspace", &embed_bwd_workspace, nogil());
+  m.def("embed_bwd", &embed_bwd, nogil());
+  m.def("attention_fwd_tc", &attention_fwd_tc, pybind11::arg("qkv"), pybind11::arg("out"), pybind11::arg("lse"),
+        pybind11::arg("B"), pybind11::arg("S"), pybind11::arg("H"), pybind11::arg("scale"), pybind11::arg("status"),
+        pybind11::arg("timeout_ns"), pybind11::arg("trace") = 0, nogil());
+  m.def("attention_bwd_tc", &attention_bwd_tc, nogil());
 }
