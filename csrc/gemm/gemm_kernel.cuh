@@ -238,7 +238,7 @@ __device__ __forceinline__ uint32_t code(float x, float quant) {
 // PAIR: a cluster of two CTAs computes one 256 x BN tile with
 // tcgen05.mma.cta_group::2 issued by the leader (cluster rank 0).  Each CTA
 // TMA-loads its own 128 rows of A and its own BN/2 rows of B from this GPU's
-// memory (no multicast); both CTAs' loads complete on the leader's "full"
+// memory only; both CTAs' loads complete on the leader's "full"
 // barrier, the leader's commits arrive on both CTAs' "empty" / "tmem full"
 // barriers, and both CTAs' epilogues release the accumulator on the leader's
 // "tmem empty" barrier.  Each CTA's TMEM holds its 128 rows x BN fp32.

@@ -34,17 +34,17 @@ def _run(case, world, timeout=300):
     assert proc.returncode == 0 and f"CASE-OK {case}" in proc.stdout, proc.stdout[-3000:] + proc.stderr[-5000:]
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_gemm_rs_all_arms(world):
     _run("gemm_rs", world)
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_ag_gemm(world):
     _run("ag_gemm", world)
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_model_matches_single_rank(world):
     _run("model", world)
 
