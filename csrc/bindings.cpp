@@ -63,8 +63,13 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
   c.max_ctas = int(max_ctas);
   c.pair = int(pair);
   if (group_m > 0) c.group_m = int(group_m);
-  if (debug) c.debug = reinterpret_cast<unsigned long long*>(debug->data_ptr<int64_t>());
   c.status = status_ptr(status);
+  if (debug) {
+    check_cuda(*debug, "debug");
+    TORCH_CHECK(debug->scalar_type() == at::kLong && debug->numel() >= 8 * int64_t(tn5b::gemm::grid_ctas(c)),
+                "debug must be int64 with 8 words per CTA");
+    c.debug = reinterpret_cast<unsigned long long*>(debug->data_ptr<int64_t>());
+  }
   raise_if(tn5b::gemm::run(c, stream()), "gemm");
 }
 

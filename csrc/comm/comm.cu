@@ -151,25 +151,40 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
     }
     return;
   }
-  // Arrival-first: lane = parity of the tile's block-within-destination.
+  // Arrival-first: lane = parity of the tile's block-within-destination.  All
+  // threads scan the lane's unclaimed tiles in parallel; the earliest ready one
+  // (in the consumer order) is claimed with a CAS tagged with the epoch.
   const int lane_id = blockIdx.x & 1;
   const uint64_t start = globaltimer_ns();
+  __shared__ int s_best;
   for (;;) {
+    if (threadIdx.x == 0) s_best = 0x7fffffff;
+    __syncthreads();
+    int best = 0x7fffffff, open = 0;
+    for (int i = threadIdx.x; i < tiles; i += kThreads) {
+      const int tile = c.tile_order ? c.tile_order[i] : i;
+      const int blk = (tile / tiles_n) * 128 / c.chunk_rows;
+      if ((blk & 1) != lane_id) continue;
+      const int old = *reinterpret_cast<volatile int*>(c.claims + tile);
+      if (int32_t(uint32_t(old) - c.epoch) >= 0) continue;  // already taken this epoch
+      open = 1;
+      if (best == 0x7fffffff && tile_ready(c, tile, tiles)) best = i;
+    }
+    if (best != 0x7fffffff) atomicMin(&s_best, best);
+    const int any_open = __syncthreads_or(open);
     if (threadIdx.x == 0) {
-      int found = -1, remaining = 0;
-      for (int i = 0; i < tiles; ++i) {
-        const int tile = c.tile_order ? c.tile_order[i] : i;
-        const int blk = (tile / tiles_n) * 128 / c.chunk_rows;
-        if ((blk & 1) != lane_id) continue;
+      int found = -1;
+      if (!any_open) {
+        found = -2;  // lane drained
+      } else if (s_best != 0x7fffffff) {
+        const int tile = c.tile_order ? c.tile_order[s_best] : s_best;
         const int old = *reinterpret_cast<volatile int*>(c.claims + tile);
-        if (int32_t(uint32_t(old) - c.epoch) >= 0) continue;  // already taken this epoch
-        ++remaining;
-        if (tile_ready(c, tile, tiles) && atomicCAS(c.claims + tile, old, int(c.epoch)) == old) {
+        // tile_ready is this thread's own acquire of the flags (monotonic epochs:
+        // ready for the scanning thread implies ready here).
+        if (int32_t(uint32_t(old) - c.epoch) < 0 && tile_ready(c, tile, tiles) &&
+            atomicCAS(c.claims + tile, old, int(c.epoch)) == old)
           found = tile;
-          break;
-        }
       }
-      if (found < 0 && remaining == 0) found = -2;  // lane drained
       if (found == -1 && globaltimer_ns() - start > c.timeout_ns) {
         record_status(c.status, kTimeoutPeerFlag);
         found = -2;
@@ -178,10 +193,9 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
     }
     __syncthreads();
     const int tile = s_tile;
-    __syncthreads();
     if (tile == -2) return;
     if (tile == -1) {
-      __nanosleep(200);
+      if (s_best == 0x7fffffff) __nanosleep(256);
       continue;
     }
     reduce_tile(c, tile, tiles_n);

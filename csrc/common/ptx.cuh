@@ -87,15 +87,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded parity wait.  Returns false (and records `code`) once `deadline_ns`
 // of %globaltimer has passed, or immediately when *abort is set by another role.
+// The deadline clock starts after the first 64 polls, so a wait that ends
+// quickly never reads the timer on its critical path.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
                                           int* status, int code, volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
+  uint64_t start = 0;
+  for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63) == 0) {
+    if ((it & 63) == 63) {
       if (abort && *abort) return false;
-      if (globaltimer_ns() - start > timeout_ns) {
+      const uint64_t now = globaltimer_ns();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > timeout_ns) {
         record_status(status, code);
         if (abort) *abort = 1;
         return false;
@@ -292,13 +296,15 @@ __device__ __forceinline__ void fence_acq_rel_sys() {
 // compared as signed differences so they survive wrap).
 __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t target,
                                               uint64_t timeout_ns, int* status, int code) {
-  if (int32_t(ld_acquire_sys(flag) - target) >= 0) return true;
-  const uint64_t start = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
+  uint64_t start = 0;
+  for (uint32_t it = 0;; ++it) {
     if (int32_t(ld_acquire_sys(flag) - target) >= 0) return true;
-    if ((it & 15) == 0) {
+    if ((it & 15) == 15) {
       if (status && *(volatile int*)status) return false;  // someone else already failed
-      if (globaltimer_ns() - start > timeout_ns) {
+      const uint64_t now = globaltimer_ns();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > timeout_ns) {
         record_status(status, code);
         return false;
       }

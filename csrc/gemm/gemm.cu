@@ -3,6 +3,7 @@
 #include "gemm_api.h"
 #include "gemm_kernel.cuh"
 
+#include <cmath>
 #include <mutex>
 #include <cstdio>
 
@@ -10,6 +11,12 @@ namespace tn5b {
 namespace gemm {
 
 namespace {
+// Wave-model constants of the auto tile choice (measured tensor-pipe busy
+// fractions on B200 at 8192^3, and the wide tile's unoverlapped epilogue
+// expressed as an equivalent K length).
+constexpr double kEffSingle = 0.74;
+constexpr double kEffWide = 0.93;
+constexpr double kWideEpilogueK = 256.0;
 thread_local std::string g_last_error;
 
 int fail(const char* msg) {
@@ -62,11 +69,11 @@ int sm_count() {
   return v;
 }
 
-template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false>
+template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false, bool WIDE = false>
 int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUtensorMap& mb,
            int grid, cudaStream_t stream) {
-  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR>;
-  auto kern = gemm_kernel<BN, STAGES, EPI_COLS, MODE, AG, PAIR>;
+  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR, WIDE>;
+  auto kern = gemm_kernel<BN, STAGES, EPI_COLS, MODE, AG, PAIR, WIDE>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -97,12 +104,28 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
   }
 }
 
-// CTA pairs (256 x 256 cluster tiles) for local / all-gather GEMMs with enough tiles.
-bool use_pair(const GemmCall& c, int bn) {
-  if (c.mode != 0 || bn != 256) return false;
-  // Opt-in only (pair == 1): CTA-pair tiles measured no faster than single-CTA
-  // tiles, and the pair path is not part of the default GEMM.
-  return c.pair == 1;
+// Tile kinds: single-CTA 128 x BN (double-buffered accumulators), CTA pair
+// 256 x 256, wide CTA pair 256 x 512 (one accumulator, twice the tensor work per
+// byte in flight).  Auto picks between single and wide with a wave model: the
+// wide tile keeps the tensor pipe busier on long K loops, but its epilogue is
+// not overlapped and its 4x larger tiles quantise into fewer, coarser waves.
+enum TileKind { kSingle = 0, kPair = 1, kWide = 2 };
+
+int tile_kind(const GemmCall& c, int bn) {
+  if (c.mode != 0 || bn != 256) return kSingle;
+  if (c.pair >= 0) {
+    if (c.pair == kWide && c.ag) return kPair;  // no all-gather wide instantiation
+    return c.pair <= kWide ? c.pair : kSingle;
+  }
+  if (c.ag || c.tile_order || c.K < 1024) return kSingle;  // explicit orders index single-CTA tiles
+  const double sms = sm_count();
+  const double tiles_s = double((c.M + 127) / 128) * double((c.N + 255) / 256);
+  const double tiles_w = double((c.M + 255) / 256) * double((c.N + 511) / 512);
+  const double waves_s = std::ceil(tiles_s / sms), waves_w = std::ceil(tiles_w / (sms / 2));
+  // Per-SM work of one wave: 1 unit (128 x 256 x K) single, 2 units wide.
+  const double cost_s = waves_s / kEffSingle;
+  const double cost_w = 2.0 * waves_w * (1.0 + kWideEpilogueK / double(c.K)) / kEffWide;
+  return cost_w < cost_s ? kWide : kSingle;
 }
 
 int pick_bn(const GemmCall& c) {
@@ -121,9 +144,11 @@ std::string last_error() { return g_last_error; }
 
 int grid_ctas(const GemmCall& c) {
   const int bn = pick_bn(c);
-  const bool pair = use_pair(c, bn);
+  const int kind = tile_kind(c, bn);
+  const bool pair = kind != kSingle;
   const int tile_m = pair ? 2 * kBM : kBM;
-  const long tiles = long((c.M + tile_m - 1) / tile_m) * ((c.N + bn - 1) / bn);
+  const int tile_n = kind == kWide ? 2 * bn : bn;
+  const long tiles = long((c.M + tile_m - 1) / tile_m) * ((c.N + tile_n - 1) / tile_n);
   int g = sm_count();
   if (c.max_ctas > 0 && c.max_ctas < g) g = c.max_ctas;
   if (pair) {
@@ -153,11 +178,13 @@ int run(const GemmCall& c, cudaStream_t stream) {
       return fail("gemm: residual epilogue needs an aligned residual");
   }
   const int bn = pick_bn(c);
-  const bool pair = use_pair(c, bn);
+  const int kind = tile_kind(c, bn);
+  const bool pair = kind != kSingle;
+  const int tile_n = kind == kWide ? 2 * bn : bn;
   Params p{};
   p.M = c.M; p.N = c.N; p.K = c.K;
   p.tiles_m = (c.M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
-  p.tiles_n = (c.N + bn - 1) / bn;
+  p.tiles_n = (c.N + tile_n - 1) / tile_n;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_blocks = (c.K + kBK - 1) / kBK;
   p.group_m = c.group_m > 0 ? c.group_m : 8;
@@ -209,6 +236,7 @@ int run(const GemmCall& c, cudaStream_t stream) {
   }
   switch (c.mode) {
     case 0:
+      if (kind == kWide) return launch<256, 4, 64, kModeLocal, false, true, true>(c, p, ma, mb, grid, stream);
       if (pair) return launch<256, 6, 64, kModeLocal, false, true>(c, p, ma, mb, grid, stream);
       if (bn == 256) return launch<256, 4, 64, kModeLocal, false>(c, p, ma, mb, grid, stream);
       return launch<128, 6, 64, kModeLocal, false>(c, p, ma, mb, grid, stream);

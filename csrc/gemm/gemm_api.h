@@ -25,7 +25,7 @@ struct GemmCall {
   const int* tile_order = nullptr;
   int group_m = 8;
   int bn = 0;            // 0 = auto, else 128 / 256
-  int pair = 0;          // CTA-pair (cta_group::2) tiles: 1 on (opt-in), otherwise off
+  int pair = -1;         // tile kind: -1 auto, 0 single CTA 128xBN, 1 CTA pair 256x256, 2 wide pair 256x512
   int max_ctas = 0;      // 0 = all SMs
   // mode 0 local, 1 RS push bf16, 2 RS push TACO
   int mode = 0;

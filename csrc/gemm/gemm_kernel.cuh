@@ -9,9 +9,10 @@
 // CTA roles (192 threads):
 //   warp 0      TMA producer: one elected lane streams A/B k-blocks into a
 //               STAGES-deep shared-memory ring (128-byte swizzle).
-//   warp 1      MMA issuer: allocates TMEM (2 accumulators x BN columns), one
-//               lane issues tcgen05.mma (M=128, N=BN, K=16) and commits to
-//               mbarriers that free smem stages / publish accumulators.
+//   warp 1      MMA issuer: allocates TMEM (512 columns: 2 accumulators x BN,
+//               or one 2*BN accumulator for the wide pair tile), one lane
+//               issues tcgen05.mma (K=16) and commits to mbarriers that free
+//               smem stages / publish accumulators.
 //   warps 2..5  epilogue: tcgen05.ld accumulator rows (warp w owns TMEM lanes
 //               32*(w%4)..+31), apply the fused epilogue, stage through a
 //               swizzled smem buffer and write coalesced 16-byte stores.
@@ -99,16 +100,20 @@ struct Params {
   AgArgs ag;
   int* status;
   uint64_t timeout_ns;
-  // Optional per-CTA cycle counters (profiling): [mma wait-full, mma total,
-  // producer wait-empty, epilogue wait-tmem-full].
+  // Optional per-CTA cycle counters (profiling), 8 words per CTA: [0] MMA wait
+  // for a loaded stage, [1] MMA role total, [2] producer wait for a free stage,
+  // [3] epilogue wait for an accumulator (summed over its warps), [4] MMA wait
+  // for a drained accumulator.
   unsigned long long* debug;
 };
 
-template <int BN, int STAGES, int EPI_COLS, bool PAIR = false>
+template <int BN, int STAGES, int EPI_COLS, bool PAIR = false, bool WIDE = false>
 struct SmemLayout {
   static constexpr int kABytes = kBM * kBK * 2;        // 16 KB
-  // In a CTA pair each CTA holds half of B's N rows.
-  static constexpr int kBBytes = (PAIR ? BN / 2 : BN) * kBK * 2;
+  // In a CTA pair each CTA holds half of B's N rows of every N=BN sub-tile
+  // (two sub-tiles in the wide pair).
+  static constexpr int kBSubBytes = (PAIR ? BN / 2 : BN) * kBK * 2;
+  static constexpr int kBBytes = kBSubBytes * (WIDE ? 2 : 1);
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStagingPerWarp = 32 * EPI_COLS * 2;
   static constexpr int kStagingBytes = kEpiWarps * kStagingPerWarp;
@@ -242,13 +247,24 @@ __device__ __forceinline__ uint32_t code(float x, float quant) {
 // barrier, the leader's commits arrive on both CTAs' "empty" / "tmem full"
 // barriers, and both CTAs' epilogues release the accumulator on the leader's
 // "tmem empty" barrier.  Each CTA's TMEM holds its 128 rows x BN fp32.
-template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false>
+// WIDE (implies PAIR): the pair's tile is 256 x 2*BN; every K step issues two
+// N=BN MMAs that share the A operand, so each 48 KB stage feeds twice the
+// tensor work of the 256 x BN pair tile (twice the latency cover per byte in
+// flight).  The single 128 x 2*BN accumulator fills all 512 TMEM columns, so
+// the next tile's MMAs wait for the epilogue (used for long K loops).
+template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false, bool WIDE = false>
 __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ Params p,
                 int a_mn, int b_mn) {
-  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR>;
+  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR, WIDE>;
   static_assert(!PAIR || MODE == kModeLocal, "CTA pairs serve the local-store epilogue");
+  static_assert(!WIDE || PAIR, "the wide tile is a CTA-pair tile");
+  constexpr int kSub = WIDE ? 2 : 1;               // N=BN MMAs per K step
+  constexpr int kTileN = BN * kSub;
+  constexpr int kAccBufs = WIDE ? 1 : 2;           // TMEM accumulators
+  constexpr int kTmemCols = kAccBufs * kTileN;     // 512 in every configuration
+  static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
   constexpr int kTileM = PAIR ? 2 * kBM : kBM;
   constexpr int kBRows = PAIR ? BN / 2 : BN;
   static_assert(BN % EPI_COLS == 0, "epilogue chunks must tile BN");
@@ -293,10 +309,10 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
   }
   if (warp == 1) {
     if constexpr (PAIR) {
-      tmem_alloc_pair(tmem_slot, 2 * BN);
+      tmem_alloc_pair(tmem_slot, kTmemCols);
       tmem_relinquish_pair();
     } else {
-      tmem_alloc(tmem_slot, 2 * BN);
+      tmem_alloc(tmem_slot, kTmemCols);
       tmem_relinquish();
     }
   }
@@ -320,7 +336,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         int tm, tn;
         tile_coords(p, t, tm, tn);
         const int row_a = tm * kTileM + int(cta_rank) * kBM;   // this CTA's A rows
-        const int row_b = tn * BN + int(cta_rank) * kBRows;    // this CTA's B rows
+        const int row_b = tn * kTileN + int(cta_rank) * kBRows;  // this CTA's B rows (sub-tile 0)
         if constexpr (AG) {
           const int chunk = row_a / p.ag.rows_per_src;
           if (chunk != waited_chunk) {
@@ -357,11 +373,16 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
 #pragma unroll
               for (int c = 0; c < kBM / 64; ++c) tma_load_2d_pair(sa + c * 8192, &tmap_a, fb, row_a + c * 64, k0);
             }
-            if (!b_mn) {
-              tma_load_2d_pair(sb, &tmap_b, fb, k0, row_b);
-            } else {
 #pragma unroll
-              for (int c = 0; c < kBRows / 64; ++c) tma_load_2d_pair(sb + c * 8192, &tmap_b, fb, row_b + c * 64, k0);
+            for (int j = 0; j < kSub; ++j) {
+              uint8_t* sbj = sb + j * L::kBSubBytes;
+              const int rb = row_b + j * BN;
+              if (!b_mn) {
+                tma_load_2d_pair(sbj, &tmap_b, fb, k0, rb);
+              } else {
+#pragma unroll
+                for (int c = 0; c < kBRows / 64; ++c) tma_load_2d_pair(sbj + c * 8192, &tmap_b, fb, rb + c * 64, k0);
+              }
             }
           } else {
             mbar_arrive_expect_tx(&full[s], L::kStageBytes);
@@ -383,7 +404,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
           last_parity[s] = int(ph);
         }
       }
-      if (p.debug) p.debug[blockIdx.x * 4 + 2] = (unsigned long long)dbg_empty;
+      if (p.debug) p.debug[blockIdx.x * 8 + 2] = (unsigned long long)dbg_empty;
       if (!ok) {
         // Abort path: let every issued TMA load land before the CTA can exit.
         if (!PAIR) {
@@ -402,21 +423,23 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
     if (lane == 0 && leader) {
-      long long dbg_full = 0;
+      long long dbg_full = 0, dbg_tempty = 0;
       const long long dbg_t0 = clock64();
       const uint32_t idesc = make_idesc_bf16(kTileM, BN, a_mn, b_mn);
       int it = 0, local = 0;
       bool ok = true;
       for (int t = cluster_id; t < p.num_tiles && ok; t += clusters, ++local) {
-        const int b = local & 1;
-        const uint32_t use = uint32_t(local >> 1);
+        const int b = local % kAccBufs;
+        const uint32_t use = uint32_t(local / kAccBufs);
+        const long long we = p.debug ? clock64() : 0;
         if (!mbar_wait(&tempty[b], (use & 1) ^ 1, p.timeout_ns, p.status, kTimeoutMmaTmemEmpty,
                        abort_flag)) {
           ok = false;
           break;
         }
+        if (p.debug) dbg_tempty += clock64() - we;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(b * BN);
+        const uint32_t d_tmem = tmem_base + uint32_t(b * kTileN);
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -433,12 +456,16 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
           for (int k = 0; k < kBK / kUmmaK; ++k) {
             const uint64_t ad = a_mn ? make_sw128_desc(sa + k * 2048, 8192, 1024)
                                      : make_sw128_desc(sa + k * 32, 16, 1024);
-            const uint64_t bd = b_mn ? make_sw128_desc(sb + k * 2048, 8192, 1024)
-                                     : make_sw128_desc(sb + k * 32, 16, 1024);
-            if constexpr (PAIR)
-              umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-            else
-              umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int j = 0; j < kSub; ++j) {
+              const uint32_t sbj = sb + j * L::kBSubBytes;
+              const uint64_t bd = b_mn ? make_sw128_desc(sbj + k * 2048, 8192, 1024)
+                                       : make_sw128_desc(sbj + k * 32, 16, 1024);
+              if constexpr (PAIR)
+                umma_f16_pair(d_tmem + j * BN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              else
+                umma_f16(d_tmem + j * BN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
           }
           if constexpr (PAIR) {
             umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 0));
@@ -462,8 +489,9 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         umma_commit(drain);
       mbar_wait(drain, 0, p.timeout_ns, p.status, kTimeoutDrain, nullptr);
       if (p.debug) {
-        p.debug[blockIdx.x * 4 + 0] = (unsigned long long)dbg_full;
-        p.debug[blockIdx.x * 4 + 1] = (unsigned long long)(clock64() - dbg_t0);
+        p.debug[blockIdx.x * 8 + 0] = (unsigned long long)dbg_full;
+        p.debug[blockIdx.x * 8 + 1] = (unsigned long long)(clock64() - dbg_t0);
+        p.debug[blockIdx.x * 8 + 4] = (unsigned long long)dbg_tempty;
       }
     }
   } else if (warp < kEpiFirstWarp + kEpiWarps) {
@@ -476,18 +504,21 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     for (int t = cluster_id; t < p.num_tiles; t += clusters, ++local) {
       int tm, tn;
       tile_coords(p, t, tm, tn);
-      const int b = local & 1;
-      const uint32_t use = uint32_t(local >> 1);
+      const int b = local % kAccBufs;
+      const uint32_t use = uint32_t(local / kAccBufs);
       int ok = 1;
-      if (lane == 0)
+      if (lane == 0) {
+        const long long we = p.debug ? clock64() : 0;
         ok = mbar_wait(&tfull[b], use & 1, p.timeout_ns, p.status, kTimeoutEpiTmemFull,
                        abort_flag);
+        if (p.debug) atomicAdd(p.debug + blockIdx.x * 8 + 3, (unsigned long long)(clock64() - we));
+      }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
       const int row_w = tm * kTileM + int(cta_rank) * kBM + q * 32;  // first row of this warp
       const int my_row = row_w + lane;
-      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * BN);
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * kTileN);
 
       // Destination of this tile (reduce-scatter modes).
       int dest = 0;
@@ -497,8 +528,8 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         remote_taco = (MODE == kModeRsTaco) && dest != p.rs.rank;
       }
 
-      for (int c0 = 0; c0 < BN; c0 += EPI_COLS) {
-        const int col0 = tn * BN + c0;
+      for (int c0 = 0; c0 < kTileN; c0 += EPI_COLS) {
+        const int col0 = tn * kTileN + c0;
         float v[EPI_COLS];
 #pragma unroll
         for (int j = 0; j < EPI_COLS; j += 32) {
@@ -508,7 +539,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[j + i] = __uint_as_float(r[i]);
         }
-        if (c0 + EPI_COLS >= BN) {
+        if (c0 + EPI_COLS >= kTileN) {
           // Accumulator fully read: hand the TMEM buffer back to the MMA warp.
           tc_fence_before();
           __syncwarp();
@@ -747,9 +778,9 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
   if (warp == 1) {
     tc_fence_after();
     if constexpr (PAIR)
-      tmem_dealloc_pair(tmem_base, 2 * BN);
+      tmem_dealloc_pair(tmem_base, kTmemCols);
     else
-      tmem_dealloc(tmem_base, 2 * BN);
+      tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 

@@ -6,8 +6,9 @@ stored [K, M] (MN-major), `b_t=True` means `b` is stored [K, N].  Epilogues:
 bias, exact GeLU with the pre-activation written to `aux`, residual add
 (out = bf16(bf16(res + bf16(acc)) + bias)), accumulate (out += acc) and GeLU
 backward (out = bf16(bf16(acc) * gelu'(pre)) with the saved pre-activation).
-`pair=1` opts into 256x256 CTA-pair tiles (tcgen05 cta_group::2); the default
-is single-CTA 128-row tiles.
+`pair` selects the tile kind: -1 auto (default), 0 single CTA 128x256 with
+double-buffered accumulators, 1 CTA pair 256x256 (tcgen05 cta_group::2), 2 wide
+CTA pair 256x512 (two N=256 MMAs per K step, for long K loops).
 """
 from __future__ import annotations
 
@@ -22,7 +23,7 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = F
            out: torch.Tensor | None = None, bias: torch.Tensor | None = None,
            gelu_aux: torch.Tensor | None = None, residual: torch.Tensor | None = None,
            accumulate: bool = False, gelu_grad_of: torch.Tensor | None = None, bn: int = 0,
-           max_ctas: int = 0, tile_order: torch.Tensor | None = None, pair: int = 0,
+           max_ctas: int = 0, tile_order: torch.Tensor | None = None, pair: int = -1,
            group_m: int = 0, debug: torch.Tensor | None = None) -> torch.Tensor:
     M = a.shape[1] if a_t else a.shape[0]
     N = b.shape[1] if b_t else b.shape[0]

@@ -141,6 +141,21 @@ def attention_case(rank, world, timer, heads=32, hidden=4096, seq=2048, batch=4)
     rows = [dict(op="attention_block", impl="ours", world=world, us=timer.run(ours), flops=flops)]
     if world > 1:
         rows.append(dict(op="attention_block", impl="nccl+cublas+sdpa", world=world, us=timer.run(library), flops=flops))
+    # Stage breakdown (each stage timed alone on the same inputs).
+    qkv, _ = tp.ag_linear(("bench_qkv", 0), xs, wqkv, bias=bqkv)
+    attn, _ = A.forward(qkv, batch, seq, lh)
+    q, k, v = qkv.view(batch, seq, 3, lh, 128).permute(2, 0, 3, 1, 4).unbind(0)
+    stages = dict(
+        ag_gemm=lambda: tp.ag_linear(("bench_qkv", 0), xs, wqkv, bias=bqkv),
+        attention=lambda: A.forward(qkv, batch, seq, lh, out=attn),
+        gemm_rs=lambda: tp.linear_rs(attn, wo, residual=xs, bias=bo, role="attn"),
+        lib_all_gather=lambda: dist.all_gather_into_tensor(full, xs) if world > 1 else None,
+        lib_qkv_gemm=lambda: F.linear(full, wqkv, bqkv),
+        lib_sdpa=lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True),
+        lib_out_gemm=lambda: torch.mm(attn, wo.t()),
+    )
+    for name, fn in stages.items():
+        rows.append(dict(op="attention_stage", stage=name, world=world, us=timer.run(fn)))
     tp.close()
     return rows
 

@@ -18,7 +18,8 @@ def _rel(x, y):
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 320), (384, 128, 1024),
                                    (1000, 520, 200), (2048, 6288, 4096)])
 @pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, True), (True, False)])
-def test_gemm_matches_fp32(M, N, K, a_t, b_t):
+@pytest.mark.parametrize("kind", [0, 1, 2])
+def test_gemm_matches_fp32(M, N, K, a_t, b_t, kind):
     from tempname_5090_b200.ops.gemm import matmul
     from tempname_5090_b200._native import check_status
     if (a_t and M % 8) or (b_t and N % 8):
@@ -26,15 +27,15 @@ def test_gemm_matches_fp32(M, N, K, a_t, b_t):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
     a = torch.randn((K, M) if a_t else (M, K), generator=g, device="cuda").to(torch.bfloat16)
     b = torch.randn((K, N) if b_t else (N, K), generator=g, device="cuda").to(torch.bfloat16)
-    out = matmul(a, b, a_t=a_t, b_t=b_t)
+    out = matmul(a, b, a_t=a_t, b_t=b_t, bn=256 if kind else 0, pair=kind)
     torch.cuda.synchronize()
     check_status()
     ref = _ref(a, b, a_t, b_t)
     assert _rel(out, ref) < 1e-2
 
 
-@pytest.mark.parametrize("bn", [128, 256])
-def test_gemm_epilogues(bn):
+@pytest.mark.parametrize("bn,kind", [(128, 0), (256, 0), (256, 1), (256, 2)])
+def test_gemm_epilogues(bn, kind):
     from tempname_5090_b200.ops.gemm import matmul
     M, N, K = 512, 768, 256
     g = torch.Generator(device="cuda").manual_seed(3)
@@ -42,20 +43,20 @@ def test_gemm_epilogues(bn):
     b = (torch.randn((N, K), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
     bias = torch.randn((N,), generator=g, device="cuda").to(torch.bfloat16)
     ref = a.float() @ b.float().t()
-    out = matmul(a, b, bias=bias, bn=bn)
+    out = matmul(a, b, bias=bias, bn=bn, pair=kind)
     assert _rel(out, ref + bias.float()) < 1e-2
     aux = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
-    out = matmul(a, b, bias=bias, gelu_aux=aux, bn=bn)
+    out = matmul(a, b, bias=bias, gelu_aux=aux, bn=bn, pair=kind)
     pre = (ref + bias.float()).to(torch.bfloat16)
     assert _rel(aux, pre) < 1e-2
     assert _rel(out, torch.nn.functional.gelu(pre.float())) < 1e-2
     res = torch.randn((M, N), generator=g, device="cuda").to(torch.bfloat16)
-    out = matmul(a, b, bias=bias, residual=res, bn=bn)
+    out = matmul(a, b, bias=bias, residual=res, bn=bn, pair=kind)
     expect = ((res.float() + ref.to(torch.bfloat16).float()).to(torch.bfloat16).float() + bias.float())
     assert _rel(out, expect) < 1e-2
     base = torch.randn((M, N), generator=g, device="cuda").to(torch.bfloat16)
     acc = base.clone()
-    matmul(a, b, out=acc, accumulate=True, bn=bn)
+    matmul(a, b, out=acc, accumulate=True, bn=bn, pair=kind)
     assert _rel(acc, base.float() + ref) < 1e-2
 
 
@@ -71,3 +72,14 @@ def test_gemm_strided_output_and_tile_order():
     matmul(a, b, out=view, bn=256, tile_order=order)
     assert _rel(view, a.float() @ b.float().t()) < 1e-2
     assert big[:, :N].abs().sum().item() == 0
+
+
+@pytest.mark.parametrize("kind", [1, 2])
+def test_pair_tiles_bitwise_equal_single_cta(kind):
+    """Same K loop order in every tile kind: identical FP32 accumulators."""
+    from tempname_5090_b200.ops.gemm import matmul
+    a = torch.randn((1024, 768), device="cuda").to(torch.bfloat16)
+    b = torch.randn((1536, 768), device="cuda").to(torch.bfloat16)
+    x = matmul(a, b, bn=256, pair=0)
+    y = matmul(a, b, bn=256, pair=kind)
+    assert torch.equal(x, y)
