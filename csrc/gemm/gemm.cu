@@ -71,8 +71,9 @@ int sm_count() {
 
 template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false, bool WIDE = false>
 int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUtensorMap& mb,
-           int grid, cudaStream_t stream) {
-  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR, WIDE>;
+           const CUtensorMap& mo, int grid, cudaStream_t stream) {
+  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR, WIDE, kStagingBuffers<MODE>>;
+  static_assert(L::kTotal <= 232448, "dynamic shared memory above the 227 KB per-block limit");
   auto kern = gemm_kernel<BN, STAGES, EPI_COLS, MODE, AG, PAIR, WIDE>;
   static bool configured[64] = {false};
   int dev = 0;
@@ -97,9 +98,9 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return int(cudaLaunchKernelEx(&cfg, kern, ma, mb, p, c.a_mn, c.b_mn));
+    return int(cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, p, c.a_mn, c.b_mn));
   } else {
-    kern<<<grid, threads, L::kTotal, stream>>>(ma, mb, p, c.a_mn, c.b_mn);
+    kern<<<grid, threads, L::kTotal, stream>>>(ma, mb, mo, p, c.a_mn, c.b_mn);
     return int(cudaGetLastError());
   }
 }
@@ -228,22 +229,28 @@ int run(const GemmCall& c, cudaStream_t stream) {
   const bool ok_b = c.b_mn ? make_map(&mb, c.B, c.N, c.K, c.ldb, 64, 64)
                            : make_map(&mb, c.B, c.K, c.N, c.ldb, 64, pair ? bn / 2 : bn);
   if (!ok_a || !ok_b) return fail("gemm: cuTensorMapEncodeTiled failed");
+  // Output tensor map for the TMA-store epilogue (local mode, aligned output).
+  CUtensorMap mo = ma;
+  p.tma_store = 0;
+  if (c.mode == 0 && c.out && !(reinterpret_cast<uintptr_t>(c.out) & 15) && c.ldo % 8 == 0 &&
+      make_map(&mo, c.out, c.N, c.M, c.ldo, 64, 32))
+    p.tma_store = 1;
   const int grid = grid_ctas(c);
   if (c.ag) {
-    if (pair) return launch<256, 6, 64, kModeLocal, true, true>(c, p, ma, mb, grid, stream);
-    if (bn == 256) return launch<256, 4, 64, kModeLocal, true>(c, p, ma, mb, grid, stream);
-    return launch<128, 6, 64, kModeLocal, true>(c, p, ma, mb, grid, stream);
+    if (pair) return launch<256, 6, 64, kModeLocal, true, true>(c, p, ma, mb, mo, grid, stream);
+    if (bn == 256) return launch<256, 4, 64, kModeLocal, true>(c, p, ma, mb, mo, grid, stream);
+    return launch<128, 6, 64, kModeLocal, true>(c, p, ma, mb, mo, grid, stream);
   }
   switch (c.mode) {
     case 0:
-      if (kind == kWide) return launch<256, 4, 64, kModeLocal, false, true, true>(c, p, ma, mb, grid, stream);
-      if (pair) return launch<256, 6, 64, kModeLocal, false, true>(c, p, ma, mb, grid, stream);
-      if (bn == 256) return launch<256, 4, 64, kModeLocal, false>(c, p, ma, mb, grid, stream);
-      return launch<128, 6, 64, kModeLocal, false>(c, p, ma, mb, grid, stream);
+      if (kind == kWide) return launch<256, 4, 64, kModeLocal, false, true, true>(c, p, ma, mb, mo, grid, stream);
+      if (pair) return launch<256, 6, 64, kModeLocal, false, true>(c, p, ma, mb, mo, grid, stream);
+      if (bn == 256) return launch<256, 4, 64, kModeLocal, false>(c, p, ma, mb, mo, grid, stream);
+      return launch<128, 6, 64, kModeLocal, false>(c, p, ma, mb, mo, grid, stream);
     case 1:
-      return launch<256, 4, 64, kModeRsPush, false>(c, p, ma, mb, grid, stream);
+      return launch<256, 4, 64, kModeRsPush, false>(c, p, ma, mb, mo, grid, stream);
     case 2:
-      return launch<256, 3, 128, kModeRsTaco, false>(c, p, ma, mb, grid, stream);
+      return launch<256, 3, 128, kModeRsTaco, false>(c, p, ma, mb, mo, grid, stream);
     default:
       return fail("gemm: unknown mode");
   }

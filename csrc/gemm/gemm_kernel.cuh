@@ -98,6 +98,7 @@ struct Params {
   const __nv_bfloat16* residual; int64_t ld_res;
   RsArgs rs;
   AgArgs ag;
+  int tma_store;                 // local mode: store the output tile with TMA (tmap_out)
   int* status;
   uint64_t timeout_ns;
   // Optional per-CTA cycle counters (profiling), 8 words per CTA: [0] MMA wait
@@ -107,7 +108,7 @@ struct Params {
   unsigned long long* debug;
 };
 
-template <int BN, int STAGES, int EPI_COLS, bool PAIR = false, bool WIDE = false>
+template <int BN, int STAGES, int EPI_COLS, bool PAIR = false, bool WIDE = false, int STG_BUFS = 1>
 struct SmemLayout {
   static constexpr int kABytes = kBM * kBK * 2;        // 16 KB
   // In a CTA pair each CTA holds half of B's N rows of every N=BN sub-tile
@@ -115,7 +116,8 @@ struct SmemLayout {
   static constexpr int kBSubBytes = (PAIR ? BN / 2 : BN) * kBK * 2;
   static constexpr int kBBytes = kBSubBytes * (WIDE ? 2 : 1);
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStagingPerWarp = 32 * EPI_COLS * 2;
+  static constexpr int kStagingBufBytes = 32 * EPI_COLS * 2;   // one warp's 32 rows x EPI_COLS bf16
+  static constexpr int kStagingPerWarp = STG_BUFS * kStagingBufBytes;
   static constexpr int kStagingBytes = kEpiWarps * kStagingPerWarp;
   static constexpr int kBarrierBytes = 256;
   // [align 1024][stages][staging][barriers]
@@ -252,12 +254,17 @@ __device__ __forceinline__ uint32_t code(float x, float quant) {
 // tensor work of the 256 x BN pair tile (twice the latency cover per byte in
 // flight).  The single 128 x 2*BN accumulator fills all 512 TMEM columns, so
 // the next tile's MMAs wait for the epilogue (used for long K loops).
+// Local-mode epilogues store the output tile with TMA (double-buffered staging
+// per warp: the store of one 32 x EPI_COLS chunk overlaps the next chunk).
+template <int MODE>
+constexpr int kStagingBuffers = MODE == kModeLocal ? 2 : 1;
+
 template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false, bool WIDE = false>
 __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ Params p,
-                int a_mn, int b_mn) {
-  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR, WIDE>;
+                const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_out,
+                const __grid_constant__ Params p, int a_mn, int b_mn) {
+  using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR, WIDE, kStagingBuffers<MODE>>;
   static_assert(!PAIR || MODE == kModeLocal, "CTA pairs serve the local-store epilogue");
   static_assert(!WIDE || PAIR, "the wide tile is a CTA-pair tile");
   constexpr int kSub = WIDE ? 2 : 1;               // N=BN MMAs per K step
@@ -498,8 +505,9 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     // ------------------------------------------------------------- epilogue
     const int q = warp & 3;                       // TMEM lane quarter
     const int ew = warp - kEpiFirstWarp;          // staging buffer
-    uint8_t* stg = staging + ew * L::kStagingPerWarp;
-    const uint32_t stg_addr = smem_u32(stg);
+    uint8_t* stg_base = staging + ew * L::kStagingPerWarp;
+    int chunk_seq = 0;  // TMA-store chunks issued by this warp (staging buffer = parity)
+    const bool tma_out = MODE == kModeLocal && p.tma_store;
     int local = 0;
     for (int t = cluster_id; t < p.num_tiles; t += clusters, ++local) {
       int tm, tn;
@@ -530,6 +538,13 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
 
       for (int c0 = 0; c0 < kTileN; c0 += EPI_COLS) {
         const int col0 = tn * kTileN + c0;
+        uint8_t* stg = stg_base + (kStagingBuffers<MODE> == 2 ? (chunk_seq & 1) * L::kStagingBufBytes : 0);
+        const uint32_t stg_addr = smem_u32(stg);
+        if (tma_out && chunk_seq >= 2) {
+          // This buffer's previous TMA store (two chunks ago) must have read it.
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+        }
         float v[EPI_COLS];
 #pragma unroll
         for (int j = 0; j < EPI_COLS; j += 32) {
@@ -699,6 +714,17 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
                            stg_addr + staging_offset<EPI_COLS>(lane, u)),
                        "r"(pk.x), "r"(pk.y), "r"(pk.z), "r"(pk.w));
         }
+        if (tma_out) {
+          // Swizzled staging == the SWIZZLE_128B box layout: hand it to TMA.
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, stg_addr, col0, row_w);
+            bulk_commit_group();
+          }
+          ++chunk_seq;
+          continue;
+        }
         __syncwarp();
         {
           constexpr int kUnits = EPI_COLS / 8;
@@ -747,6 +773,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         }
       }
     }
+    if (tma_out && lane == 0) bulk_wait_group_all();  // stores complete before the CTA exits
   } else {
     // ------------------------------------------- AG push warp (AG mode only)
     if constexpr (AG) {
