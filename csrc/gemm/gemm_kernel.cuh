@@ -786,8 +786,18 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
       for (int step = 1; step <= p.ag.world; ++step) {
         const int dst = (p.ag.rank + step) % p.ag.world;
         uint8_t* out = p.ag.gather[dst] + int64_t(p.ag.rank) * p.ag.shard_bytes;
-        for (int64_t u = lo + lane; u < hi; u += 32)
-          st_global_v4(out + u * 16, ld_global_nc_v4(p.ag.shard + u * 16));
+        // Eight independent 16-byte loads in flight per lane before their stores
+        // (a load->store chain per unit would pay one HBM latency per 512 bytes).
+        constexpr int kUnroll = 8;
+        int64_t u = lo + lane;
+        for (; u + (kUnroll - 1) * 32 < hi; u += kUnroll * 32) {
+          uint4 v[kUnroll];
+#pragma unroll
+          for (int i = 0; i < kUnroll; ++i) v[i] = ld_global_nc_v4(p.ag.shard + (u + i * 32) * 16);
+#pragma unroll
+          for (int i = 0; i < kUnroll; ++i) st_global_v4(out + (u + i * 32) * 16, v[i]);
+        }
+        for (; u < hi; u += 32) st_global_v4(out + u * 16, ld_global_nc_v4(p.ag.shard + u * 16));
         __syncwarp();
         if (lane == 0) {
           fence_acq_rel_sys();

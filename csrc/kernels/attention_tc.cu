@@ -122,14 +122,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint64_t xbar[4];  // per lane quarter: the two softmax warps' handshake
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int qt = int(gridDim.x) - 1 - int(blockIdx.x);
-  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  // Grid (B*H, S/128): blocks are scheduled x-fastest, so every head's heaviest
+  // (latest) query tile runs in the first wave and the light ones fill the tail.
+  const int bh = blockIdx.x;
+  const int qt = int(gridDim.y) - 1 - int(blockIdx.y);
+  const int b = bh / H, h = bh % H;
   const int q0 = qt * kBlk;
   const int row0 = b * S;
   const int nkb = qt + 1;
   // Optional progress trace (16 words per CTA): [0] SM id and stage, [1] producer,
   // [2] MMA issuer, [3..10] elementwise warps (block index + 1 reached).
-  unsigned long long* tr = trace ? trace + (size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 16 : nullptr;
+  unsigned long long* tr = trace ? trace + (size_t(bh) * gridDim.y + qt) * 16 : nullptr;
   const unsigned long long tsm = (unsigned long long)smid() << 16;
   if (threadIdx.x == 0) trace_put(tr, 0, tsm | 1);
 
@@ -336,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv = 1.f / ltot;
       const int qidx = q0 + row;
-      if (half == 0) lse[int64_t(blockIdx.y) * S + qidx] = (m_run + log2f(ltot)) / kLog2e;
+      if (half == 0) lse[int64_t(bh) * S + qidx] = (m_run + log2f(ltot)) / kLog2e;
       // Stage 32 rows x 64 columns (128 B per row) of this warp through smem (Q tile is dead).
       uint8_t* stg = sm + kSmQ + (q * 2 + half) * 4096;
 #pragma unroll
@@ -491,8 +494,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int kb = blockIdx.x;  // small key blocks carry the most query blocks: run them first
-  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  // Grid (B*H, S/128), x-fastest: small key blocks carry the most query blocks
+  // and run first for every head.
+  const int bh = blockIdx.x;
+  const int kb = blockIdx.y;
+  const int b = bh / H, h = bh % H;
   const int row0 = b * S;
   const int k0 = kb * kBlk;
   const int nqb = S / kBlk;
@@ -538,8 +544,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sQ + st * 32768 + 16384, &tq, q_full + st, h * kD + 64, row0 + i * kBlk);
         tma_load_2d(sO + st * 32768, &tdo, q_full + st, h * kD, row0 + i * kBlk);
         tma_load_2d(sO + st * 32768 + 16384, &tdo, q_full + st, h * kD + 64, row0 + i * kBlk);
-        bulk_load(sStat + st * 256, lse + int64_t(blockIdx.y) * S + i * kBlk, 512, q_full + st);
-        bulk_load(sStat + st * 256 + 128, Dvec + int64_t(blockIdx.y) * S + i * kBlk, 512, q_full + st);
+        bulk_load(sStat + st * 256, lse + int64_t(bh) * S + i * kBlk, 512, q_full + st);
+        bulk_load(sStat + st * 256 + 128, Dvec + int64_t(bh) * S + i * kBlk, 512, q_full + st);
       }
     }
   } else if (warp == 1) {
@@ -639,8 +645,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int qt = int(gridDim.x) - 1 - int(blockIdx.x);  // heavy first
-  const int b = blockIdx.y / H, h = blockIdx.y % H;
+  const int bh = blockIdx.x;  // grid (B*H, S/128), x-fastest: heavy query tiles first
+  const int qt = int(gridDim.y) - 1 - int(blockIdx.y);
+  const int b = bh / H, h = bh % H;
   const int row0 = b * S;
   const int q0 = qt * kBlk;
   const int nkb = qt + 1;
@@ -722,8 +729,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     const float sl2 = scale * kLog2e;
-    const float lse2 = lse[int64_t(blockIdx.y) * S + q0 + row] * kLog2e;
-    const float drow = Dvec[int64_t(blockIdx.y) * S + q0 + row];
+    const float lse2 = lse[int64_t(bh) * S + q0 + row] * kLog2e;
+    const float drow = Dvec[int64_t(bh) * S + q0 + row];
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
       if (!warp_wait(s_full, j & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
@@ -763,7 +770,7 @@ int attention_fwd_tc(const void* qkv, int64_t ld_qkv, void* out, int64_t ld_out,
     cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmTotal);
     configured[dev] = true;
   }
-  dim3 grid(S / kBlk, B * H);
+  dim3 grid(B * H, S / kBlk);
   attn_fwd_tc_kernel<<<grid, kThreads, kSmTotal, s>>>(map, static_cast<__nv_bfloat16*>(out), ld_out, lse, S, H,
                                                       scale, status, timeout_ns, trace);
   return int(cudaGetLastError());
@@ -784,7 +791,7 @@ int attention_bwd_tc(const void* qkv, int64_t ld_qkv, const void* dout, int64_t 
     cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
     configured[dev] = true;
   }
-  dim3 grid(S / kBlk, B * H);
+  dim3 grid(B * H, S / kBlk);
   attn_bwd_dkdv_tc_kernel<<<grid, kThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
                                                              ld_dqkv, S, H, scale, status, timeout_ns);
   attn_bwd_dq_tc_kernel<<<grid, kThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),

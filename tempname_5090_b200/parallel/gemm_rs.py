@@ -105,7 +105,10 @@ class GemmRS:
         self.timeout_ns = int(timeout_ns)
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.order = mapping.schedule(m, n, k, self.world, chunk_rows, arm, plan)
-        ids = mapping.linear_tile_ids(m, n, k, self.world, chunk_rows, arm, plan, tile_n=TILE_N)
+        # In-kernel pushes start on destination rank+1 (no incast); the NCCL
+        # transport keeps the reference CTA map.
+        shift = self.rank + 1 if transport == "nvlink" else 0
+        ids = mapping.linear_tile_ids(m, n, k, self.world, chunk_rows, arm, plan, tile_n=TILE_N, shift=shift)
         self.tile_order = torch.tensor(ids, dtype=torch.int32, device=self.device)
         local = mapping.consumer_tile_order(m, n, k, self.world, chunk_rows, arm, self.rank, plan, TILE_N)
         self.consumer_order = torch.tensor(local, dtype=torch.int32, device=self.device)

@@ -94,10 +94,23 @@ def cta_mapping(m, n, k, world, chunk_rows, arm, plan=None):
     return tile_order(m, n, k, world, chunk_rows, arm, plan, tile_n=128)
 
 
-def linear_tile_ids(m, n, k, world, chunk_rows, arm, plan=None, tile_n=256):
-    """Tile order as linear ids tm * tiles_n + tn (the GEMM kernel's table)."""
+def linear_tile_ids(m, n, k, world, chunk_rows, arm, plan=None, tile_n=256, shift=0):
+    """Tile order as linear ids tm * tiles_n + tn (the GEMM kernel's table).
+
+    `shift` rotates destinations: a tile of destination d is replaced by the tile
+    at the same position inside destination (d + shift) % W.  The arm's slot
+    structure is kept; with shift = rank + 1 the ranks of an in-kernel push start
+    on different destinations (and end on their own rows) instead of all pushing
+    into the same GPU at once.  Results do not depend on the order: the owner
+    reduces sources in index order."""
     cols = n // tile_n
-    return [tm * cols + tn for tm, tn in tile_order(m, n, k, world, chunk_rows, arm, plan, tile_n)]
+    per_dest = m // world // TILE_M
+    out = []
+    for tm, tn in tile_order(m, n, k, world, chunk_rows, arm, plan, tile_n):
+        if shift:
+            tm = ((tm // per_dest + shift) % world) * per_dest + tm % per_dest
+        out.append(tm * cols + tn)
+    return out
 
 
 def consumer_tile_order(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n=256):

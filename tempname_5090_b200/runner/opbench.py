@@ -3,6 +3,9 @@
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m tempname_5090_b200.runner.opbench --op gemmrs
     ... --op attention      # AG->GEMM QKV + causal attention + GemmRS out-proj (TP8, SP)
     ... --op sweep          # GemmRS N=4096, K=16384/TP, M in 2048..32768, bf16 vs TACO
+    python -m tempname_5090_b200.runner.opbench --op gemm         # 1 GPU: tile kinds vs cuBLAS
+    python -m tempname_5090_b200.runner.opbench --op gemm_once --kind 2   # one GEMM (profiler case)
+    python -m tempname_5090_b200.runner.opbench --op attn_kernel  # 1 GPU: attention fwd/bwd kernels
 
 Timing: every iteration is bracketed by CUDA events on the launching stream,
 the L2 is flushed (a 256 MiB write) between iterations outside the events,
@@ -160,9 +163,95 @@ def attention_case(rank, world, timer, heads=32, hidden=4096, seq=2048, batch=4)
     return rows
 
 
+GEMM_SHAPES = ((8192, 8192, 8192), (8192, 12288, 4096), (8192, 16384, 4096), (8192, 4096, 16384),
+               (8192, 4096, 4096), (8192, 4096, 2048))
+
+
+def gemm_case(shapes, timer):
+    """Tile kinds (0 single CTA, 1 CTA pair, 2 wide pair, -1 auto) against cuBLAS,
+    with the kernel's own cycle counters (MMA-role cycles and wait fractions)."""
+    import torch
+    from ..ops.gemm import matmul
+    from .._native import check_status
+    rows = []
+    for (m, n, k) in shapes:
+        a = torch.randn((m, k), device="cuda").to(torch.bfloat16)
+        b = torch.randn((n, k), device="cuda").to(torch.bfloat16)
+        out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+        ref = torch.mm(a, b.t())
+        flops = 2.0 * m * n * k
+        for kind in (0, 1, 2, -1):
+            fn = (lambda kind=kind: matmul(a, b, out=out, bn=256 if kind else 0, pair=kind))
+            fn()
+            torch.cuda.synchronize()
+            check_status()
+            exact = bool(torch.equal(out, ref))
+            us = timer.run(fn)
+            dbg = torch.zeros(148 * 8, dtype=torch.int64, device="cuda")
+            matmul(a, b, out=out, bn=256 if kind else 0, pair=kind, debug=dbg)
+            torch.cuda.synchronize()
+            d = dbg.view(-1, 8).double()
+            lead = d[d[:, 1] > 0]
+            rows.append(dict(op="gemm", kind=kind, m=m, n=n, k=k, us=us, tflops=flops / us / 1e6,
+                             bitwise_equal_cublas=exact, mma_cycles=lead[:, 1].mean().item(),
+                             mma_wait_data=(lead[:, 0] / lead[:, 1]).mean().item(),
+                             mma_wait_accumulator=(lead[:, 4] / lead[:, 1]).mean().item()))
+        us = timer.run(lambda: torch.mm(a, b.t(), out=out))
+        rows.append(dict(op="gemm", kind="cublas", m=m, n=n, k=k, us=us, tflops=flops / us / 1e6))
+    return rows
+
+
+def gemm_once(m, n, k, kind):
+    """Three launches of one GEMM (a small, self-ending case for a profiler)."""
+    import torch
+    from ..ops.gemm import matmul
+    a = torch.randn((m, k), device="cuda").to(torch.bfloat16)
+    b = torch.randn((n, k), device="cuda").to(torch.bfloat16)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    for _ in range(3):
+        if kind == "cublas":
+            torch.mm(a, b.t(), out=out)
+        else:
+            matmul(a, b, out=out, bn=256 if int(kind) else 0, pair=int(kind))
+    torch.cuda.synchronize()
+    return [dict(op="gemm_once", kind=kind, m=m, n=n, k=k)]
+
+
+def attention_kernel_case(timer, shapes=((4, 2048, 4), (1, 2048, 32), (4, 2048, 32))):
+    """Causal attention kernels (head_dim 128) against an fp32 torch reference."""
+    import torch
+    import torch.nn.functional as F
+    from ..ops import attention as A
+    rows = []
+    for (B, S, H) in shapes:
+        d = 128
+        qkv = torch.randn((B * S, 3 * H * d), device="cuda").to(torch.bfloat16)
+        out, lse = A.forward(qkv, B, S, H)
+        dout = torch.randn((B * S, H * d), device="cuda").to(torch.bfloat16)
+        dqkv = A.backward(qkv, out, dout, lse, B, S, H)
+        q, k, v = qkv.float().reshape(B, S, 3, H, d).permute(2, 0, 3, 1, 4).unbind(0)
+        q.requires_grad_(True); k.requires_grad_(True); v.requires_grad_(True)
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(B * S, H * d)
+        o.backward(dout.float())
+        g = dqkv.float().reshape(B, S, 3, H, d).permute(2, 0, 3, 1, 4)
+        rel = lambda x, y: ((x - y).norm() / y.norm()).item()
+        again = A.backward(qkv, out, dout, lse, B, S, H)
+        flops = 4.0 * B * H * S * S * d / 2
+        fwd_us = timer.run(lambda: A.forward(qkv, B, S, H, out=out))
+        bwd_us = timer.run(lambda: A.backward(qkv, out, dout, lse, B, S, H, dqkv=dqkv))
+        rows.append(dict(op="attention_kernel", B=B, S=S, H=H, fwd_us=fwd_us, bwd_us=bwd_us,
+                         fwd_tflops=flops / fwd_us / 1e6, bwd_tflops=2.5 * flops / bwd_us / 1e6,
+                         out_rel_err=rel(out.float(), o.detach()), dq_rel_err=rel(g[0], q.grad),
+                         dk_rel_err=rel(g[1], k.grad), dv_rel_err=rel(g[2], v.grad),
+                         backward_deterministic=bool(torch.equal(again, dqkv))))
+    return rows
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep"), default="gemmrs")
+    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep", "gemm", "gemm_once", "attn_kernel"),
+                    default="gemmrs")
+    ap.add_argument("--kind", default="2", help="gemm_once: tile kind 0/1/2/-1 or 'cublas'")
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=2048)
@@ -185,6 +274,12 @@ def main(argv=None):
     rows = []
     if args.op == "gemmrs":
         rows += gemmrs_case(args.m, args.n, args.k, rank, world, timer, arms, transports)
+    elif args.op == "gemm":
+        rows += gemm_case(GEMM_SHAPES, timer)
+    elif args.op == "gemm_once":
+        rows += gemm_once(args.m, args.n, args.k, args.kind)
+    elif args.op == "attn_kernel":
+        rows += attention_kernel_case(timer)
     elif args.op == "attention":
         rows += attention_case(rank, world, timer)
     else:

@@ -92,7 +92,7 @@ def case_model(rank, world):
     from tempname_5090_b200.models.gpt import GPT
     from tempname_5090_b200.models.train import Trainer
     from tempname_5090_b200._native import check_status
-    cfg = dict(layers=2, hidden=512, ffn=2048, heads=4, sequence=512, micro_batch=2,
+    cfg = dict(layers=2, hidden=1024, ffn=4096, heads=8, sequence=512, micro_batch=2,
                accumulation_steps=1, vocab=4096, chunk_rows=128)
     for arm in ("flux", "flux_taco"):
         model = GPT(cfg, arm=arm, device="cuda", seed=21)

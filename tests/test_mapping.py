@@ -83,3 +83,25 @@ def test_plan_only_for_arrival_arm():
     mutated["arrival_order"] = list(reversed(plan["arrival_order"]))
     with pytest.raises(ValueError):
         mp.schedule(2048, 4096, 512, 8, 128, "flux_taco_interleaved_arrival", mutated)
+
+
+@pytest.mark.parametrize("arm", ["flux", "flux_taco_interleaved"])
+def test_rotated_push_order_is_a_permutation_keeping_within_destination_order(arm):
+    from tempname_5090_b200.parallel import mapping
+    m, n, k, world, chunk = 8192, 4096, 512, 8, 128
+    base = mapping.linear_tile_ids(m, n, k, world, chunk, arm, tile_n=256)
+    per_dest = m // world // 128
+    cols = n // 256
+    firsts = set()
+    for rank in range(world):
+        rot = mapping.linear_tile_ids(m, n, k, world, chunk, arm, tile_n=256, shift=rank + 1)
+        assert sorted(rot) == sorted(base)
+        # position i keeps its within-destination tile; only the destination rotates
+        for a, b in zip(base, rot):
+            ta, tb = a // cols, b // cols
+            assert ta % per_dest == tb % per_dest and a % cols == b % cols
+            assert tb // per_dest == (ta // per_dest + rank + 1) % world
+        firsts.add(rot[0] // cols // per_dest)
+        if arm == "flux":
+            assert rot[-1] // cols // per_dest == rank  # own rows last
+    assert len(firsts) == world  # every rank starts on a different destination
