@@ -211,7 +211,36 @@ __global__ void wait_probe_kernel(const uint32_t* flag, uint32_t target, uint64_
   if (threadIdx.x == 0 && blockIdx.x == 0)
     wait_flag_geq(flag, target, timeout_ns, status, kTimeoutPeerFlag);
 }
+// Grid-stride 16-byte copy with eight loads in flight per thread; `dst` may be
+// a peer's memory (CUDA-IPC mapping): plain stores, no TMA.
+__global__ void __launch_bounds__(256) copy16_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                                     int64_t n16) {
+  constexpr int kUnroll = 8;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < n16; i += kUnroll * stride) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = __ldg(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) dst[i + u * stride] = v[u];
+  }
+  for (; i < n16; i += stride) dst[i] = __ldg(src + i);
+}
 }  // namespace
+
+int copy16(void* dst, const void* src, int64_t bytes, int ctas, cudaStream_t stream) {
+  if (bytes <= 0 || bytes % 16 || (reinterpret_cast<uintptr_t>(dst) & 15) || (reinterpret_cast<uintptr_t>(src) & 15))
+    return -1;
+  if (ctas <= 0) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    ctas = 4 * sms;
+  }
+  copy16_kernel<<<ctas, 256, 0, stream>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), bytes / 16);
+  return int(cudaGetLastError());
+}
 
 int rs_reduce(const RsReduceCall& c, cudaStream_t stream) {
   if (c.rows % 128 || c.n % 128 || c.tile_n % 128 || !c.recv || !c.flags || !c.out) return -1;

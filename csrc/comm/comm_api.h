@@ -37,6 +37,8 @@ int rs_reduce(const RsReduceCall& c, cudaStream_t stream);
 
 namespace tn5b {
 namespace comm {
+// 16-byte-aligned device copy (dst may be a peer's IPC-mapped memory); ctas <= 0: 4 per SM.
+int copy16(void* dst, const void* src, int64_t bytes, int ctas, cudaStream_t stream);
 int wait_probe(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status,
                cudaStream_t stream);
 }  // namespace comm

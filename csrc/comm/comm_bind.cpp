@@ -44,6 +44,15 @@ at::Tensor view_ptr(int64_t ptr, std::vector<int64_t> shape, at::ScalarType dtyp
   return torch::from_blob(reinterpret_cast<void*>(ptr), shape, opts);
 }
 
+// Copy `bytes` from a local CUDA tensor to a raw device pointer (own kernel).
+void copy_to_ptr(int64_t dst, const at::Tensor& src, int64_t bytes, int64_t ctas) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous() && src.numel() * src.element_size() >= bytes);
+  const c10::cuda::CUDAGuard guard(src.device());
+  const int code = tn5b::comm::copy16(reinterpret_cast<void*>(dst), src.data_ptr(), bytes, int(ctas),
+                                      at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(code == 0, "copy_to_ptr failed (", code, ")");
+}
+
 void rs_reduce(int64_t recv, int64_t flags, int64_t slot_bytes, int64_t rank, int64_t world,
                int64_t rows, int64_t n, int64_t tile_n, int64_t chunk_rows, bool quantized,
                int64_t epoch, at::Tensor& out, const c10::optional<at::Tensor>& residual,
@@ -103,4 +112,5 @@ void register_comm(pybind11::module& m) {
   using nogil = pybind11::call_guard<pybind11::gil_scoped_release>;
   m.def("rs_reduce", &rs_reduce, nogil());
   m.def("wait_probe", &wait_probe, nogil());
+  m.def("copy_to_ptr", &copy_to_ptr, nogil());
 }

@@ -6,6 +6,7 @@
     python -m tempname_5090_b200.runner.opbench --op gemm         # 1 GPU: tile kinds vs cuBLAS
     python -m tempname_5090_b200.runner.opbench --op gemm_once --kind 2   # one GEMM (profiler case)
     python -m tempname_5090_b200.runner.opbench --op attn_kernel  # 1 GPU: attention fwd/bwd kernels
+    torchrun ... -m tempname_5090_b200.runner.opbench --op nvlink   # SM-issued peer stores vs local copy
 
 Timing: every iteration is bracketed by CUDA events on the launching stream,
 the L2 is flushed (a 256 MiB write) between iterations outside the events,
@@ -247,9 +248,42 @@ def attention_kernel_case(timer, shapes=((4, 2048, 4), (1, 2048, 32), (4, 2048, 
     return rows
 
 
+def nvlink_case(rank, world, timer, mib=64):
+    """Egress bandwidth of SM-issued 16-byte stores into peers' memory (this
+    framework's copy kernel writing through CUDA-IPC mappings): ring (every rank
+    -> rank+1) and all-to-all (every rank -> every peer, one launch per peer),
+    against a local device copy of the same size."""
+    import torch
+    from .._native import lib
+    from ..parallel.symmetric import SymmetricBuffer
+    nbytes = mib << 20
+    buf = SymmetricBuffer(world * nbytes)
+    src = torch.randn(nbytes // 4, device="cuda")
+    local_dst = torch.empty_like(src)
+    part = (nbytes // (world - 1)) // 16 * 16
+    ring_dst = buf.peers[(rank + 1) % world] + rank * nbytes
+    peers = [buf.peers[p] + rank * nbytes for p in range(world) if p != rank]
+    C = lib()
+
+    def all_to_all():
+        for i, dst in enumerate(peers):
+            C.copy_to_ptr(dst, src[i * part // 4:], part, 0)
+    rows = [dict(op="nvlink", pattern="local_copy", world=world, bytes=nbytes,
+                 us=timer.run(lambda: C.copy_to_ptr(local_dst.data_ptr(), src, nbytes, 0)))]
+    rows.append(dict(op="nvlink", pattern="ring", world=world, bytes=nbytes,
+                     us=timer.run(lambda: C.copy_to_ptr(ring_dst, src, nbytes, 0))))
+    rows.append(dict(op="nvlink", pattern="all_to_all", world=world, bytes=part * (world - 1),
+                     us=timer.run(all_to_all)))
+    for r in rows:
+        r["gbs_per_rank"] = r["bytes"] / r["us"] / 1e3
+    torch.cuda.synchronize()
+    buf.close()
+    return rows
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep", "gemm", "gemm_once", "attn_kernel"),
+    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep", "gemm", "gemm_once", "attn_kernel", "nvlink"),
                     default="gemmrs")
     ap.add_argument("--kind", default="2", help="gemm_once: tile kind 0/1/2/-1 or 'cublas'")
     ap.add_argument("--m", type=int, default=8192)
@@ -280,6 +314,8 @@ def main(argv=None):
         rows += gemm_once(args.m, args.n, args.k, args.kind)
     elif args.op == "attn_kernel":
         rows += attention_kernel_case(timer)
+    elif args.op == "nvlink":
+        rows += nvlink_case(rank, world, timer)
     elif args.op == "attention":
         rows += attention_case(rank, world, timer)
     else:
