@@ -57,6 +57,11 @@ def status_tensor(device):
     """Per-device int32 status word shared by all kernels' bounded waits."""
     import torch
     device = torch.device(device)
+    if device.type == "cpu":  # host-logic tests: a stand-in word nothing writes
+        t = _STATUS.get("cpu")
+        if t is None:
+            t = _STATUS["cpu"] = torch.zeros(4, dtype=torch.int32)
+        return t
     index = device.index if device.index is not None else torch.cuda.current_device()
     t = _STATUS.get(index)
     if t is None:

@@ -48,8 +48,10 @@ class _Lanes:
         key = id(group)
         if key not in cls._cache:
             ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
-            lanes = tuple(dist.new_group(ranks=ranks, backend="nccl") for _ in range(2))
-            streams = tuple(torch.cuda.Stream() for _ in range(2))
+            # Same backend as the parent group (NCCL on GPUs; Gloo for CPU ranks in tests).
+            backend = dist.get_backend(group)
+            lanes = tuple(dist.new_group(ranks=ranks, backend=backend) for _ in range(2))
+            streams = tuple(torch.cuda.Stream() for _ in range(2)) if backend == "nccl" else (None, None)
             cls._cache[key] = (lanes, streams)
         return cls._cache[key]
 
@@ -60,7 +62,7 @@ class RSWorkspace:
     operators may share it: each call is a full exchange, so the parity chain
     argument holds across operators."""
 
-    def __init__(self, m: int, n: int, world: int, group=None, *, recv=None, flags=None):
+    def __init__(self, m: int, n: int, world: int, group=None, *, recv=None, flags=None, device=None):
         self.rows = m // world
         self.slot_bytes = self.rows * n * 2
         self.tiles_per_dest = (self.rows // 128) * (n // TILE_N)
@@ -68,8 +70,8 @@ class RSWorkspace:
             recv = [SymmetricBuffer(world * self.slot_bytes, group) for _ in range(2)]
             flags = SymmetricBuffer(world * self.tiles_per_dest * 4, group)
         self.recv, self.flags = recv, flags
-        self.claims = torch.zeros(self.tiles_per_dest, dtype=torch.int32,
-                                  device=torch.device("cuda", torch.cuda.current_device()))
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        self.claims = torch.zeros(self.tiles_per_dest, dtype=torch.int32, device=device)
         self.epoch = 0
 
     def close(self):
@@ -84,7 +86,7 @@ class GemmRS:
     def __init__(self, m: int, n: int, k: int, group=None, arm: str = "flux", chunk_rows: int = 128,
                  plan=None, transport: str = "nvlink", timeout_ns: int = DEFAULT_TIMEOUT_NS,
                  b_mn: bool = False, workspace: RSWorkspace | None = None,
-                 _emulate: tuple | None = None):
+                 _emulate: tuple | None = None, device: torch.device | None = None):
         if arm not in mapping.ARMS:
             raise ValueError(f"unknown arm {arm}")
         if transport not in ("nvlink", "nccl"):
@@ -103,7 +105,9 @@ class GemmRS:
         self.arrival = arm in mapping.ARRIVAL_ARMS
         self.rows = m // self.world
         self.timeout_ns = int(timeout_ns)
-        self.device = torch.device("cuda", torch.cuda.current_device())
+        # `device` defaults to the current CUDA device; CPU is for host-logic tests
+        # (NCCL transport on Gloo ranks, or a recording stand-in for the kernels).
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.order = mapping.schedule(m, n, k, self.world, chunk_rows, arm, plan)
         # In-kernel pushes start on destination rank+1 (no incast); the NCCL
         # transport keeps the reference CTA map.
@@ -121,7 +125,7 @@ class GemmRS:
         self.workspace = None
         if transport == "nvlink":
             if _emulate is not None:
-                workspace = RSWorkspace(m, n, self.world, recv=_emulate[2], flags=_emulate[3])
+                workspace = RSWorkspace(m, n, self.world, recv=_emulate[2], flags=_emulate[3], device=self.device)
             self.workspace = workspace if workspace is not None else RSWorkspace(m, n, self.world, group)
         else:
             self.lanes, self.lane_streams = _Lanes.get(group)
@@ -238,10 +242,8 @@ class GemmRS:
     def _forward_nccl(self, x, w, b_mn, residual, bias, out):
         from ..ops import gemm as G, taco
         G.matmul(x, w, b_t=b_mn, out=self.partial, tile_order=None)
-        stream = torch.cuda.current_stream()
         per = self.rows // self.chunk_rows
         elements = self.chunk_rows * self.n
-        received = torch.cuda.Event()
         for item in self.order:
             p, dest, within, lane = item["physical"], item["destination"], item["within"], item["lane"]
             block = self.partial.narrow(0, p * self.chunk_rows, self.chunk_rows)

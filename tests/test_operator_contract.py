@@ -1,0 +1,142 @@
+"""Host-side contract of the fused GemmRS operator, on CPU.
+
+1. NVLink transport with a recording stand-in for the native module: per call
+   exactly one producer launch then one receiver launch, both with the call's
+   epoch and the same receive-slot parity; mode and consumer policy per arm; the
+   rotated production order and the unrotated consumer order; a failed launch
+   poisons the operator (later calls raise and launch nothing).
+2. NCCL transport (the reference mechanism: one GEMM, per-block sparse
+   all_to_all on two lane groups, ordered (decode+)reduce) on two Gloo ranks:
+   bitwise equal to the ordered BF16 sum of the sources' partials, with remote
+   blocks through the TACO codec in the quantized arm.
+"""
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+
+M, N, K, CHUNK = 512, 512, 64, 128
+
+
+class _Buf:
+    """Stand-in for a symmetric buffer: a device-pointer table and a local pointer."""
+
+    def __init__(self, tag):
+        self.ptrs = torch.tensor([tag, tag + 1], dtype=torch.int64)
+        self.local = tag
+
+
+class _FakeLib:
+    def __init__(self):
+        self.calls = []
+        self.fail_push = False
+
+    def gemm_rs_push(self, x, a_mn, w, b_mn, mode, recv_ptrs, flag_ptrs, rank, world, chunk_rows, epoch,
+                     slot_bytes, tile_order, status, timeout_ns, max_ctas, delay_tile, delay_ns):
+        if self.fail_push:
+            raise RuntimeError("injected launch failure")
+        self.calls.append(("push", dict(mode=mode, recv=recv_ptrs, flags=flag_ptrs, epoch=epoch,
+                                        order=tile_order.tolist(), rank=rank, world=world)))
+
+    def rs_reduce(self, recv, flags, slot_bytes, rank, world, rows, n, tile_n, chunk_rows, quantized, epoch,
+                  out, residual, bias, order, arrival, claims, status, timeout_ns, max_ctas, stamps):
+        self.calls.append(("reduce", dict(recv=recv, flags=flags, epoch=epoch, quantized=quantized,
+                                          arrival=arrival, claims=claims is not None, order=order.tolist(),
+                                          residual=residual is not None, bias=bias is not None)))
+
+
+@pytest.mark.parametrize("arm", ["flux", "flux_taco", "flux_taco_interleaved", "flux_taco_interleaved_arrival"])
+@pytest.mark.parametrize("rank,world", [(0, 2), (1, 2), (2, 4)])
+def test_nvlink_transport_launch_contract(monkeypatch, arm, rank, world):
+    from tempname_5090_b200.parallel import gemm_rs, mapping, planning
+    fake = _FakeLib()
+    monkeypatch.setattr(gemm_rs, "lib", lambda: fake)
+    monkeypatch.setattr(gemm_rs, "count_launch", lambda n=1: None)
+    plan = planning.make_role(M, N, K, world, CHUNK) if arm.endswith("arrival") else None
+    recv, flags = [_Buf(100), _Buf(200)], _Buf(300)
+    op = gemm_rs.GemmRS(M, N, K, arm=arm, chunk_rows=CHUNK, plan=plan,
+                        _emulate=(rank, world, recv, flags), device="cpu")
+    x = torch.zeros((M, K), dtype=torch.bfloat16)
+    w = torch.zeros((N, K), dtype=torch.bfloat16)
+    quantized = arm in mapping.QUANTIZED_ARMS
+    production = mapping.linear_tile_ids(M, N, K, world, CHUNK, arm, plan, tile_n=256, shift=rank + 1)
+    consumer = mapping.consumer_tile_order(M, N, K, world, CHUNK, arm, rank, plan, 256)
+    for call in range(1, 5):
+        out = op.forward(x, w, residual=torch.zeros((M // world, N), dtype=torch.bfloat16))
+        assert out.shape == (M // world, N)
+        push, reduce = fake.calls[-2], fake.calls[-1]
+        assert [push[0], reduce[0]] == ["push", "reduce"]
+        assert len(fake.calls) == 2 * call  # one producer + one receiver launch per call
+        p, r = push[1], reduce[1]
+        assert p["epoch"] == r["epoch"] == call
+        assert p["recv"] == recv[call & 1].ptrs.data_ptr() and r["recv"] == recv[call & 1].local
+        assert p["flags"] == flags.ptrs.data_ptr() and r["flags"] == flags.local
+        assert p["mode"] == (2 if quantized else 1) and r["quantized"] == quantized
+        assert r["arrival"] == arm.endswith("arrival") and r["claims"] == arm.endswith("arrival")
+        assert p["order"] == production and r["order"] == consumer
+        assert r["residual"] and not r["bias"]
+    # A failed launch poisons the operator: no further launches.
+    fake.fail_push = True
+    with pytest.raises(RuntimeError, match="injected"):
+        op.forward(x, w)
+    fake.fail_push = False
+    before = len(fake.calls)
+    with pytest.raises(RuntimeError, match="previously failed"):
+        op.forward(x, w)
+    assert len(fake.calls) == before and op.failed
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _inputs(rank):
+    g = torch.Generator().manual_seed(40 + rank)
+    x = torch.randn((M, K), generator=g).to(torch.bfloat16)
+    w = (0.1 * torch.randn((N, K), generator=g)).to(torch.bfloat16)
+    return x, w
+
+
+def _nccl_worker(rank, world, port, out_dir, arm):
+    import torch.distributed as dist
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        op = GemmRS(M, N, K, arm=arm, chunk_rows=CHUNK, transport="nccl", device="cpu")
+        x, w = _inputs(rank)
+        outs = [op.forward(x, w).clone() for _ in range(2)]
+        torch.save(dict(outs=outs, state=op.state()), os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("arm", ["flux", "flux_taco"])
+def test_nccl_transport_two_gloo_ranks_match_ordered_sum(arm):
+    import torch.multiprocessing as mp
+    from tempname_5090_b200.ops import taco
+    from tempname_5090_b200.ops.gemm import matmul
+    world = 2
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_nccl_worker, args=(world, _free_port(), d, arm), nprocs=world, join=True)
+        res = [torch.load(os.path.join(d, f"rank{r}.pt")) for r in range(world)]
+    partials = [matmul(*_inputs(s)) for s in range(world)]
+    rows = M // world
+    for r in range(world):
+        sources = []
+        for s in range(world):
+            part = partials[s][r * rows:(r + 1) * rows]
+            if arm == "flux_taco" and s != r:
+                blocks = [taco.decode_cpu(taco.encode_cpu(part[b:b + CHUNK]), CHUNK * N)
+                          for b in range(0, rows, CHUNK)]
+                part = torch.cat(blocks).reshape(rows, N)
+            sources.append(part.reshape(-1))
+        want = taco.ordered_sum_cpu(sources).reshape(rows, N)
+        for got in res[r]["outs"]:
+            assert torch.equal(got, want)
+        assert res[r]["state"]["calls"] == 2 and res[r]["state"]["reduction_order"] == list(range(world))
