@@ -38,6 +38,7 @@ from ..ops import gemm as G
 from ..ops import loss as CE
 from ..ops import norm as N
 from ..parallel.tp import TensorParallel
+from ..utils import tracing
 
 ALIGN = 64  # elements; keeps every parameter view 128-byte aligned
 
@@ -219,20 +220,8 @@ class GPT:
         E.add_position(x, self.p["position"], row0)
         saved = []
         for i in range(c["layers"]):
-            p = f"layers.{i}."
-            x_in = x
-            ln1, mean1, rstd1 = N.layer_norm_fwd(x_in, self.p[p + "ln1_weight"], self.p[p + "ln1_bias"], self.eps)
-            qkv, ln1_full = tp.ag_linear(("qkv", i), ln1, self.p[p + "qkv_weight"], bias=self.p[p + "qkv_bias"])
-            attn, lse = A.forward(qkv, c["micro_batch"], c["sequence"], lh)
-            x2 = tp.linear_rs(attn, self.p[p + "attn_weight"], residual=x_in, bias=self.p[p + "attn_bias"],
-                              role="attn")
-            ln2, mean2, rstd2 = N.layer_norm_fwd(x2, self.p[p + "ln2_weight"], self.p[p + "ln2_bias"], self.eps)
-            pre = torch.empty((M, self.f // self.world), dtype=torch.bfloat16, device=self.device)
-            act, ln2_full = tp.ag_linear(("fc1", i), ln2, self.p[p + "fc1_weight"], bias=self.p[p + "fc1_bias"],
-                                         gelu_aux=pre)
-            x = tp.linear_rs(act, self.p[p + "fc2_weight"], residual=x2, bias=self.p[p + "fc2_bias"], role="mlp")
-            if keep:
-                saved.append((x_in, mean1, rstd1, ln1_full, qkv, attn, lse, x2, mean2, rstd2, ln2_full, pre, act))
+            with tracing.scope(f"gpt.layer{i}.forward"):
+                x = self._layer_forward(i, x, saved, keep)
         x_final = x
         lnf, meanf, rstdf = N.layer_norm_fwd(x_final, self.p["final_weight"], self.p["final_bias"], self.eps)
         logits, lnf_full = tp.ag_linear(("head", 0), lnf, self.p["embedding"])
@@ -240,6 +229,60 @@ class GPT:
         self.forward_calls += 1
         tape = (tokens, targets, saved, x_final, meanf, rstdf, lnf_full, logits, ce_state) if keep else None
         return loss, tape
+
+    def _layer_forward(self, i, x, saved, keep):
+        """One transformer block forward (pre-LN); appends its tape when `keep`."""
+        c, tp, M = self.config, self.tp, self.M
+        lh = self.lh
+        p = f"layers.{i}."
+        x_in = x
+        ln1, mean1, rstd1 = N.layer_norm_fwd(x_in, self.p[p + "ln1_weight"], self.p[p + "ln1_bias"], self.eps)
+        qkv, ln1_full = tp.ag_linear(("qkv", i), ln1, self.p[p + "qkv_weight"], bias=self.p[p + "qkv_bias"])
+        attn, lse = A.forward(qkv, c["micro_batch"], c["sequence"], lh)
+        x2 = tp.linear_rs(attn, self.p[p + "attn_weight"], residual=x_in, bias=self.p[p + "attn_bias"],
+                          role="attn")
+        ln2, mean2, rstd2 = N.layer_norm_fwd(x2, self.p[p + "ln2_weight"], self.p[p + "ln2_bias"], self.eps)
+        pre = torch.empty((M, self.f // self.world), dtype=torch.bfloat16, device=self.device)
+        act, ln2_full = tp.ag_linear(("fc1", i), ln2, self.p[p + "fc1_weight"], bias=self.p[p + "fc1_bias"],
+                                     gelu_aux=pre)
+        x = tp.linear_rs(act, self.p[p + "fc2_weight"], residual=x2, bias=self.p[p + "fc2_bias"], role="mlp")
+        if keep:
+            saved.append((x_in, mean1, rstd1, ln1_full, qkv, attn, lse, x2, mean2, rstd2, ln2_full, pre, act))
+        return x
+
+    def _layer_backward(self, i, tape, dx, ln_ws, col_ws):
+        """One transformer block backward: writes its parameter gradients and
+        returns the gradient of its input."""
+        c, tp, g = self.config, self.tp, self.g
+        p = f"layers.{i}."
+        (x_in, mean1, rstd1, ln1_full, qkv, attn, lse, x2, mean2, rstd2, ln2_full, pre, act) = tape
+        # fc2 (row-parallel): x = x2 + RS(act @ Wfc2^T) + b
+        N.column_sum(dx, out=g[p + "fc2_bias"], workspace=col_ws)
+        dpre, dfull = tp.ag_linear(("fc2_bwd", i % 2), dx, self.p[p + "fc2_weight"], b_mn=True,
+                                   gelu_grad_of=pre)
+        G.matmul(dfull, act, a_t=True, b_t=True, out=g[p + "fc2_weight"])
+        # fc1 (column-parallel): pre = gather(ln2) @ Wfc1^T + b
+        N.column_sum(dpre, out=g[p + "fc1_bias"], workspace=col_ws)
+        dln2 = tp.linear_rs(dpre, self.p[p + "fc1_weight"], b_mn=True, role="mlp_bwd")
+        G.matmul(dpre, ln2_full, a_t=True, b_t=True, out=g[p + "fc1_weight"])
+        dx2, dw2, db2 = N.layer_norm_bwd(dln2, x2, self.p[p + "ln2_weight"], mean2, rstd2, dres=dx,
+                                         workspace=ln_ws)
+        g[p + "ln2_weight"].copy_(dw2)
+        g[p + "ln2_bias"].copy_(db2)
+        # attention out-projection (row-parallel): x2 = x_in + RS(attn @ Wattn^T) + b
+        N.column_sum(dx2, out=g[p + "attn_bias"], workspace=col_ws)
+        dattn, dfull2 = tp.ag_linear(("attn_bwd", i % 2), dx2, self.p[p + "attn_weight"], b_mn=True)
+        G.matmul(dfull2, attn, a_t=True, b_t=True, out=g[p + "attn_weight"])
+        dqkv = A.backward(qkv, attn, dattn, lse, c["micro_batch"], c["sequence"], self.lh)
+        # QKV (column-parallel)
+        N.column_sum(dqkv, out=g[p + "qkv_bias"], workspace=col_ws)
+        dln1 = tp.linear_rs(dqkv, self.p[p + "qkv_weight"], b_mn=True, role="attn_bwd")
+        G.matmul(dqkv, ln1_full, a_t=True, b_t=True, out=g[p + "qkv_weight"])
+        dx, dw1, db1 = N.layer_norm_bwd(dln1, x_in, self.p[p + "ln1_weight"], mean1, rstd1, dres=dx2,
+                                        workspace=ln_ws)
+        g[p + "ln1_weight"].copy_(dw1)
+        g[p + "ln1_bias"].copy_(db1)
+        return dx
 
     @torch.no_grad()
     def loss(self, tokens, targets) -> torch.Tensor:
@@ -273,34 +316,8 @@ class GPT:
         g["final_weight"].copy_(dwf)
         g["final_bias"].copy_(dbf)
         for i in reversed(range(c["layers"])):
-            p = f"layers.{i}."
-            (x_in, mean1, rstd1, ln1_full, qkv, attn, lse, x2, mean2, rstd2, ln2_full, pre, act) = saved[i]
-            # fc2 (row-parallel): x = x2 + RS(act @ Wfc2^T) + b
-            N.column_sum(dx, out=g[p + "fc2_bias"], workspace=col_ws)
-            dpre, dfull = tp.ag_linear(("fc2_bwd", i % 2), dx, self.p[p + "fc2_weight"], b_mn=True,
-                                       gelu_grad_of=pre)
-            G.matmul(dfull, act, a_t=True, b_t=True, out=g[p + "fc2_weight"])
-            # fc1 (column-parallel): pre = gather(ln2) @ Wfc1^T + b
-            N.column_sum(dpre, out=g[p + "fc1_bias"], workspace=col_ws)
-            dln2 = tp.linear_rs(dpre, self.p[p + "fc1_weight"], b_mn=True, role="mlp_bwd")
-            G.matmul(dpre, ln2_full, a_t=True, b_t=True, out=g[p + "fc1_weight"])
-            dx2, dw2, db2 = N.layer_norm_bwd(dln2, x2, self.p[p + "ln2_weight"], mean2, rstd2, dres=dx,
-                                             workspace=ln_ws)
-            g[p + "ln2_weight"].copy_(dw2)
-            g[p + "ln2_bias"].copy_(db2)
-            # attention out-projection (row-parallel): x2 = x_in + RS(attn @ Wattn^T) + b
-            N.column_sum(dx2, out=g[p + "attn_bias"], workspace=col_ws)
-            dattn, dfull2 = tp.ag_linear(("attn_bwd", i % 2), dx2, self.p[p + "attn_weight"], b_mn=True)
-            G.matmul(dfull2, attn, a_t=True, b_t=True, out=g[p + "attn_weight"])
-            dqkv = A.backward(qkv, attn, dattn, lse, c["micro_batch"], c["sequence"], self.lh)
-            # QKV (column-parallel)
-            N.column_sum(dqkv, out=g[p + "qkv_bias"], workspace=col_ws)
-            dln1 = tp.linear_rs(dqkv, self.p[p + "qkv_weight"], b_mn=True, role="attn_bwd")
-            G.matmul(dqkv, ln1_full, a_t=True, b_t=True, out=g[p + "qkv_weight"])
-            dx, dw1, db1 = N.layer_norm_bwd(dln1, x_in, self.p[p + "ln1_weight"], mean1, rstd1, dres=dx2,
-                                            workspace=ln_ws)
-            g[p + "ln1_weight"].copy_(dw1)
-            g[p + "ln1_bias"].copy_(db1)
+            with tracing.scope(f"gpt.layer{i}.backward"):
+                dx = self._layer_backward(i, saved[i], dx, ln_ws, col_ws)
         # value = scatter_sum(embedding contributions) + position
         E.position_grad(dx, c["sequence"], self.rank * self.Ml, out=g["position"])
         dcontrib = tp.gather_rows(dx)

@@ -21,6 +21,7 @@ import torch
 from .._native import check_status
 from ..ops import optim as O
 from .gpt import GPT
+from ..utils import tracing
 
 
 class Trainer:
@@ -51,11 +52,20 @@ class Trainer:
         if len(batches) != self.acc:
             raise ValueError(f"expected {self.acc} micro-batches")
         self.loss_sum.zero_()
-        for tokens, labels in batches:
-            loss = model.forward_backward(tokens, labels, loss_scale=1.0 / self.acc)
-            self.loss_sum.add_(loss.reshape(()) / self.acc)
-            if self.grad32 is not None:
-                self.grad32.add_(st.grad)
+        for mb, (tokens, labels) in enumerate(batches):
+            with tracing.scope(f"trainer.micro_batch{mb}"):
+                loss = model.forward_backward(tokens, labels, loss_scale=1.0 / self.acc)
+                self.loss_sum.add_(loss.reshape(()) / self.acc)
+                if self.grad32 is not None:
+                    self.grad32.add_(st.grad)
+        with tracing.scope("trainer.optimizer"):
+            self._optimizer_step()
+        return self.loss_sum, self.norm2
+
+    def _optimizer_step(self):
+        """Replicated-gradient all-reduce, global norm (FP64, replicated counted
+        once), clipped FP32-master AdamW on sharded and replicated parameters."""
+        model, st = self.model, self.model.store
         sh = st.sharded_end
         if self.grad32 is not None:
             sharded = self.grad32[:sh]
@@ -78,7 +88,6 @@ class Trainer:
                 st.replicated_decay_end - sh, self.norm2, **common)
         if self.grad32 is not None:
             self.grad32.zero_()
-        return self.loss_sum, self.norm2
 
     def train_step(self, host_batches):
         """Public one-call step: copies each micro-batch's (tokens, labels) from

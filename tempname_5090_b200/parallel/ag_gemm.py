@@ -26,6 +26,7 @@ import torch.distributed as dist
 from .._native import count_launch, lib, status_tensor
 from ..ops import gemm as G
 from .symmetric import SymmetricBuffer
+from ..utils import tracing
 
 DEFAULT_TIMEOUT_NS = 10_000_000_000
 
@@ -99,10 +100,11 @@ class AGGemm:
         if gelu_grad_of is not None:
             epi |= G.EPI_GELU_BWD
             aux = gelu_grad_of
-        lib().ag_gemm(shard.contiguous(), self.gathered, w, b_mn, out, epi, bias, aux,
-                      self.gather.ptrs.data_ptr(), self.flags.ptrs.data_ptr(), self.flags.local,
-                      self.rank, self.world, self.flag_total, self._order(n, bn), self.status,
-                      self.timeout_ns, bn)
+        with tracing.scope("ag_gemm"):
+            lib().ag_gemm(shard.contiguous(), self.gathered, w, b_mn, out, epi, bias, aux,
+                          self.gather.ptrs.data_ptr(), self.flags.ptrs.data_ptr(), self.flags.local,
+                          self.rank, self.world, self.flag_total, self._order(n, bn), self.status,
+                          self.timeout_ns, bn)
         count_launch()
         self.calls += 1
         return out

@@ -34,6 +34,7 @@ import torch.distributed as dist
 from .._native import count_launch, lib, status_tensor
 from . import mapping
 from .symmetric import SymmetricBuffer
+from ..utils import tracing
 
 TILE_N = 256
 DEFAULT_TIMEOUT_NS = 10_000_000_000
@@ -172,10 +173,13 @@ class GemmRS:
         self.epoch += 1
         try:
             if self.transport == "nvlink":
-                self.push(x, w, b_mn)
-                self.reduce(out, residual, bias)
+                with tracing.scope("gemm_rs.push"):
+                    self.push(x, w, b_mn)
+                with tracing.scope("gemm_rs.reduce"):
+                    self.reduce(out, residual, bias)
             else:
-                self._forward_nccl(x, w, b_mn, residual, bias, out)
+                with tracing.scope("gemm_rs.nccl"):
+                    self._forward_nccl(x, w, b_mn, residual, bias, out)
         except BaseException:
             self.failed = True
             raise

@@ -13,6 +13,7 @@ from __future__ import annotations
 import math
 import random
 import statistics
+import hashlib
 from pathlib import Path
 
 from . import protocol as P
@@ -94,6 +95,11 @@ def replay(root) -> dict:
         rows = [P.read(directory / f"rank{r}.json") for r in range(config["world_size"])]
         cfg = P.config_for_job(config, job, execution_plan) if job["stage"] in ("operator", "train") else config
         P.validate_rows(rows, job, cfg)
+        for row in rows:
+            trace = row.get("trace")
+            if trace:  # optional profiler trace: the file must still hash to the recorded digest
+                data = (directory / trace["path"]).read_bytes()
+                P.require(hashlib.sha256(data).hexdigest() == trace["sha256"], "trace file differs from its digest")
         if job["stage"] == "calibrate":
             execution_plan = P.calibration_from_rows(rows, config)
             P.require(P.digest(execution_plan) == plan.get("execution_plan_sha256", P.digest(execution_plan)),

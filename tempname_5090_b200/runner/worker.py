@@ -218,7 +218,7 @@ def arrival_diagnostic(op, x, w, expected, group, delay_ns: int = 20_000_000) ->
 
 
 # ---------------------------------------------------------------------- train
-def train(config: dict, arm: str, rank: int, world: int, group) -> dict:
+def train(config: dict, arm: str, rank: int, world: int, group, out_dir=None) -> dict:
     import torch
     from ..config import parameter_counts
     from ..models.gpt import GPT
@@ -253,8 +253,18 @@ def train(config: dict, arm: str, rank: int, world: int, group) -> dict:
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    trace = None
+    if config.get("profile") and out_dir is not None:
+        # One extra, untimed step under the profiler with the named scopes on.
+        from ..utils import tracing
+        acts = [torch.profiler.ProfilerActivity.CPU, torch.profiler.ProfilerActivity.CUDA]
+        with tracing.enabled(), torch.profiler.profile(activities=acts) as prof:
+            trainer.step(batches)
+            torch.cuda.synchronize()
+        path, sha = tracing.export(prof, Path(out_dir) / f"trace_rank{rank}.json")
+        trace = dict(path=Path(path).name, sha256=sha, untimed=True)
     counts = parameter_counts(c, world)
-    row = dict(timed_steps=timing["timed_steps"], warmup_steps=timing["warmup_steps"], step_ms=float(t.item()),
+    row = dict(trace=trace, timed_steps=timing["timed_steps"], warmup_steps=timing["warmup_steps"], step_ms=float(t.item()),
                losses=losses, grad_norms=norms, tokens_per_step=c["sequence"] * c["micro_batch"] * c["accumulation_steps"],
                initialization_sha256=init_sha, input_sha256=input_sha, final_parameters_sha256=tensor_sha(model.store.flat),
                parameters_per_rank=counts["parameters_per_rank"], parameter_counts=counts, dtype="bfloat16",
@@ -296,7 +306,7 @@ def main(argv=None):
         elif args.stage == "operator":
             row.update(operators(config, args.arm, rank, world, group))
         else:
-            row.update(train(config, args.arm, rank, world, group))
+            row.update(train(config, args.arm, rank, world, group, args.out))
         torch.cuda.synchronize()
         row.update(completed=True, passed=True)
         P.write(args.out / f"rank{rank}.json", row)

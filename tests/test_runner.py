@@ -127,6 +127,54 @@ def test_replay_rejects_tampering(tmp_path):
         R.replay(out)
 
 
+def _edit(path, fn):
+    row = json.loads(Path(path).read_text())
+    fn(row)
+    Path(path).write_text(json.dumps(row))
+
+
+def _add_trace(run, directory, tamper):
+    d = run / directory
+    (d / "trace_rank0.json").write_text('{"traceEvents": []}')
+    sha = hashlib.sha256((d / "trace_rank0.json").read_bytes()).hexdigest()
+    _edit(d / "rank0.json", lambda r: r.update(trace=dict(path="trace_rank0.json", sha256=sha, untimed=True)))
+    if tamper:
+        (d / "trace_rank0.json").write_text('{"traceEvents": [{"name": "x"}]}')
+
+
+TAMPERS = {
+    "missing_rank": lambda run: (run / "operator/trial1/block003-flux/rank1.json").unlink(),
+    "run_id": lambda run: _edit(run / "train/trial1/block000-flux/rank0.json", lambda r: r.update(run_id="other")),
+    "arm_swap": lambda run: _edit(run / "train/trial1/block001-flux_taco/rank1.json", lambda r: r.update(arm="flux")),
+    "failed_rank": lambda run: _edit(run / "operator/trial1/block002-flux/rank0.json", lambda r: r.update(passed=False)),
+    "negative_step_time": lambda run: _edit(run / "train/trial1/block002-flux/rank1.json",
+                                            lambda r: r.update(step_ms=-1.0)),
+    "short_losses": lambda run: _edit(run / "train/trial1/block004-flux/rank0.json",
+                                      lambda r: r.update(losses=r["losses"][:-1])),
+    "plan_digest": lambda run: _edit(run / "train/trial1/block005-flux/rank0.json",
+                                     lambda r: r.update(execution_plan_sha256="0" * 64)),
+    "frozen_plan_digest": lambda run: _edit(run / "plan.json", lambda p: p.update(execution_plan_sha256="0" * 64)),
+    "taco_trajectory": lambda run: _edit(run / "train/trial1/block006-flux_taco_interleaved/rank0.json",
+                                         lambda r: r.update(final_parameters_sha256=_hash("different"))),
+    "trace_bytes": lambda run: _add_trace(run, "train/trial1/block007-flux", tamper=True),
+}
+
+
+@pytest.mark.parametrize("name", sorted(TAMPERS))
+def test_replay_rejects_each_tamper(tmp_path, name):
+    out = C.execute(_args(tmp_path), launcher=_fake_launcher(2))
+    R.replay(out)  # intact run replays
+    TAMPERS[name](out)
+    with pytest.raises((ValueError, FileNotFoundError, KeyError)):
+        R.replay(out)
+
+
+def test_replay_accepts_an_intact_trace(tmp_path):
+    out = C.execute(_args(tmp_path), launcher=_fake_launcher(2))
+    _add_trace(out, "train/trial1/block007-flux", tamper=False)
+    R.replay(out)
+
+
 def test_taco_trajectory_mismatch_fails_the_run(tmp_path):
     calls = {"n": 0}
     base = _fake_launcher(2)
