@@ -153,3 +153,40 @@ def test_bounded_wait_times_out_and_context_survives():
     x = torch.ones(8, device="cuda")
     assert x.sum().item() == 8.0  # context still usable
     check_status()
+
+
+@pytest.mark.parametrize("arm", ["flux", "flux_taco"])
+def test_guard_regions_stay_intact_and_detect_an_overrun(arm):
+    """Guarded receive slots and flags around emulated GemmRS calls: every
+    rank's guards keep their pattern; a byte written into a guard (on purpose,
+    from the host side) is reported for that rank."""
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    from tempname_5090_b200._native import check_status, lib
+    world, m, n, k = 4, 1024, 512, 256
+    rows = m // world
+    g = 4096
+    recv = [SymmetricBuffer(world * rows * n * 2, guard_bytes=g, _emulate_world=world) for _ in range(2)]
+    flags = SymmetricBuffer(world * (rows // 128) * (n // 256) * 4, guard_bytes=g, _emulate_world=world)
+    ops = [GemmRS(m, n, k, arm=arm, _emulate=(r, world, [b.as_rank(r) for b in recv], flags.as_rank(r)))
+           for r in range(world)]
+    xs = [torch.randn((m, k), generator=_gen(r), device="cuda").to(torch.bfloat16) for r in range(world)]
+    ws = [(0.05 * torch.randn((n, k), generator=_gen(50 + r), device="cuda")).to(torch.bfloat16) for r in range(world)]
+    for _ in range(3):
+        for op in ops:
+            op.begin()
+        for r, op in enumerate(ops):
+            op.push(xs[r], ws[r])
+        for op in ops:
+            op.reduce(torch.empty((rows, n), dtype=torch.bfloat16, device="cuda"))
+    torch.cuda.synchronize()
+    check_status()
+    assert all(b.check_guards() == [] for b in recv + [flags])
+    # Corrupt the trailing guard of rank 2's flag region and the leading guard of rank 1's slot 0.
+    lib().view_ptr(flags.peers[2] + flags.nbytes + 7, [1], torch.uint8, 0).fill_(0)
+    lib().view_ptr(recv[0].peers[1] - 1, [1], torch.uint8, 0).fill_(0)
+    assert flags.check_guards() == [2]
+    assert recv[0].check_guards() == [1]
+    assert recv[1].check_guards() == []
+    for b in recv + [flags]:
+        b.close()
