@@ -5,7 +5,7 @@
     python -m tempname_5090_b200.runner.controller --execute --background --out DIR
     python -m tempname_5090_b200.runner.controller --report DIR         # read-only replay
 
-Each job runs as `torch.distributed.run --standalone --nnodes=1 --nproc-per-node W
+Each job runs as `torch.distributed.run --standalone --local-addr 127.0.0.1 --nnodes=1 --nproc-per-node W
 -m tempname_5090_b200.runner.worker ...` in its own process group with a
 timeout (SIGTERM, then SIGKILL of that group only).  After every job the
 per-rank rows are validated; the calibration plan is frozen into
@@ -96,7 +96,9 @@ def snapshot_sources(out: Path) -> dict:
 
 
 def command_for(python: str, directory: Path, job: dict, world: int) -> list:
-    return [python, "-m", "torch.distributed.run", "--standalone", "--nnodes=1", f"--nproc-per-node={world}",
+    # Loopback rendezvous: the host name of a container need not resolve.
+    return [python, "-m", "torch.distributed.run", "--standalone", "--local-addr", "127.0.0.1", "--nnodes=1",
+            f"--nproc-per-node={world}",
             "-m", "tempname_5090_b200.runner.worker", "--config", str(directory / "config.json"),
             "--out", str(directory), "--stage", job["stage"], "--arm", job["arm"]]
 
