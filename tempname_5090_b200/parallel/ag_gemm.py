@@ -48,7 +48,7 @@ def ag_tile_order(m: int, n: int, world: int, rank: int, bn: int) -> list:
 
 class AGGemm:
     def __init__(self, m: int, k: int, group=None, timeout_ns: int = DEFAULT_TIMEOUT_NS,
-                 _emulate: tuple | None = None):
+                 _emulate: tuple | None = None, device: torch.device | None = None):
         if _emulate is not None:
             self.rank, self.world, self.gather, self.flags = _emulate
         else:
@@ -58,7 +58,8 @@ class AGGemm:
         if k % 8:
             raise ValueError("K must be a multiple of 8")
         self.m, self.k, self.group = m, k, group
-        self.device = torch.device("cuda", torch.cuda.current_device())
+        # `device` defaults to the current CUDA device; CPU serves host-logic tests.
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.timeout_ns = int(timeout_ns)
         if _emulate is None:
             self.gather = SymmetricBuffer(m * k * 2, group)

@@ -1,4 +1,4 @@
-"""Host-side contract of the fused GemmRS operator, on CPU.
+"""Host-side contract of the fused operators (GemmRS, AG->GEMM), on CPU.
 
 1. NVLink transport with a recording stand-in for the native module: per call
    exactly one producer launch then one receiver launch, both with the call's
@@ -9,6 +9,9 @@
    all_to_all on two lane groups, ordered (decode+)reduce) on two Gloo ranks:
    bitwise equal to the ordered BF16 sum of the sources' partials, with remote
    blocks through the TACO codec in the quantized arm.
+3. AG->GEMM with a recording stand-in: cumulative chunk-flag targets (every
+   CTA of every call bumps each owner's counter once), epilogue bits, own row
+   chunk first in the tile order, shard-shape checks.
 """
 import os
 import socket
@@ -140,3 +143,60 @@ def test_nccl_transport_two_gloo_ranks_match_ordered_sum(arm):
         for got in res[r]["outs"]:
             assert torch.equal(got, want)
         assert res[r]["state"]["calls"] == 2 and res[r]["state"]["reduction_order"] == list(range(world))
+
+
+class _FakeAGLib:
+    def __init__(self, grid):
+        self.grid = grid
+        self.calls = []
+
+    def gemm_grid(self, m, n, bn, mode):
+        return self.grid
+
+    def ag_gemm(self, shard, gather, w, b_mn, out, epi, bias, aux, gather_ptrs, flag_ptrs, local_flags,
+                rank, world, target, tile_order, status, timeout_ns, bn):
+        self.calls.append(dict(epi=epi, rank=rank, world=world, target=target, order=tile_order.tolist(),
+                               bn=bn, b_mn=b_mn, aux=aux is not None, bias=bias is not None,
+                               local_flags=local_flags, gather_ptrs=gather_ptrs))
+
+
+class _AGBuf(_Buf):
+    def __init__(self, tag, m=1, k=1):
+        super().__init__(tag)
+        self._m, self._k = m, k
+
+    def local_view(self, shape, dtype, offset=0):
+        return torch.zeros(shape, dtype=dtype)
+
+
+@pytest.mark.parametrize("rank,world", [(0, 2), (3, 4), (5, 8)])
+def test_ag_gemm_launch_contract(monkeypatch, rank, world):
+    from tempname_5090_b200.parallel import ag_gemm
+    from tempname_5090_b200.ops import gemm as G
+    fake = _FakeAGLib(grid=148)
+    monkeypatch.setattr(ag_gemm, "lib", lambda: fake)
+    monkeypatch.setattr(ag_gemm, "count_launch", lambda n=1: None)
+    m, k, n = 128 * world * 2, 256, 1024
+    gather, flags = _AGBuf(500), _AGBuf(600)
+    op = ag_gemm.AGGemm(m, k, _emulate=(rank, world, gather, flags), device="cpu")
+    shard = torch.zeros((m // world, k), dtype=torch.bfloat16)
+    w = torch.zeros((n, k), dtype=torch.bfloat16)
+    aux = torch.zeros((m, n), dtype=torch.bfloat16)
+    op.forward(shard, w, bias=torch.zeros(n, dtype=torch.bfloat16))
+    op.forward(shard, w, gelu_aux=aux)
+    op.forward(shard, w.t().contiguous(), b_mn=True, gelu_grad_of=aux)
+    c = fake.calls
+    # Cumulative chunk-flag targets: every CTA of every call bumps each owner's counter once.
+    assert [x["target"] for x in c] == [148, 296, 444]
+    assert [x["epi"] for x in c] == [G.EPI_BIAS, G.EPI_GELU, G.EPI_GELU_BWD]
+    assert [x["aux"] for x in c] == [False, True, True] and [x["b_mn"] for x in c] == [False, False, True]
+    # Own chunk first, then rank+1, ...: the first tiles need no peer data.
+    order = c[0]["order"]
+    tiles_n = (n + c[0]["bn"] - 1) // c[0]["bn"]
+    per = m // world // 128
+    first_rows = {tid // tiles_n for tid in order[:per * tiles_n]}
+    assert first_rows == set(range(rank * per, (rank + 1) * per))
+    assert sorted(order) == list(range(len(order)))
+    assert all(x["local_flags"] == flags.local and x["gather_ptrs"] == gather.ptrs.data_ptr() for x in c)
+    with pytest.raises(ValueError):
+        op.forward(torch.zeros((m // world + 128, k), dtype=torch.bfloat16), w)
