@@ -34,6 +34,7 @@ def lib():
     with _LOCK:
         if _LIB is None:
             try:
+                import torch  # noqa: F401  (loads the libraries the extension links against)
                 from . import _C  # type: ignore
                 _LIB = _C
             except Exception as exc:  # pragma: no cover - depends on build state
