@@ -250,7 +250,7 @@ int run(const GemmCall& c, cudaStream_t stream) {
     case 1:
       return launch<256, 4, 64, kModeRsPush, false>(c, p, ma, mb, mo, grid, stream);
     case 2:
-      return launch<256, 3, 128, kModeRsTaco, false>(c, p, ma, mb, mo, grid, stream);
+      return launch<256, 4, 128, kModeRsTaco, false>(c, p, ma, mb, mo, grid, stream);
     default:
       return fail("gemm: unknown mode");
   }
