@@ -152,15 +152,20 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
     return;
   }
   // Arrival-first: lane = parity of the tile's block-within-destination.  All
-  // threads scan the lane's unclaimed tiles in parallel; the earliest ready one
-  // (in the consumer order) is claimed with a CAS tagged with the epoch.
+  // threads scan the lane's unclaimed tiles in parallel; the CTA claims (CAS
+  // tagged with the epoch) the first ready tile at or after its own starting
+  // position in the consumer order, cyclically.  The starting positions of the
+  // lane's CTAs are spread evenly over the order, so CTAs do not all race for
+  // the same tile.
   const int lane_id = blockIdx.x & 1;
+  const int lane_ctas = max(1, int(gridDim.x) >> 1);
+  const int origin = int((int64_t(blockIdx.x >> 1) * tiles) / lane_ctas);
   const uint64_t start = globaltimer_ns();
   __shared__ int s_best;
   for (;;) {
     if (threadIdx.x == 0) s_best = 0x7fffffff;
     __syncthreads();
-    int best = 0x7fffffff, open = 0;
+    int best = 0x7fffffff, open = 0;  // best: cyclic distance from `origin`
     for (int i = threadIdx.x; i < tiles; i += kThreads) {
       const int tile = c.tile_order ? c.tile_order[i] : i;
       const int blk = (tile / tiles_n) * 128 / c.chunk_rows;
@@ -168,7 +173,8 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
       const int old = *reinterpret_cast<volatile int*>(c.claims + tile);
       if (int32_t(uint32_t(old) - c.epoch) >= 0) continue;  // already taken this epoch
       open = 1;
-      if (best == 0x7fffffff && tile_ready(c, tile, tiles)) best = i;
+      const int dist = (i - origin + tiles) % tiles;
+      if (dist < best && tile_ready(c, tile, tiles)) best = dist;
     }
     if (best != 0x7fffffff) atomicMin(&s_best, best);
     const int any_open = __syncthreads_or(open);
@@ -177,7 +183,8 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
       if (!any_open) {
         found = -2;  // lane drained
       } else if (s_best != 0x7fffffff) {
-        const int tile = c.tile_order ? c.tile_order[s_best] : s_best;
+        const int pos = (origin + s_best) % tiles;
+        const int tile = c.tile_order ? c.tile_order[pos] : pos;
         const int old = *reinterpret_cast<volatile int*>(c.claims + tile);
         // tile_ready is this thread's own acquire of the flags (monotonic epochs:
         // ready for the scanning thread implies ready here).
