@@ -155,6 +155,83 @@ def confirmed(record, minimum_gain):
             and all(r["fractional_gain"] > minimum_gain for r in record["paired_samples"]))
 
 
+def replay_role_evidence(plan, m, n, k, world, chunk_rows) -> dict:
+    """Re-derive a frozen role plan's decision from its recorded raw samples.
+
+    Checks, from the plan's diagnostics alone: every pair gain and every
+    record's geometric-mean gain recomputed from the recorded seconds; AB/BA
+    alternation; each training record compares the identity order with the
+    candidate of that name (digests); the proposed candidate is the best
+    training gain above the bar; confirmation uses disjoint seeds and the
+    acceptance rule; the frozen order is the accepted candidate's order or the
+    identity.  Returns the recomputed summary; raises ValueError on any
+    mismatch.  Mirrors TempName-5090 tools/5090/report.py:214-269."""
+    plan = validate_role_plan(plan, m, n, k, world, chunk_rows)
+    diag = plan.get("diagnostics") or {}
+    cfg = settings(diag.get("settings"))
+    arr = diag.get("arrival")
+    if not isinstance(arr, dict):
+        raise ValueError("plan has no arrival calibration evidence")
+    identity = make_role(m, n, k, world, chunk_rows)
+    cands = {c["name"]: make_role(m, n, k, world, chunk_rows, c["arrival_order"])
+             for c in candidates(m, n, k, world, chunk_rows)[1:]}
+
+    def check_record(rec, name, phase, pairs):
+        if rec.get("name") != name or rec.get("phase") != phase:
+            raise ValueError("calibration record identity mismatch")
+        samples = rec.get("paired_samples")
+        if not isinstance(samples, list) or len(samples) != pairs:
+            raise ValueError("wrong number of calibration pairs")
+        logs = []
+        for i, smp in enumerate(samples):
+            want_order = ["reference", "candidate"] if i % 2 == 0 else ["candidate", "reference"]
+            if smp.get("pair") != i or smp.get("execution_order") != want_order:
+                raise ValueError("calibration pairs are not AB/BA alternated")
+            ref_s, cand_s = _elapsed(smp.get("reference_seconds")), _elapsed(smp.get("candidate_seconds"))
+            if abs((1 - cand_s / ref_s) - smp.get("fractional_gain", float("nan"))) > 1e-12:
+                raise ValueError("recorded pair gain differs from its seconds")
+            logs.append(math.log(cand_s / ref_s))
+        gain = 1 - math.exp(statistics.mean(logs))
+        if abs(gain - rec.get("fractional_gain", float("nan"))) > 1e-12:
+            raise ValueError("recorded gain differs from its samples")
+        if rec.get("reference_digest") != role_digest(identity) or \
+                rec.get("candidate_digest") != role_digest(cands[name]):
+            raise ValueError("calibration record measured a different order")
+        return gain, [s["seed"] for s in samples]
+
+    records = arr.get("training_candidates") or []
+    if sorted(r.get("name") for r in records) != sorted(cands):
+        raise ValueError("training did not cover exactly the candidate family")
+    best_name, best_gain, training_seeds = "identity", 0.0, set()
+    for rec in records:
+        gain, seeds = check_record(rec, rec.get("name"), "arrival_training", cfg["training_pairs"])
+        training_seeds.update(seeds)
+        if gain > max(cfg["min_gain"], best_gain):
+            best_name, best_gain = rec["name"], gain
+    if arr.get("proposed_candidate") != best_name:
+        raise ValueError("proposed candidate is not the best training gain")
+    accepted = False
+    conf = arr.get("confirmation")
+    if best_name != "identity":
+        if conf is None:
+            raise ValueError("a proposed candidate must be confirmed")
+        _, seeds = check_record(conf, best_name, "arrival_confirmation", cfg["confirmation_pairs"])
+        if training_seeds & set(seeds):
+            raise ValueError("confirmation seeds overlap the training seeds")
+        accepted = confirmed(conf, cfg["min_gain"])
+    elif conf is not None:
+        raise ValueError("confirmation recorded without a proposed candidate")
+    if arr.get("accepted") != accepted or arr.get("identity_fallback") != (not accepted):
+        raise ValueError("recorded acceptance differs from the confirmation rule")
+    selected = best_name if accepted else "identity"
+    if arr.get("selected_candidate") != selected:
+        raise ValueError("recorded selection differs from the evidence")
+    want = (cands[best_name] if accepted else identity)["arrival_order"]
+    if list(plan["arrival_order"]) != list(want):
+        raise ValueError("frozen order differs from the selected candidate")
+    return dict(selected=selected, proposed=best_name, accepted=accepted, best_training_gain=best_gain)
+
+
 def fit_role(m, n, k, world, chunk_rows, evaluate, *, config=None, seed=8000000):
     """Fit, confirm and freeze one role plan (timing injected by `evaluate`)."""
     cfg = settings(config)

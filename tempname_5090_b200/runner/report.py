@@ -81,10 +81,35 @@ def summarize_stage(samples: list, stage: str, trials: int, blocks: int) -> dict
     return result
 
 
+def validate_calibration_evidence(execution_plan: dict, config: dict) -> None:
+    """Every frozen role plan's decision must follow from its recorded samples."""
+    from ..parallel.planning import replay_role_evidence
+    for role, rp in sorted(execution_plan["roles"].items()):
+        m, n, k = rp["shape"]
+        try:
+            replay_role_evidence(rp, m, n, k, config["world_size"], rp["chunk_rows"])
+        except ValueError as exc:
+            raise ValueError(f"calibration evidence of role {role}: {exc}") from exc
+
+
+def validate_sources(root: Path, plan: dict) -> None:
+    """The run's source snapshot still hashes to its manifest (and to the plan's copy)."""
+    manifest = P.read(root / "sources-manifest.json")
+    P.require(plan.get("sources", manifest) == manifest, "plan and source manifest differ")
+    base = root / "sources"
+    present = sorted(str(p.relative_to(base)) for p in base.rglob("*") if p.is_file()
+                     and "__pycache__" not in p.parts and p.suffix in (".py", ".cu", ".cuh", ".h", ".cpp"))
+    P.require(present == sorted(manifest), "source snapshot files differ from the manifest")
+    for rel, sha in manifest.items():
+        P.require(hashlib.sha256((base / rel).read_bytes()).hexdigest() == sha, f"source {rel} was modified")
+
+
 def replay(root) -> dict:
     """Re-validate a finished run directory from disk and produce the report dict."""
     root = Path(root)
     plan = P.read(root / "plan.json")
+    if (root / "sources-manifest.json").exists():
+        validate_sources(root, plan)
     config = plan["config"]
     jobs = plan["jobs"]
     execution_plan = None
@@ -104,6 +129,7 @@ def replay(root) -> dict:
             execution_plan = P.calibration_from_rows(rows, config)
             P.require(P.digest(execution_plan) == plan.get("execution_plan_sha256", P.digest(execution_plan)),
                       "calibration plan digest differs from the frozen plan")
+            validate_calibration_evidence(execution_plan, config)
         elif job["stage"] in samples:
             samples[job["stage"]].extend(samples_from_rows(job, rows))
             if job["stage"] == "train":

@@ -75,3 +75,48 @@ def test_numerical_failure_is_fatal():
         return dict(elapsed_seconds=1.0, correctness_passed=False)
     with pytest.raises(ValueError):
         pl.fit_role(*SHAPE, evaluate)
+
+
+def _fitted(gains, **cfg):
+    return pl.fit_role(*SHAPE, _evaluator(gains, []), config=dict(training_pairs=2, confirmation_pairs=2, **cfg))
+
+
+def test_replay_of_calibration_evidence_matches_the_frozen_plan():
+    accepted = _fitted({"reverse_all": 0.05, "rotate": 0.01})
+    assert pl.replay_role_evidence(accepted, *SHAPE)["selected"] == "reverse_all"
+    identity = _fitted({})
+    assert pl.replay_role_evidence(identity, *SHAPE)["selected"] == "identity"
+
+
+def _tamper(plan, fn):
+    import copy
+    p = copy.deepcopy(plan)
+    fn(p["diagnostics"]["arrival"], p)
+    return p
+
+
+@pytest.mark.parametrize("what", ["seconds", "gain", "order_swap", "accept_flip", "frozen_order", "seed_reuse",
+                                  "drop_candidate", "proposal"])
+def test_replay_rejects_doctored_evidence(what):
+    plan = _fitted({"reverse_all": 0.05, "rotate": 0.01})
+
+    def edit(arr, p):
+        rec = arr["training_candidates"][0]
+        if what == "seconds":
+            rec["paired_samples"][0]["candidate_seconds"] *= 0.5
+        elif what == "gain":
+            rec["fractional_gain"] += 0.01
+        elif what == "order_swap":
+            rec["paired_samples"][1]["execution_order"].reverse()
+        elif what == "accept_flip":
+            arr["accepted"], arr["identity_fallback"] = False, True
+        elif what == "frozen_order":
+            p["arrival_order"] = pl.base_order(*SHAPE)
+        elif what == "seed_reuse":
+            arr["confirmation"]["paired_samples"][0]["seed"] = rec["paired_samples"][0]["seed"]
+        elif what == "drop_candidate":
+            arr["training_candidates"].pop()
+        elif what == "proposal":
+            arr["proposed_candidate"] = "rotate"
+    with pytest.raises(ValueError):
+        pl.replay_role_evidence(_tamper(plan, edit), *SHAPE)

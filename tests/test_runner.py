@@ -65,12 +65,18 @@ def fake_rows(job, cfg, world, timing, *, taco_losses=None):
         if job["stage"] == "preflight":
             row["checks"] = dict(tcgen05_gemm=True, nccl_all_gather=True)
         elif job["stage"] == "calibrate":
-            from tempname_5090_b200.parallel.planning import make_role, SCHEMA
+            from tempname_5090_b200.parallel.planning import fit_role, SCHEMA
             m = cfg["model"]
             M = m["sequence"] * m["micro_batch"]
+
+            def evaluate(plan, seed, arm, label):  # deterministic stand-in timings
+                return 0.95 if (label.endswith("candidate") and "/reverse_all/" in label) else 1.0
+            settings = dict(cfg["calibration"])
             row["calibration_plan"] = dict(schema=SCHEMA, world_size=world, transport_lanes=2, roles={
-                "attn": make_role(M, m["hidden"], m["hidden"] // world, world, m["chunk_rows"]),
-                "mlp": make_role(M, m["hidden"], m["ffn"] // world, world, m["chunk_rows"])})
+                "attn": fit_role(M, m["hidden"], m["hidden"] // world, world, m["chunk_rows"], evaluate,
+                                 config=settings),
+                "mlp": fit_role(M, m["hidden"], m["ffn"] // world, world, m["chunk_rows"], evaluate,
+                                config=settings)})
         elif job["stage"] == "operator":
             base = {"flux": 100.0, "flux_taco": 90.0, "flux_taco_interleaved": 89.0, P.ARRIVAL: 88.0}[job["arm"]]
             row["operator_results"] = [dict(role=role, us_per_call=base + job["block"] * 0.1, correctness_passed=True,
@@ -157,7 +163,16 @@ TAMPERS = {
     "taco_trajectory": lambda run: _edit(run / "train/trial1/block006-flux_taco_interleaved/rank0.json",
                                          lambda r: r.update(final_parameters_sha256=_hash("different"))),
     "trace_bytes": lambda run: _add_trace(run, "train/trial1/block007-flux", tamper=True),
+    "source_bytes": lambda run: (run / "sources/tempname_5090_b200/config.py").write_text("# edited\n"),
+    "source_added": lambda run: (run / "sources/csrc/extra.cu").write_text("// new\n"),
+    "calibration_samples": lambda run: [_edit(run / "calibrate" / f"rank{r}.json", _doctor_calibration)
+                                        for r in range(2)],
 }
+
+
+def _doctor_calibration(row):
+    rec = row["calibration_plan"]["roles"]["attn"]["diagnostics"]["arrival"]["training_candidates"][0]
+    rec["paired_samples"][0]["candidate_seconds"] *= 0.5
 
 
 @pytest.mark.parametrize("name", sorted(TAMPERS))
