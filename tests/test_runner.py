@@ -226,3 +226,27 @@ def test_timeout_stops_only_the_owned_process_group(tmp_path):
     finally:
         bystander.kill()
         bystander.wait()
+
+
+def test_background_relaunch_preserves_arguments_without_a_shell(tmp_path, monkeypatch):
+    """--background re-executes the controller detached with the same arguments
+    (minus --background) as an argument list: no shell ever parses them."""
+    seen = {}
+
+    class _Proc:
+        pid = 4242
+
+    def fake_popen(cmd, **kw):
+        seen["cmd"], seen["kw"] = cmd, kw
+        return _Proc()
+    monkeypatch.setattr(C.subprocess, "Popen", fake_popen)
+    odd = str(tmp_path / "run; echo injected $(id)")
+    argv = ["--execute", "--background", "--out", odd, "--world", "2", "--small-model"]
+    C.main(argv)
+    cmd, kw = seen["cmd"], seen["kw"]
+    assert isinstance(cmd, list) and not kw.get("shell", False) and kw.get("start_new_session") is True
+    assert cmd[1:3] == ["-m", "tempname_5090_b200.runner.controller"]
+    assert cmd[3:] == ["--execute", "--out", odd, "--world", "2", "--small-model"]
+    receipt = json.loads(Path(odd + ".launcher.json").read_text())
+    assert receipt["pid"] == 4242 and receipt["argv"] == cmd[3:] and len(receipt["token"]) == 32
+    assert kw["env"]["TN5B_CONTROLLER_TOKEN"] == receipt["token"]
