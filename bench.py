@@ -31,7 +31,7 @@ BASELINE_METRIC = "GPT-6.7B TP8 train step ms (max over ranks) at 1/2/4/8 GPU; G
 BASELINE_MS = 984.779
 
 REFERENCE_UNAVAILABLE = (
-    "reference cannot be installed or run on B200: /root/reference has no setup.py/pyproject.toml "
+    "reference cannot be installed or run on B200: its source tree has no setup.py/pyproject.toml "
     "(pip: 'not installable'); its worker and codec hard-gate on RTX 5090 (compute capability 12.0, "
     "170 SMs, name check: python/flux_5090/worker.py:368, codec.py:156) and its native GEMM build needs "
     "CUTLASS 3.9.0 headers fetched over the network against third_party/cutlass.lock.json")
@@ -200,7 +200,7 @@ def main():
             "higher_is_better": False,
             "scaling": "strong",
             "vs_baseline": round(ms / BASELINE_MS, 4),
-            "baseline_ref": "984.779 ms/step: Flux BF16 GemmOnly + NCCL RS, 8xRTX 5090 (BASELINE.md)",
+            "baseline_ref": "984.779 ms/step: Flux BF16 GemmOnly + NCCL RS, 8xRTX 5090 (published, reference lineage)",
             "dtype": "bf16",
             "data": "synthetic token ids uniform in [0, vocab), random-init weights N(0, 0.02)",
             "impl": "ours",
