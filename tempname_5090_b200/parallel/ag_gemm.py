@@ -86,6 +86,16 @@ class AGGemm:
         n = w.shape[1] if b_mn else w.shape[0]
         if shard.shape != (self.m // self.world, self.k):
             raise ValueError(f"shard must be [{self.m // self.world}, {self.k}]")
+        if w.dim() != 2 or (w.shape[0] if b_mn else w.shape[1]) != self.k or w.stride(-1) != 1:
+            raise ValueError(f"w must be 2-D with K={self.k} ({'[K, N]' if b_mn else '[N, K]'}) and unit inner stride")
+        for t, name in ((shard, "shard"), (w, "w")):
+            if t.dtype != torch.bfloat16 or t.device != self.device:
+                raise ValueError(f"{name} must be bf16 on {self.device}")
+        if bias is not None and tuple(bias.shape) != (n,):
+            raise ValueError(f"bias must have shape [{n}]")
+        for t, name in ((gelu_aux, "gelu_aux"), (gelu_grad_of, "gelu_grad_of"), (out, "out")):
+            if t is not None and tuple(t.shape) != (self.m, n):
+                raise ValueError(f"{name} must have shape [{self.m}, {n}]")
         out = torch.empty((self.m, n), dtype=torch.bfloat16, device=self.device) if out is None else out
         if bn == 0:
             bn = 256 if n >= 256 and (self.m // 128) * ((n + 255) // 256) >= 148 else 128

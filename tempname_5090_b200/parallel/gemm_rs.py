@@ -167,6 +167,7 @@ class GemmRS:
         b_mn = self.b_mn if b_mn is None else b_mn
         if self.failed:
             raise RuntimeError("this GemmRS operator previously failed")
+        self._check_operands(x, w, b_mn, residual, bias, out)
         if self.epoch + 2 >= 2 ** 31:
             raise RuntimeError("epoch exhausted; create a new operator")
         out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device) if out is None else out
@@ -186,9 +187,27 @@ class GemmRS:
         self.calls += 1
         return out
 
+    def _check_operands(self, x, w, b_mn, residual=None, bias=None, out=None):
+        """Operands must match the shape this operator's tile table, slots and flags
+        were built for: a mismatch would address tiles outside them."""
+        def need(t, shape, name):
+            if t.dtype != torch.bfloat16 or tuple(t.shape) != shape or t.stride(-1) != 1 \
+                    or t.device != self.device:
+                raise ValueError(f"{name} must be a bf16 tensor of shape {list(shape)} with unit inner "
+                                 f"stride on {self.device} (got {t.dtype} {list(t.shape)} on {t.device})")
+        need(x, (self.m, self.k), "x")
+        need(w, (self.k, self.n) if b_mn else (self.n, self.k), "w")
+        if residual is not None:
+            need(residual, (self.rows, self.n), "residual")
+        if bias is not None:
+            need(bias, (self.n,), "bias")
+        if out is not None:
+            need(out, (self.rows, self.n), "out")
+
     def push(self, x, w, b_mn: bool | None = None, delay_tile: int = -1, delay_ns: int = 0):
         """Producer phase: the GEMM whose epilogue pushes tiles to their owners."""
         b_mn = self.b_mn if b_mn is None else b_mn
+        self._check_operands(x, w, b_mn)
         parity = self.epoch & 1
         mode = 2 if self.quantized else 1
         lib().gemm_rs_push(x, False, w, b_mn, mode, self.recv[parity].ptrs.data_ptr(),

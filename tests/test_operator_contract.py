@@ -200,3 +200,56 @@ def test_ag_gemm_launch_contract(monkeypatch, rank, world):
     assert all(x["local_flags"] == flags.local and x["gather_ptrs"] == gather.ptrs.data_ptr() for x in c)
     with pytest.raises(ValueError):
         op.forward(torch.zeros((m // world + 128, k), dtype=torch.bfloat16), w)
+
+
+@pytest.mark.parametrize("bad", ["x_rows", "x_dtype", "w_k", "w_layout", "residual", "bias", "out"])
+def test_gemm_rs_rejects_mismatched_operands_before_launching(monkeypatch, bad):
+    from tempname_5090_b200.parallel import gemm_rs
+    fake = _FakeLib()
+    monkeypatch.setattr(gemm_rs, "lib", lambda: fake)
+    monkeypatch.setattr(gemm_rs, "count_launch", lambda n=1: None)
+    world = 2
+    op = gemm_rs.GemmRS(M, N, K, _emulate=(0, world, [_Buf(1), _Buf(2)], _Buf(3)), device="cpu")
+    bf = torch.bfloat16
+    args = dict(x=torch.zeros((M, K), dtype=bf), w=torch.zeros((N, K), dtype=bf))
+    kw = {}
+    if bad == "x_rows":
+        args["x"] = torch.zeros((M + 128, K), dtype=bf)
+    elif bad == "x_dtype":
+        args["x"] = torch.zeros((M, K), dtype=torch.float32)
+    elif bad == "w_k":
+        args["w"] = torch.zeros((N, K + 8), dtype=bf)
+    elif bad == "w_layout":
+        kw["b_mn"] = True  # [N, K] passed where [K, N] is declared
+    elif bad == "residual":
+        kw["residual"] = torch.zeros((M, N), dtype=bf)
+    elif bad == "bias":
+        kw["bias"] = torch.zeros((N + 1,), dtype=bf)
+    elif bad == "out":
+        kw["out"] = torch.zeros((M // world, N + 256), dtype=bf)
+    with pytest.raises(ValueError):
+        op.forward(args["x"], args["w"], **kw)
+    assert fake.calls == [] and not op.failed and op.epoch == 0
+
+
+@pytest.mark.parametrize("bad", ["w_k", "bias", "aux", "dtype"])
+def test_ag_gemm_rejects_mismatched_operands_before_launching(monkeypatch, bad):
+    from tempname_5090_b200.parallel import ag_gemm
+    fake = _FakeAGLib(grid=148)
+    monkeypatch.setattr(ag_gemm, "lib", lambda: fake)
+    monkeypatch.setattr(ag_gemm, "count_launch", lambda n=1: None)
+    world, m, k, n = 2, 512, 256, 512
+    op = ag_gemm.AGGemm(m, k, _emulate=(0, world, _AGBuf(1), _AGBuf(2)), device="cpu")
+    bf = torch.bfloat16
+    shard, w, kw = torch.zeros((m // world, k), dtype=bf), torch.zeros((n, k), dtype=bf), {}
+    if bad == "w_k":
+        w = torch.zeros((n, k + 8), dtype=bf)
+    elif bad == "bias":
+        kw["bias"] = torch.zeros((n - 1,), dtype=bf)
+    elif bad == "aux":
+        kw["gelu_aux"] = torch.zeros((m // world, n), dtype=bf)
+    elif bad == "dtype":
+        shard = shard.float()
+    with pytest.raises(ValueError):
+        op.forward(shard, w, **kw)
+    assert fake.calls == [] and op.flag_total == 0
