@@ -1,6 +1,7 @@
 """Checkpoint / resume on CPU: saving after two optimizer steps and resuming in
 a fresh model + trainer continues bitwise like the uninterrupted run; loading
-rejects a different configuration, TP size or a missing optimizer state."""
+rejects a different configuration, TP size or a missing optimizer state; and
+gradient accumulation over micro-batches is exact."""
 import pytest
 import torch
 
@@ -50,3 +51,18 @@ def test_load_rejects_mismatches(tmp_path):
     (tmp_path / "full" / "rank0-of-1.pt").rename(tmp_path / "full" / "rank0-of-2.pt")
     with pytest.raises(FileNotFoundError):
         load_checkpoint(str(tmp_path / "full"), a.model, a)
+
+
+def test_gradient_accumulation_matches_single_batch():
+    """Two identical micro-batches with accumulation_steps=2 (loss scale 1/2,
+    FP32 gradient accumulator) take exactly the step of one batch with
+    accumulation_steps=1."""
+    one = _trainer(cfg=CFG)
+    two = _trainer(cfg=dict(CFG, accumulation_steps=2))
+    b = _batches(11)
+    for _ in range(2):
+        l1, n1 = one.step_host(b)
+        l2, n2 = two.step_host(b + b)
+        assert (l1, n1) == (l2, n2)
+    for (k, v1), (_, v2) in zip(one.model.state_dict().items(), two.model.state_dict().items()):
+        assert torch.equal(v1, v2), k
