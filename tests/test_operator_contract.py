@@ -253,3 +253,34 @@ def test_ag_gemm_rejects_mismatched_operands_before_launching(monkeypatch, bad):
     with pytest.raises(ValueError):
         op.forward(shard, w, **kw)
     assert fake.calls == [] and op.flag_total == 0
+
+
+def test_role_plans_reach_their_operators(monkeypatch):
+    """The arrival arm's calibrated plans are routed by role (attn / mlp); roles
+    without a plan (other shapes) get the identity order; other arms get none."""
+    from tempname_5090_b200.parallel import gemm_rs, planning
+    from tempname_5090_b200.parallel.tp import TensorParallel
+    made = []
+
+    class Recorder:
+        def __init__(self, m, n, k, group, *, arm, chunk_rows, plan, transport, timeout_ns, workspace):
+            made.append(dict(m=m, n=n, k=k, arm=arm, plan=plan))
+            self.workspace = object()
+    monkeypatch.setattr(gemm_rs, "GemmRS", Recorder)
+    world, m, h, f = 8, 2048, 4096, 16384
+    orders = planning.candidates(m, h, h // world, world, 128)
+    attn_plan = planning.make_role(m, h, h // world, world, 128, orders[1]["arrival_order"])
+    mlp_plan = planning.make_role(m, h, f // world, world, 128)
+    tp = TensorParallel(None, arm="flux_taco_interleaved_arrival", plans=dict(attn=attn_plan, mlp=mlp_plan))
+    tp.world = world
+    tp.rs_operator(m, h, h // world, "attn")
+    tp.rs_operator(m, h, f // world, "mlp")
+    tp.rs_operator(m, h, 3 * h // world, "attn_bwd")
+    assert made[0]["plan"] is attn_plan and made[1]["plan"] is mlp_plan
+    assert made[2]["plan"]["arrival_order"] == planning.base_order(m, h, 3 * h // world, world, 128)
+    assert tp.rs_operator(m, h, h // world, "attn") is tp.rs_operator(m, h, h // world, "attn")  # cached
+    made.clear()
+    plain = TensorParallel(None, arm="flux_taco", plans=dict(attn=attn_plan))
+    plain.world = world
+    plain.rs_operator(m, h, h // world, "attn")
+    assert made[0]["plan"] is None
