@@ -146,10 +146,13 @@ void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor
   raise_if(tn5b::gemm::run(c, stream()), "ag_gemm");
 }
 
+// Grid of an all-gather GEMM launch (every CTA bumps each owner's chunk counter
+// once, so this is the per-call increment of the flag target).  Marked as an
+// all-gather call like ag_gemm's, so it gets the same (single-CTA) tile kind.
 int64_t gemm_grid(int64_t M, int64_t N, int64_t bn, int64_t mode) {
   tn5b::gemm::GemmCall c;
   c.M = int(M); c.N = int(N); c.bn = int(bn); c.mode = int(mode);
-  // same pair decision as ag_gemm's launch (auto)
+  c.ag = 1;
   return tn5b::gemm::grid_ctas(c);
 }
 
