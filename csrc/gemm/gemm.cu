@@ -182,6 +182,8 @@ int run(const GemmCall& c, cudaStream_t stream) {
   const int kind = tile_kind(c, bn);
   const bool pair = kind != kSingle;
   const int tile_n = kind == kWide ? 2 * bn : bn;
+  if (c.tile_order && pair)
+    return fail("gemm: an explicit tile order lists single-CTA tiles; use pair=0 with it");
   Params p{};
   p.M = c.M; p.N = c.N; p.K = c.K;
   p.tiles_m = (c.M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
