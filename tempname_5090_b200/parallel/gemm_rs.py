@@ -133,9 +133,12 @@ class GemmRS:
             self.partial = torch.empty((m, n), dtype=torch.bfloat16, device=self.device)
             pbytes = chunk_rows * n // 128 * 136
             self.packet_bytes = pbytes
-            self.send_packets = torch.empty((m // chunk_rows, pbytes), dtype=torch.uint8, device=self.device)
-            self.recv_blocks = torch.empty((m // chunk_rows // self.world, self.world - 1,
-                                            chunk_rows * n * 2), dtype=torch.uint8, device=self.device)
+            # Quantized arms send and receive packets only: no BF16-sized remote storage.
+            self.send_packets = torch.empty((m // chunk_rows, pbytes) if self.quantized else (0, pbytes),
+                                            dtype=torch.uint8, device=self.device)
+            block_bytes = pbytes if self.quantized else chunk_rows * n * 2
+            self.recv_blocks = torch.empty((m // chunk_rows // self.world, self.world - 1, block_bytes),
+                                           dtype=torch.uint8, device=self.device)
 
     @property
     def epoch(self) -> int:

@@ -41,7 +41,8 @@ class _FakeLib:
         if self.fail_push:
             raise RuntimeError("injected launch failure")
         self.calls.append(("push", dict(mode=mode, recv=recv_ptrs, flags=flag_ptrs, epoch=epoch,
-                                        order=tile_order.tolist(), rank=rank, world=world)))
+                                        order=tile_order.tolist(), rank=rank, world=world,
+                                        delay=(delay_tile, delay_ns))))
 
     def rs_reduce(self, recv, flags, slot_bytes, rank, world, rows, n, tile_n, chunk_rows, quantized, epoch,
                   out, residual, bias, order, arrival, claims, status, timeout_ns, max_ctas, stamps):
@@ -80,6 +81,7 @@ def test_nvlink_transport_launch_contract(monkeypatch, arm, rank, world):
         assert r["arrival"] == arm.endswith("arrival") and r["claims"] == arm.endswith("arrival")
         assert p["order"] == production and r["order"] == consumer
         assert r["residual"] and not r["bias"]
+        assert p["delay"] == (-1, 0)  # the lane-skew diagnostic never fires in a normal call
     # A failed launch poisons the operator: no further launches.
     fake.fail_push = True
     with pytest.raises(RuntimeError, match="injected"):
@@ -114,7 +116,8 @@ def _nccl_worker(rank, world, port, out_dir, arm):
         op = GemmRS(M, N, K, arm=arm, chunk_rows=CHUNK, transport="nccl", device="cpu")
         x, w = _inputs(rank)
         outs = [op.forward(x, w).clone() for _ in range(2)]
-        torch.save(dict(outs=outs, state=op.state()), os.path.join(out_dir, f"rank{rank}.pt"))
+        torch.save(dict(outs=outs, state=op.state(), recv_shape=tuple(op.recv_blocks.shape),
+                        send_shape=tuple(op.send_packets.shape)), os.path.join(out_dir, f"rank{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
@@ -143,6 +146,11 @@ def test_nccl_transport_two_gloo_ranks_match_ordered_sum(arm):
         for got in res[r]["outs"]:
             assert torch.equal(got, want)
         assert res[r]["state"]["calls"] == 2 and res[r]["state"]["reduction_order"] == list(range(world))
+        per, pbytes = rows // CHUNK, CHUNK * N // 128 * 136
+        if arm == "flux_taco":  # packets only: no BF16-sized remote storage
+            assert res[r]["recv_shape"] == (per, world - 1, pbytes) and res[r]["send_shape"] == (M // CHUNK, pbytes)
+        else:
+            assert res[r]["recv_shape"] == (per, world - 1, CHUNK * N * 2) and res[r]["send_shape"][0] == 0
 
 
 class _FakeAGLib:
