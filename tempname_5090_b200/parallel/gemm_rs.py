@@ -27,6 +27,7 @@ call t reduce (stream order) -- so r never reads a slot being overwritten.
 from __future__ import annotations
 
 import contextlib
+import threading
 
 import torch
 import torch.distributed as dist
@@ -71,6 +72,11 @@ class RSWorkspace:
             recv = [SymmetricBuffer(world * self.slot_bytes, group) for _ in range(2)]
             flags = SymmetricBuffer(world * self.tiles_per_dest * 4, group)
         self.recv, self.flags = recv, flags
+        # A failed exchange leaves slots and flags of an unfinished epoch: every
+        # operator sharing this workspace refuses further calls.  The lock keeps
+        # each call's epoch, push and reduce together when threads share operators.
+        self.failed = False
+        self.lock = threading.Lock()
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
         self.claims = torch.zeros(self.tiles_per_dest, dtype=torch.int32, device=device)
         self.epoch = 0
@@ -168,26 +174,30 @@ class GemmRS:
                 bias=None, out=None) -> torch.Tensor:
         """x [M, K] bf16; w [N, K] (or [K, N] when b_mn); returns [M/W, N] bf16."""
         b_mn = self.b_mn if b_mn is None else b_mn
-        if self.failed:
-            raise RuntimeError("this GemmRS operator previously failed")
+        ws = self.workspace
+        if self.failed or (ws is not None and ws.failed):
+            raise RuntimeError("this GemmRS operator (or one sharing its receive workspace) previously failed")
         self._check_operands(x, w, b_mn, residual, bias, out)
-        if self.epoch + 2 >= 2 ** 31:
-            raise RuntimeError("epoch exhausted; create a new operator")
         out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device) if out is None else out
-        self.epoch += 1
-        try:
-            if self.transport == "nvlink":
-                with tracing.scope("gemm_rs.push"):
-                    self.push(x, w, b_mn)
-                with tracing.scope("gemm_rs.reduce"):
-                    self.reduce(out, residual, bias)
-            else:
-                with tracing.scope("gemm_rs.nccl"):
-                    self._forward_nccl(x, w, b_mn, residual, bias, out)
-        except BaseException:
-            self.failed = True
-            raise
-        self.calls += 1
+        with (ws.lock if ws is not None else contextlib.nullcontext()):
+            if self.epoch + 2 >= 2 ** 31:
+                raise RuntimeError("epoch exhausted; create a new operator")
+            self.epoch += 1
+            try:
+                if self.transport == "nvlink":
+                    with tracing.scope("gemm_rs.push"):
+                        self.push(x, w, b_mn)
+                    with tracing.scope("gemm_rs.reduce"):
+                        self.reduce(out, residual, bias)
+                else:
+                    with tracing.scope("gemm_rs.nccl"):
+                        self._forward_nccl(x, w, b_mn, residual, bias, out)
+            except BaseException:
+                self.failed = True
+                if ws is not None:
+                    ws.failed = True
+                raise
+            self.calls += 1
         return out
 
     def _check_operands(self, x, w, b_mn, residual=None, bias=None, out=None):
@@ -241,8 +251,23 @@ class GemmRS:
             raise RuntimeError("profile_call needs the NVLink transport")
         if not 0 <= delay_ns <= 100_000_000:
             raise ValueError("diagnostic delay must be within 100 ms")
+        ws = self.workspace
+        if self.failed or ws.failed:
+            raise RuntimeError("this GemmRS operator (or one sharing its receive workspace) previously failed")
         out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device)
         stamps = torch.zeros(self.tiles_per_dest, dtype=torch.int64, device=self.device)
+        with ws.lock:
+            try:
+                delayed_local = self._profiled_call(x, w, out, stamps, delay_ns, delay_rank)
+            except BaseException:
+                self.failed = ws.failed = True
+                raise
+        torch.cuda.synchronize()
+        s = stamps.cpu()
+        rel = (s - s.min()).tolist()
+        return out, rel, delayed_local
+
+    def _profiled_call(self, x, w, out, stamps, delay_ns, delay_rank):
         self.epoch += 1
         delay_tile, delayed_local = -1, None
         if delay_ns:
@@ -260,10 +285,7 @@ class GemmRS:
                   delay_ns=delay_ns if self.rank == delay_rank else 0)
         self.reduce(out, stamps=stamps)
         self.calls += 1
-        torch.cuda.synchronize()
-        s = stamps.cpu()
-        rel = (s - s.min()).tolist()
-        return out, rel, delayed_local
+        return delayed_local
 
     def _forward_nccl(self, x, w, b_mn, residual, bias, out):
         from ..ops import gemm as G, taco

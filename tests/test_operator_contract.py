@@ -292,3 +292,54 @@ def test_role_plans_reach_their_operators(monkeypatch):
     plain.world = world
     plain.rs_operator(m, h, h // world, "attn")
     assert made[0]["plan"] is None
+
+
+def test_failure_poisons_every_operator_sharing_the_workspace(monkeypatch):
+    from tempname_5090_b200.parallel import gemm_rs
+    fake = _FakeLib()
+    monkeypatch.setattr(gemm_rs, "lib", lambda: fake)
+    monkeypatch.setattr(gemm_rs, "count_launch", lambda n=1: None)
+    recv, flags = [_Buf(1), _Buf(2)], _Buf(3)
+    a = gemm_rs.GemmRS(M, N, K, _emulate=(0, 2, recv, flags), device="cpu")
+    b = gemm_rs.GemmRS(M, N, 2 * K, _emulate=(0, 2, recv, flags), device="cpu")
+    b.workspace = a.workspace  # two projections of one (M, N) share slots, flags and epochs
+    x, w = torch.zeros((M, K), dtype=torch.bfloat16), torch.zeros((N, K), dtype=torch.bfloat16)
+    x2, w2 = torch.zeros((M, 2 * K), dtype=torch.bfloat16), torch.zeros((N, 2 * K), dtype=torch.bfloat16)
+    a.forward(x, w)
+    b.forward(x2, w2)
+    assert [c[1]["epoch"] for c in fake.calls] == [1, 1, 2, 2]  # one epoch sequence per workspace
+    fake.fail_push = True
+    with pytest.raises(RuntimeError, match="injected"):
+        a.forward(x, w)
+    fake.fail_push = False
+    n = len(fake.calls)
+    with pytest.raises(RuntimeError, match="previously failed"):
+        b.forward(x2, w2)
+    assert len(fake.calls) == n
+
+
+def test_concurrent_calls_keep_each_epoch_together(monkeypatch):
+    import threading
+    import time
+    from tempname_5090_b200.parallel import gemm_rs
+
+    class Yielding(_FakeLib):
+        def gemm_rs_push(self, *a, **k):
+            time.sleep(0)  # invite a thread switch between the two phases of one call
+            super().gemm_rs_push(*a, **k)
+            time.sleep(0)
+    fake = Yielding()
+    monkeypatch.setattr(gemm_rs, "lib", lambda: fake)
+    monkeypatch.setattr(gemm_rs, "count_launch", lambda n=1: None)
+    op = gemm_rs.GemmRS(M, N, K, _emulate=(0, 2, [_Buf(1), _Buf(2)], _Buf(3)), device="cpu")
+    x, w = torch.zeros((M, K), dtype=torch.bfloat16), torch.zeros((N, K), dtype=torch.bfloat16)
+    threads = [threading.Thread(target=lambda: [op.forward(x, w) for _ in range(40)]) for _ in range(3)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    calls = fake.calls
+    assert len(calls) == 2 * 120 and op.epoch == 120
+    for i in range(0, len(calls), 2):
+        assert calls[i][0] == "push" and calls[i + 1][0] == "reduce"
+        assert calls[i][1]["epoch"] == calls[i + 1][1]["epoch"] == i // 2 + 1
