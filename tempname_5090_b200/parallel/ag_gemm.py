@@ -20,6 +20,8 @@ push, which r issues after every stream-ordered reader of call t.
 """
 from __future__ import annotations
 
+import threading
+
 import torch
 import torch.distributed as dist
 
@@ -66,6 +68,8 @@ class AGGemm:
             self.flags = SymmetricBuffer(self.world * 4, group)
         self.flag_total = 0
         self.calls = 0
+        self.failed = False
+        self._lock = threading.Lock()
         self._orders: dict = {}
         self.status = status_tensor(self.device)
 
@@ -83,6 +87,8 @@ class AGGemm:
 
     def forward(self, shard: torch.Tensor, w: torch.Tensor, *, b_mn: bool = False, bias=None,
                 gelu_aux=None, gelu_grad_of=None, out=None, bn: int = 0) -> torch.Tensor:
+        if self.failed:
+            raise RuntimeError("this AG->GEMM operator previously failed (its chunk counters are out of step)")
         n = w.shape[1] if b_mn else w.shape[0]
         if shard.shape != (self.m // self.world, self.k):
             raise ValueError(f"shard must be [{self.m // self.world}, {self.k}]")
@@ -99,8 +105,6 @@ class AGGemm:
         out = torch.empty((self.m, n), dtype=torch.bfloat16, device=self.device) if out is None else out
         if bn == 0:
             bn = 256 if n >= 256 and (self.m // 128) * ((n + 255) // 256) >= 148 else 128
-        grid = lib().gemm_grid(self.m, n, bn, 0)
-        self.flag_total += grid
         epi = 0
         aux = None
         if bias is not None:
@@ -111,13 +115,24 @@ class AGGemm:
         if gelu_grad_of is not None:
             epi |= G.EPI_GELU_BWD
             aux = gelu_grad_of
-        with tracing.scope("ag_gemm"):
-            lib().ag_gemm(shard.contiguous(), self.gathered, w, b_mn, out, epi, bias, aux,
-                          self.gather.ptrs.data_ptr(), self.flags.ptrs.data_ptr(), self.flags.local,
-                          self.rank, self.world, self.flag_total, self._order(n, bn), self.status,
-                          self.timeout_ns, bn)
-        count_launch()
-        self.calls += 1
+        # The counter target is cumulative over calls (every CTA of every call bumps
+        # each owner's counter once): a launch that fails leaves it out of step, so
+        # the operator refuses further calls; the lock keeps target and launch paired.
+        with self._lock:
+            try:
+                grid = lib().gemm_grid(self.m, n, bn, 0)
+                target = self.flag_total + grid
+                with tracing.scope("ag_gemm"):
+                    lib().ag_gemm(shard.contiguous(), self.gathered, w, b_mn, out, epi, bias, aux,
+                                  self.gather.ptrs.data_ptr(), self.flags.ptrs.data_ptr(), self.flags.local,
+                                  self.rank, self.world, target, self._order(n, bn), self.status,
+                                  self.timeout_ns, bn)
+                self.flag_total = target
+            except BaseException:
+                self.failed = True
+                raise
+            count_launch()
+            self.calls += 1
         return out
 
     def close(self):

@@ -343,3 +343,30 @@ def test_concurrent_calls_keep_each_epoch_together(monkeypatch):
     for i in range(0, len(calls), 2):
         assert calls[i][0] == "push" and calls[i + 1][0] == "reduce"
         assert calls[i][1]["epoch"] == calls[i + 1][1]["epoch"] == i // 2 + 1
+
+
+def test_ag_gemm_failed_launch_poisons_the_operator(monkeypatch):
+    from tempname_5090_b200.parallel import ag_gemm
+
+    class Failing(_FakeAGLib):
+        fail = False
+
+        def ag_gemm(self, *a, **k):
+            if self.fail:
+                raise RuntimeError("injected launch failure")
+            super().ag_gemm(*a, **k)
+    fake = Failing(grid=148)
+    monkeypatch.setattr(ag_gemm, "lib", lambda: fake)
+    monkeypatch.setattr(ag_gemm, "count_launch", lambda n=1: None)
+    m, k, n = 512, 256, 512
+    op = ag_gemm.AGGemm(m, k, _emulate=(0, 2, _AGBuf(1), _AGBuf(2)), device="cpu")
+    shard, w = torch.zeros((m // 2, k), dtype=torch.bfloat16), torch.zeros((n, k), dtype=torch.bfloat16)
+    op.forward(shard, w)
+    fake.fail = True
+    with pytest.raises(RuntimeError, match="injected"):
+        op.forward(shard, w)
+    assert op.flag_total == 148 and op.failed  # the failed call did not advance the target
+    fake.fail = False
+    with pytest.raises(RuntimeError, match="previously failed"):
+        op.forward(shard, w)
+    assert len(fake.calls) == 1
