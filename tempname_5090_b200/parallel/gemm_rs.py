@@ -116,10 +116,7 @@ class GemmRS:
         # (NCCL transport on Gloo ranks, or a recording stand-in for the kernels).
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.order = mapping.schedule(m, n, k, self.world, chunk_rows, arm, plan)
-        # In-kernel pushes start on destination rank+1 (no incast); the NCCL
-        # transport keeps the reference CTA map.
-        shift = self.rank + 1 if transport == "nvlink" else 0
-        ids = mapping.linear_tile_ids(m, n, k, self.world, chunk_rows, arm, plan, tile_n=TILE_N, shift=shift)
+        ids = self.production_ids(self.rank)
         self.tile_order = torch.tensor(ids, dtype=torch.int32, device=self.device)
         local = mapping.consumer_tile_order(m, n, k, self.world, chunk_rows, arm, self.rank, plan, TILE_N)
         self.consumer_order = torch.tensor(local, dtype=torch.int32, device=self.device)
@@ -145,6 +142,14 @@ class GemmRS:
             block_bytes = pbytes if self.quantized else chunk_rows * n * 2
             self.recv_blocks = torch.empty((m // chunk_rows // self.world, self.world - 1, block_bytes),
                                            dtype=torch.uint8, device=self.device)
+
+    def production_ids(self, rank: int) -> list:
+        """Tile order of `rank`'s producer GEMM.  In-kernel pushes start on
+        destination rank+1 (no incast); the NCCL transport keeps the reference
+        CTA map."""
+        shift = rank + 1 if self.transport == "nvlink" else 0
+        return mapping.linear_tile_ids(self.m, self.n, self.k, self.world, self.chunk_rows, self.arm, self.plan,
+                                       tile_n=TILE_N, shift=shift)
 
     @property
     def epoch(self) -> int:
@@ -271,9 +276,11 @@ class GemmRS:
         self.epoch += 1
         delay_tile, delayed_local = -1, None
         if delay_ns:
+            # Every rank identifies the same tile: the first lane-0 tile of
+            # `delay_rank`'s own production order (orders differ per rank).
             tiles_n = self.n // TILE_N
             per_dest_m = self.rows // 128
-            for tid in self.tile_order.tolist():
+            for tid in self.production_ids(delay_rank):
                 tm = tid // tiles_n
                 block = (tm * 128 % self.rows) // self.chunk_rows
                 if block % 2 == 0:

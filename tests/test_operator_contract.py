@@ -370,3 +370,33 @@ def test_ag_gemm_failed_launch_poisons_the_operator(monkeypatch):
     with pytest.raises(RuntimeError, match="previously failed"):
         op.forward(shard, w)
     assert len(fake.calls) == 1
+
+
+def test_lane_skew_diagnostic_names_the_same_tile_on_every_rank(monkeypatch):
+    """profile_call: only `delay_rank` arms the bounded publication delay, on the
+    first lane-0 tile of its own (rotated) production order, and every rank
+    reports that same tile as (owner, local tile id)."""
+    from tempname_5090_b200.parallel import gemm_rs
+    fake = _FakeLib()
+    monkeypatch.setattr(gemm_rs, "lib", lambda: fake)
+    monkeypatch.setattr(gemm_rs, "count_launch", lambda n=1: None)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a, **k: None)
+    world = 4
+    x, w = torch.zeros((M, K), dtype=torch.bfloat16), torch.zeros((N, K), dtype=torch.bfloat16)
+    named = []
+    for rank in range(world):
+        op = gemm_rs.GemmRS(M, N, K, _emulate=(rank, world, [_Buf(1), _Buf(2)], _Buf(3)), device="cpu")
+        fake.calls.clear()
+        _, _, delayed = op.profile_call(x, w, delay_ns=1000, delay_rank=2)
+        named.append(delayed)
+        delay_tile, delay_ns = fake.calls[0][1]["delay"]
+        if rank == 2:
+            tiles_n = N // 256
+            per_dest_m = M // world // 128
+            tm = delay_tile // tiles_n
+            dest = tm // per_dest_m
+            assert delay_ns == 1000 and delayed == (dest, (tm - dest * per_dest_m) * tiles_n + delay_tile % tiles_n)
+            assert dest == 3  # rank 2 produces for destination 3 first
+        else:
+            assert (delay_tile, delay_ns) == (-1, 0)
+    assert len(set(named)) == 1
