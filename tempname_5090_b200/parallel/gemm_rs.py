@@ -335,6 +335,7 @@ class GemmRS:
                     world=self.world, calls=self.calls, epoch=self.epoch,
                     shape=[self.m, self.n, self.k], chunk_rows=self.chunk_rows,
                     production_schedule=self.order, tile_n=TILE_N,
+                    push_destination_rotation=(self.rank + 1) % self.world if self.transport == "nvlink" else 0,
                     quantization="all_remote_h128_e4m3" if self.quantized else "none",
                     remote_wire_bytes_per_source=mapping.wire_bytes(self.m, self.n, self.world, self.quantized),
                     reduction_order=list(range(self.world)), rounding="bf16_after_each_source",
