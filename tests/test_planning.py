@@ -34,12 +34,11 @@ def test_digest_stable():
 
 
 def _evaluator(gains, calls):
+    """Stand-in timings: the challenger of candidate `name` is `gains[name]` faster."""
     def evaluate(plan, seed, arm, label):
         calls.append((label, seed))
-        name = label.split("/")[1]
-        side = label.split("/")[-1]
-        base = 1.0
-        return base * (1 - gains.get(name, 0.0)) if side == "candidate" else base
+        stage, name, index, side = label.split(":")
+        return 1.0 - gains.get(name, 0.0) if side == "challenger" else 1.0
     return evaluate
 
 
@@ -47,27 +46,64 @@ def test_fit_selects_and_confirms_best():
     calls = []
     plan = pl.fit_role(*SHAPE, _evaluator({"reverse_all": 0.05, "rotate": 0.01}, calls),
                        config=dict(training_pairs=2, confirmation_pairs=2))
-    arrival = plan["diagnostics"]["arrival"]
-    assert arrival["selected_candidate"] == "reverse_all" and arrival["accepted"]
+    d = plan["diagnostics"]
+    assert d["selected"] == "reverse_all" and d["accepted"] and d["proposal"] == "reverse_all"
     assert plan["arrival_order"] != pl.base_order(*SHAPE)
-    train = {s for l, s in calls if "training" in l}
-    confirm = {s for l, s in calls if "confirmation" in l}
+    train = {s for l, s in calls if l.startswith("training")}
+    confirm = {s for l, s in calls if l.startswith("confirmation")}
     assert train.isdisjoint(confirm)
-    orders = [l.split("/")[-1] for l, _ in calls if "pair1" in l and "reverse_all" in l
-              and "training" in l]
-    assert orders == ["candidate", "reference"]   # BA order on odd pairs
+    sides = [l.split(":")[-1] for l, _ in calls if l.startswith("training:reverse_all:1:")]
+    assert sides == ["challenger", "baseline"]   # BA order on odd pairs
+    sides = [l.split(":")[-1] for l, _ in calls if l.startswith("training:reverse_all:0:")]
+    assert sides == ["baseline", "challenger"]
+    # both sides of one pair see the same inputs
+    seeds = {s for l, s in calls if l.startswith("training:reverse_all:1:")}
+    assert len(seeds) == 1
+
+
+def test_geometric_gain_and_confirmation_rule():
+    rec = dict(gain=pl.geometric_gain([0.9, 0.8]), pairs=[dict(gain=0.1), dict(gain=0.2)])
+    assert abs(rec["gain"] - (1 - math.sqrt(0.72))) < 1e-15
+    assert pl.confirmed(rec, 0.05)
+    rec["pairs"][1]["gain"] = 0.001  # one weak pair vetoes the candidate
+    assert not pl.confirmed(rec, 0.05)
+
+
+def test_family_orders_keep_every_slot_destination():
+    m, n, k, world, chunk = SHAPE
+    per = m // world // chunk
+    for cand in pl.candidates(*SHAPE):
+        order = cand["arrival_order"]
+        assert all(block // per == slot % world for slot, block in enumerate(order))
+    names = [c["name"] for c in pl.candidates(3 * 8 * 128, 4096, 512, 8, 128)]
+    assert names == ["identity", "reverse_all", "reverse_odd", "reverse_even", "rotate"]
+    # two blocks per destination: rotating is reversing, listed once
+    assert [c["name"] for c in pl.candidates(*SHAPE)] == ["identity", "reverse_all", "reverse_odd", "reverse_even"]
+    # one block per destination: every rule collapses to the identity
+    assert [c["name"] for c in pl.candidates(1024, 4096, 512, 8, 128)] == ["identity"]
+
+
+def test_a_plan_in_the_other_implementations_layout_is_accepted():
+    """Plans exchanged with the reference carry the same four fields; their
+    diagnostics are opaque to validation."""
+    order = pl.candidates(*SHAPE)[2]["arrival_order"]
+    foreign = dict(shape=list(SHAPE[:3]), chunk_rows=SHAPE[4], arrival_order=order,
+                   diagnostics=dict(method="other-implementation", arrival=dict(selected_candidate="reverse_odd")))
+    assert pl.validate_role_plan(foreign, *SHAPE) is foreign
+    with pytest.raises(ValueError):
+        pl.validate_role_plan(dict(foreign, extra=1), *SHAPE)
 
 
 def test_unstable_confirmation_falls_back_to_identity():
-    state = {"n": 0}
-
     def evaluate(plan, seed, arm, label):
-        if "confirmation" in label and label.endswith("candidate"):
+        stage, name, index, side = label.split(":")
+        if stage == "confirmation" and side == "challenger":
             return 1.2
-        return 0.9 if label.endswith("candidate") and "reverse_all" in label else 1.0
+        return 0.9 if side == "challenger" and name == "reverse_all" else 1.0
     plan = pl.fit_role(*SHAPE, evaluate)
     assert plan["arrival_order"] == pl.base_order(*SHAPE)
-    assert plan["diagnostics"]["arrival"]["identity_fallback"]
+    d = plan["diagnostics"]
+    assert d["proposal"] == "reverse_all" and not d["accepted"] and d["selected"] == "identity"
 
 
 def test_numerical_failure_is_fatal():
@@ -91,32 +127,36 @@ def test_replay_of_calibration_evidence_matches_the_frozen_plan():
 def _tamper(plan, fn):
     import copy
     p = copy.deepcopy(plan)
-    fn(p["diagnostics"]["arrival"], p)
+    fn(p["diagnostics"], p)
     return p
 
 
 @pytest.mark.parametrize("what", ["seconds", "gain", "order_swap", "accept_flip", "frozen_order", "seed_reuse",
-                                  "drop_candidate", "proposal"])
+                                  "drop_candidate", "proposal", "digest", "settings"])
 def test_replay_rejects_doctored_evidence(what):
     plan = _fitted({"reverse_all": 0.05, "rotate": 0.01})
 
-    def edit(arr, p):
-        rec = arr["training_candidates"][0]
+    def edit(d, p):
+        rec = d["trials"][0]
         if what == "seconds":
-            rec["paired_samples"][0]["candidate_seconds"] *= 0.5
+            rec["pairs"][0]["challenger_s"] *= 0.5
         elif what == "gain":
-            rec["fractional_gain"] += 0.01
+            rec["gain"] += 0.01
         elif what == "order_swap":
-            rec["paired_samples"][1]["execution_order"].reverse()
+            rec["pairs"][1]["first"] = "baseline"
         elif what == "accept_flip":
-            arr["accepted"], arr["identity_fallback"] = False, True
+            d["accepted"], d["selected"] = False, "identity"
         elif what == "frozen_order":
             p["arrival_order"] = pl.base_order(*SHAPE)
         elif what == "seed_reuse":
-            arr["confirmation"]["paired_samples"][0]["seed"] = rec["paired_samples"][0]["seed"]
+            d["confirmation"]["pairs"][0]["seed"] = rec["pairs"][0]["seed"]
         elif what == "drop_candidate":
-            arr["training_candidates"].pop()
+            d["trials"].pop()
         elif what == "proposal":
-            arr["proposed_candidate"] = "rotate"
+            d["proposal"] = "rotate"
+        elif what == "digest":
+            rec["challenger_sha256"] = "0" * 64
+        elif what == "settings":
+            d["settings"]["min_gain"] = 0.2
     with pytest.raises(ValueError):
         pl.replay_role_evidence(_tamper(plan, edit), *SHAPE)

@@ -70,7 +70,7 @@ def fake_rows(job, cfg, world, timing, *, taco_losses=None):
             M = m["sequence"] * m["micro_batch"]
 
             def evaluate(plan, seed, arm, label):  # deterministic stand-in timings
-                return 0.95 if (label.endswith("candidate") and "/reverse_all/" in label) else 1.0
+                return 0.95 if (label.endswith(":challenger") and ":reverse_all:" in label) else 1.0
             settings = dict(cfg["calibration"])
             row["calibration_plan"] = dict(schema=SCHEMA, world_size=world, transport_lanes=2, roles={
                 "attn": fit_role(M, m["hidden"], m["hidden"] // world, world, m["chunk_rows"], evaluate,
@@ -171,8 +171,8 @@ TAMPERS = {
 
 
 def _doctor_calibration(row):
-    rec = row["calibration_plan"]["roles"]["attn"]["diagnostics"]["arrival"]["training_candidates"][0]
-    rec["paired_samples"][0]["candidate_seconds"] *= 0.5
+    rec = row["calibration_plan"]["roles"]["attn"]["diagnostics"]["trials"][0]
+    rec["pairs"][0]["challenger_s"] *= 0.5
 
 
 @pytest.mark.parametrize("name", sorted(TAMPERS))
