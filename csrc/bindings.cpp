@@ -106,14 +106,95 @@ void gemm_rs_push(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn
   raise_if(tn5b::gemm::run(c, stream()), "gemm_rs_push");
 }
 
-// All-gather -> GEMM: out = epilogue(gather(shards) * B^T); `gather` is this
-// rank's symmetric gather buffer [M, K] that peers push their shards into.
+// GEMM -> reduce-scatter, pull transport: one launch whose GEMM CTAs store the
+// partial tiles of A*B^T into this rank's partial buffer and publish them to
+// their owners, while its `comm_ctas` reducer CTAs pull this rank's tiles from
+// every source and reduce them (ordered, BF16 after every source) into `out`.
+// `phase` (bit1 reduce, bit2 GEMM) splits the launch for single-GPU emulation.
+void gemm_rs_pull(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_t partial_local,
+                  int64_t partial_ptrs, int64_t flag_ptrs, int64_t my_flags, int64_t rank, int64_t world,
+                  int64_t epoch, const at::Tensor& tile_order, const at::Tensor& consumer_order, at::Tensor& out,
+                  const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& bias,
+                  const at::Tensor& status, int64_t timeout_ns, int64_t comm_ctas, int64_t phase,
+                  const c10::optional<at::Tensor>& stamps, const c10::optional<at::Tensor>& produced,
+                  int64_t delay_tile, int64_t delay_ns, int64_t max_ctas,
+                  const c10::optional<at::Tensor>& cta_stamps) {
+  check_bf16(A, "A"); check_bf16(B, "B"); check_rows(A, "A"); check_rows(B, "B");
+  check_bf16(out, "out");
+  TORCH_CHECK(out.is_contiguous(), "gemm_rs_pull: out must be contiguous");
+  const c10::cuda::CUDAGuard guard(A.device());
+  tn5b::gemm::GemmCall c;
+  c.A = A.data_ptr(); c.lda = A.stride(0); c.a_mn = a_mn;
+  c.B = B.data_ptr(); c.ldb = B.stride(0); c.b_mn = b_mn;
+  c.M = int(a_mn ? A.size(1) : A.size(0));
+  c.N = int(b_mn ? B.size(1) : B.size(0));
+  const int64_t ka = a_mn ? A.size(0) : A.size(1);
+  const int64_t kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(ka == kb, "gemm_rs_pull: K mismatch");
+  c.K = int(ka);
+  TORCH_CHECK(world >= 1 && c.M % world == 0 && out.size(0) == c.M / world && out.size(1) == c.N,
+              "gemm_rs_pull: out must be [M / world, N]");
+  c.mode = 3;
+  c.rs_partial_local = reinterpret_cast<void*>(partial_local);
+  c.rs_partials = reinterpret_cast<const uint8_t* const*>(partial_ptrs);
+  c.rs_flags = reinterpret_cast<uint32_t* const*>(flag_ptrs);
+  c.rs_my_flags = reinterpret_cast<const uint32_t*>(my_flags);
+  c.rank = int(rank); c.world = int(world);
+  c.epoch = uint32_t(epoch);
+  check_cuda(tile_order, "tile_order");
+  TORCH_CHECK(tile_order.scalar_type() == at::kInt);
+  c.tile_order = tile_order.data_ptr<int>();
+  check_cuda(consumer_order, "consumer_order");
+  TORCH_CHECK(consumer_order.scalar_type() == at::kInt);
+  c.rs_consumer_order = consumer_order.data_ptr<int>();
+  c.rs_out = out.data_ptr();
+  if (residual) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == out.sizes(), "residual must match out");
+    c.rs_residual = residual->data_ptr();
+  }
+  if (bias) {
+    check_bf16(*bias, "bias");
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == c.N, "bias must be [N]");
+    c.rs_bias = bias->data_ptr();
+  }
+  if (stamps) {
+    TORCH_CHECK(stamps->is_cuda() && stamps->scalar_type() == at::kLong, "stamps must be CUDA int64");
+    c.rs_stamps = reinterpret_cast<unsigned long long*>(stamps->data_ptr<int64_t>());
+  }
+  if (produced) {
+    TORCH_CHECK(produced->is_cuda() && produced->scalar_type() == at::kLong, "produced must be CUDA int64");
+    c.rs_produced = reinterpret_cast<unsigned long long*>(produced->data_ptr<int64_t>());
+  }
+  c.status = status_ptr(status);
+  c.timeout_ns = uint64_t(timeout_ns);
+  c.comm_ctas = int(comm_ctas);
+  c.phase = int(phase);
+  c.delay_tile = int(delay_tile);
+  c.delay_ns = uint64_t(delay_ns);
+  c.max_ctas = int(max_ctas);
+  if (cta_stamps) {
+    TORCH_CHECK(cta_stamps->is_cuda() && cta_stamps->scalar_type() == at::kLong &&
+                    cta_stamps->numel() >= 2 * int64_t(tn5b::gemm::grid_ctas(c)),
+                "cta_stamps must be CUDA int64 with 2 words per CTA");
+    c.cta_stamps = reinterpret_cast<unsigned long long*>(cta_stamps->data_ptr<int64_t>());
+  }
+  raise_if(tn5b::gemm::run(c, stream()), "gemm_rs_pull");
+}
+
+// All-gather -> GEMM, pull transport: out = epilogue(gather(shards) * B^T).
+// `gather` is this rank's symmetric gather buffer [M, K]; its gatherer CTAs
+// pull the peers' chunks into it while the GEMM CTAs consume arrived blocks
+// (the own chunk straight from `shard`).  `ctrl_ptrs` are the peers' control
+// blocks: published[world] flags at byte 0, the pulled counter at byte 256.
 void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor& B, bool b_mn,
              at::Tensor& out, int64_t epi, const c10::optional<at::Tensor>& bias,
-             const c10::optional<at::Tensor>& aux, int64_t gather_ptrs, int64_t flag_ptrs,
-             int64_t local_flags, int64_t rank, int64_t world, int64_t target,
-             const at::Tensor& tile_order, const at::Tensor& status, int64_t timeout_ns,
-             int64_t bn) {
+             const c10::optional<at::Tensor>& aux, int64_t gather_ptrs, int64_t published_ptrs,
+             int64_t pulled_ptrs, int64_t ctrl_local, const at::Tensor& ready, const at::Tensor& own_done,
+             int64_t rank, int64_t world, int64_t epoch, int64_t own_target, int64_t pulled_target,
+             int64_t ready_target, const at::Tensor& tile_order, const at::Tensor& status, int64_t timeout_ns,
+             int64_t bn, int64_t comm_ctas, int64_t phase, const c10::optional<at::Tensor>& cta_stamps,
+             const c10::optional<at::Tensor>& block_stamps) {
   check_bf16(shard, "shard"); check_bf16(gather, "gather"); check_bf16(B, "B"); check_bf16(out, "out");
   TORCH_CHECK(shard.is_contiguous() && gather.is_contiguous(), "shard/gather must be contiguous");
   check_rows(B, "B"); check_rows(out, "out");
@@ -128,32 +209,66 @@ void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor
   TORCH_CHECK(shard.numel() * world == gather.numel(), "ag_gemm: shard size mismatch");
   c.out = out.data_ptr(); c.ldo = out.stride(0);
   c.epi = int(epi);
-  if (bias) { check_bf16(*bias, "bias"); c.bias = bias->data_ptr(); }
+  if (bias) {
+    check_bf16(*bias, "bias");
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == c.N, "ag_gemm: bias must be a contiguous [N]");
+    c.bias = bias->data_ptr();
+  }
   if (aux) { check_bf16(*aux, "aux"); check_rows(*aux, "aux"); c.aux = aux->data_ptr(); c.ld_aux = aux->stride(0); }
+  TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == at::kInt && ready.numel() >= world * (c.M / world / 128),
+              "ag_gemm: ready must be int32 [world * blocks]");
+  TORCH_CHECK(own_done.is_cuda() && own_done.scalar_type() == at::kInt, "ag_gemm: own_done must be int32");
   c.ag = 1;
   c.rank = int(rank); c.world = int(world);
-  c.ag_chunk_flags = reinterpret_cast<const uint32_t*>(local_flags);
-  c.ag_target = uint32_t(target);
   c.ag_shard = shard.data_ptr();
-  c.ag_shard_bytes = shard.numel() * 2;
   c.ag_gather = reinterpret_cast<uint8_t* const*>(gather_ptrs);
-  c.ag_peer_flags = reinterpret_cast<uint32_t* const*>(flag_ptrs);
+  c.ag_published = reinterpret_cast<uint32_t* const*>(published_ptrs);
+  c.ag_pulled = reinterpret_cast<uint32_t* const*>(pulled_ptrs);
+  c.ag_published_local = reinterpret_cast<const uint32_t*>(ctrl_local);
+  c.ag_pulled_local = reinterpret_cast<const uint32_t*>(ctrl_local + 256);
+  c.ag_ready = reinterpret_cast<uint32_t*>(ready.data_ptr<int>());
+  c.ag_own_done = reinterpret_cast<uint32_t*>(own_done.data_ptr<int>());
+  c.ag_epoch = uint32_t(epoch);
+  c.ag_own_target = uint32_t(own_target);
+  c.ag_pulled_target = uint32_t(pulled_target);
+  c.ag_ready_target = uint32_t(ready_target);
   check_cuda(tile_order, "tile_order");
   c.tile_order = tile_order.data_ptr<int>();
   c.status = status_ptr(status);
   c.timeout_ns = uint64_t(timeout_ns);
   c.bn = int(bn);
+  c.comm_ctas = int(comm_ctas);
+  c.phase = int(phase);
+  if (cta_stamps) {
+    TORCH_CHECK(cta_stamps->is_cuda() && cta_stamps->scalar_type() == at::kLong &&
+                    cta_stamps->numel() >= 2 * int64_t(tn5b::gemm::grid_ctas(c)),
+                "cta_stamps must be CUDA int64 with 2 words per CTA");
+    c.cta_stamps = reinterpret_cast<unsigned long long*>(cta_stamps->data_ptr<int64_t>());
+  }
+  if (block_stamps) {
+    TORCH_CHECK(block_stamps->is_cuda() && block_stamps->scalar_type() == at::kLong &&
+                    block_stamps->numel() >= world * (c.M / world / 128),
+                "block_stamps must be CUDA int64 [world * blocks]");
+    c.ag_block_stamps = reinterpret_cast<unsigned long long*>(block_stamps->data_ptr<int64_t>());
+  }
   raise_if(tn5b::gemm::run(c, stream()), "ag_gemm");
 }
 
-// Grid of an all-gather GEMM launch (every CTA bumps each owner's chunk counter
-// once, so this is the per-call increment of the flag target).  Marked as an
-// all-gather call like ag_gemm's, so it gets the same (single-CTA) tile kind.
-int64_t gemm_grid(int64_t M, int64_t N, int64_t bn, int64_t mode) {
+// Grid of a fused launch (GEMM CTAs + communication CTAs) for profiling buffers.
+int64_t fused_grid(int64_t M, int64_t N, int64_t K, int64_t mode, int64_t ag, int64_t bn, int64_t comm_ctas,
+                   int64_t phase) {
   tn5b::gemm::GemmCall c;
-  c.M = int(M); c.N = int(N); c.bn = int(bn); c.mode = int(mode);
-  c.ag = 1;
+  c.M = int(M); c.N = int(N); c.K = int(K); c.mode = int(mode); c.ag = int(ag); c.bn = int(bn);
+  c.comm_ctas = int(comm_ctas); c.phase = int(phase);
   return tn5b::gemm::grid_ctas(c);
+}
+
+// Number of SMs of the current device.
+int64_t sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
 }
 
 }  // namespace
@@ -166,8 +281,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using nogil = pybind11::call_guard<pybind11::gil_scoped_release>;
   m.def("gemm", &gemm, "tcgen05 BF16 GEMM with fused epilogue", nogil());
   m.def("gemm_rs_push", &gemm_rs_push, "tcgen05 GEMM whose epilogue pushes tiles to owners", nogil());
-  m.def("ag_gemm", &ag_gemm, "all-gather fused into a tcgen05 GEMM", nogil());
-  m.def("gemm_grid", &gemm_grid, "persistent grid size of a GEMM call");
+  m.def("gemm_rs_pull", &gemm_rs_pull, "tcgen05 GEMM with in-launch pull reduce-scatter", nogil());
+  m.def("ag_gemm", &ag_gemm, "all-gather (in-launch pull) fused into a tcgen05 GEMM", nogil());
+  m.def("sm_count", &sm_count, "number of SMs of the current device");
+  m.def("fused_grid", &fused_grid, "grid of a fused GEMM launch (GEMM + communication CTAs)");
   register_kernels(m);
   register_comm(m);
 }

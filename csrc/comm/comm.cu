@@ -234,7 +234,78 @@ __global__ void __launch_bounds__(256) copy16_kernel(uint4* __restrict__ dst, co
   }
   for (; i < n16; i += stride) dst[i] = __ldg(src + i);
 }
+
+// Bulk-engine copy: one elected thread per CTA streams `chunk`-byte pieces of
+// `src` (this GPU's memory or a peer's CUDA-IPC mapping; untiled bulk loads,
+// no multicast) through a `stages`-deep shared-memory ring and writes each
+// piece to `dst` (this GPU's memory) with an untiled bulk store.  CTA c copies
+// pieces c, c + grid, ... so every CTA sweeps the whole buffer in step.
+__global__ void __launch_bounds__(32) bulk_copy_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src,
+                                                       int64_t bytes, int chunk, int stages, uint64_t timeout_ns,
+                                                       int* status) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[16];
+  if (threadIdx.x != 0) return;
+  for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+  fence_mbar_init();
+  const int64_t pieces = (bytes + chunk - 1) / chunk;
+  auto piece_bytes = [&](int64_t p) { const int64_t left = bytes - p * chunk; return uint32_t(left < chunk ? left : chunk); };
+  int64_t issued = 0, done = 0;  // per-CTA piece counters
+  const int64_t mine = pieces > blockIdx.x ? (pieces - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  for (; issued < mine && issued < stages; ++issued) {
+    const int64_t p = blockIdx.x + issued * gridDim.x;
+    const int s = int(issued % stages);
+    mbar_arrive_expect_tx(&full[s], piece_bytes(p));
+    bulk_load(ring + int64_t(s) * chunk, src + p * chunk, piece_bytes(p), &full[s]);
+  }
+  bool ok = true;
+  for (; done < mine; ++done) {
+    const int s = int(done % stages);
+    const uint32_t parity = uint32_t((done / stages) & 1);
+    if (!mbar_wait(&full[s], parity, timeout_ns, status, kTimeoutPeerFlag, nullptr)) {
+      ok = false;
+      break;
+    }
+    const int64_t p = blockIdx.x + done * gridDim.x;
+    bulk_store(dst + p * chunk, smem_u32(ring + int64_t(s) * chunk), piece_bytes(p));
+    bulk_commit_group();
+    if (issued < mine) {
+      bulk_wait_group_read<0>();  // the store has read stage s: refill it
+      const int64_t q = blockIdx.x + issued * gridDim.x;
+      mbar_arrive_expect_tx(&full[s], piece_bytes(q));
+      bulk_load(ring + int64_t(s) * chunk, src + q * chunk, piece_bytes(q), &full[s]);
+      ++issued;
+    }
+  }
+  if (!ok) {
+    // Abort: let every issued load land before the CTA exits (bounded).
+    for (; done < issued; ++done)
+      mbar_wait(&full[done % stages], uint32_t((done / stages) & 1), timeout_ns, status, kTimeoutDrain, nullptr);
+  }
+  bulk_wait_group_all();
+}
 }  // namespace
+
+int bulk_copy(void* dst, const void* src, int64_t bytes, int ctas, int chunk, int stages, uint64_t timeout_ns,
+              int* status, cudaStream_t stream) {
+  if (bytes <= 0 || bytes % 16 || chunk <= 0 || chunk % 16 || stages < 1 || stages > 16 || ctas <= 0 ||
+      (reinterpret_cast<uintptr_t>(dst) & 15) || (reinterpret_cast<uintptr_t>(src) & 15))
+    return -1;
+  const int64_t smem = int64_t(chunk) * stages;
+  if (smem > 200 * 1024) return -1;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !configured[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(bulk_copy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return int(e);
+    if (dev < 64) configured[dev] = true;
+  }
+  bulk_copy_kernel<<<ctas, 32, smem, stream>>>(static_cast<uint8_t*>(dst), static_cast<const uint8_t*>(src),
+                                                bytes, chunk, stages, timeout_ns, status);
+  return int(cudaGetLastError());
+}
 
 int copy16(void* dst, const void* src, int64_t bytes, int ctas, cudaStream_t stream) {
   if (bytes <= 0 || bytes % 16 || (reinterpret_cast<uintptr_t>(dst) & 15) || (reinterpret_cast<uintptr_t>(src) & 15))

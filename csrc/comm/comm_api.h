@@ -39,6 +39,11 @@ namespace tn5b {
 namespace comm {
 // 16-byte-aligned device copy (dst may be a peer's IPC-mapped memory); ctas <= 0: 4 per SM.
 int copy16(void* dst, const void* src, int64_t bytes, int ctas, cudaStream_t stream);
+// Bulk-engine copy through shared memory (src may be a peer's IPC mapping; untiled
+// bulk loads without multicast; dst is this GPU's memory): `ctas` CTAs of one
+// issuing thread, `stages` x `chunk` bytes in flight per CTA.
+int bulk_copy(void* dst, const void* src, int64_t bytes, int ctas, int chunk, int stages, uint64_t timeout_ns,
+              int* status, cudaStream_t stream);
 int wait_probe(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status,
                cudaStream_t stream);
 }  // namespace comm

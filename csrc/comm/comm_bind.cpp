@@ -53,6 +53,26 @@ void copy_to_ptr(int64_t dst, const at::Tensor& src, int64_t bytes, int64_t ctas
   TORCH_CHECK(code == 0, "copy_to_ptr failed (", code, ")");
 }
 
+// Raw pointer to raw pointer copy with this framework's 16-byte copy kernel
+// (either side may be a peer's IPC mapping: push when dst is remote, pull when
+// src is remote).
+void copy_ptr(int64_t dst, int64_t src, int64_t bytes, int64_t ctas) {
+  const int code = tn5b::comm::copy16(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes,
+                                      int(ctas), at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(code == 0, "copy_ptr failed (", code, ")");
+}
+
+// Bulk-engine pull/copy: src may be a peer's memory, dst is local.
+void bulk_copy(int64_t dst, int64_t src, int64_t bytes, int64_t ctas, int64_t chunk, int64_t stages,
+               int64_t timeout_ns, const at::Tensor& status) {
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "status must be a CUDA int32 tensor");
+  const c10::cuda::CUDAGuard guard(status.device());
+  const int code = tn5b::comm::bulk_copy(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes,
+                                         int(ctas), int(chunk), int(stages), uint64_t(timeout_ns),
+                                         status.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(code == 0, "bulk_copy failed (", code < 0 ? "bad arguments" : cudaGetErrorString(cudaError_t(code)), ")");
+}
+
 void rs_reduce(int64_t recv, int64_t flags, int64_t slot_bytes, int64_t rank, int64_t world,
                int64_t rows, int64_t n, int64_t tile_n, int64_t chunk_rows, bool quantized,
                int64_t epoch, at::Tensor& out, const c10::optional<at::Tensor>& residual,
@@ -113,4 +133,6 @@ void register_comm(pybind11::module& m) {
   m.def("rs_reduce", &rs_reduce, nogil());
   m.def("wait_probe", &wait_probe, nogil());
   m.def("copy_to_ptr", &copy_to_ptr, nogil());
+  m.def("copy_ptr", &copy_ptr, nogil());
+  m.def("bulk_copy", &bulk_copy, nogil());
 }

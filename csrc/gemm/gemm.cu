@@ -71,9 +71,12 @@ int sm_count() {
 
 template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false, bool WIDE = false>
 int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUtensorMap& mb,
-           const CUtensorMap& mo, int grid, cudaStream_t stream) {
+           const CUtensorMap& mo, const CUtensorMap& ma2, int grid, cudaStream_t stream) {
   using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR, WIDE, kStagingBuffers<MODE>>;
   static_assert(L::kTotal <= 232448, "dynamic shared memory above the 227 KB per-block limit");
+  static_assert(!(MODE == kModeRsPull || AG) || L::kTotal >= 1024 + kCommStages * (kPiece + 16) + 16,
+                "communication CTAs need their ring in the same dynamic shared memory");
+  if (grid <= 0) return 0;
   auto kern = gemm_kernel<BN, STAGES, EPI_COLS, MODE, AG, PAIR, WIDE>;
   static bool configured[64] = {false};
   int dev = 0;
@@ -84,7 +87,7 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
     if (e != cudaSuccess) return int(e);
     if (dev < 64) configured[dev] = true;
   }
-  const int threads = kThreads + (AG ? 32 : 0);
+  const int threads = kThreads;
   if constexpr (PAIR) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(grid), 1, 1);
@@ -98,9 +101,9 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return int(cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, p, c.a_mn, c.b_mn));
+    return int(cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, ma2, p, c.a_mn, c.b_mn));
   } else {
-    kern<<<grid, threads, L::kTotal, stream>>>(ma, mb, mo, p, c.a_mn, c.b_mn);
+    kern<<<grid, threads, L::kTotal, stream>>>(ma, mb, mo, ma2, p, c.a_mn, c.b_mn);
     return int(cudaGetLastError());
   }
 }
@@ -143,21 +146,31 @@ int pick_bn(const GemmCall& c) {
 
 std::string last_error() { return g_last_error; }
 
-int grid_ctas(const GemmCall& c) {
+int comm_active(const GemmCall& c) {
+  const bool comm_mode = c.mode == 3 || c.ag;
+  return (comm_mode && (c.phase & 3)) ? c.comm_ctas : 0;
+}
+
+int gemm_ctas(const GemmCall& c) {
+  if (!(c.phase & 4)) return 0;
   const int bn = pick_bn(c);
   const int kind = tile_kind(c, bn);
   const bool pair = kind != kSingle;
   const int tile_m = pair ? 2 * kBM : kBM;
   const int tile_n = kind == kWide ? 2 * bn : bn;
   const long tiles = long((c.M + tile_m - 1) / tile_m) * ((c.N + tile_n - 1) / tile_n);
-  int g = sm_count();
+  const bool comm_mode = c.mode == 3 || c.ag;
+  int g = sm_count() - (comm_mode ? c.comm_ctas : 0);
   if (c.max_ctas > 0 && c.max_ctas < g) g = c.max_ctas;
+  if (g < (pair ? 2 : 1)) g = pair ? 2 : 1;
   if (pair) {
     const long clusters = tiles < g / 2 ? tiles : g / 2;
     return int(2 * clusters);
   }
   return int(tiles < g ? tiles : g);
 }
+
+int grid_ctas(const GemmCall& c) { return gemm_ctas(c) + comm_active(c); }
 
 int run(const GemmCall& c, cudaStream_t stream) {
   if (c.M <= 0 || c.N <= 0 || c.K <= 0) return fail("gemm: non-positive M/N/K");
@@ -200,7 +213,40 @@ int run(const GemmCall& c, cudaStream_t stream) {
   p.status = c.status;
   p.timeout_ns = c.timeout_ns;
   p.debug = c.debug;
-  if (c.mode != 0) {
+  p.cta_stamps = c.cta_stamps;
+  p.gemm_ctas = gemm_ctas(c);
+  p.comm_ctas = comm_active(c);
+  if ((p.comm_ctas & 1) && pair) return fail("gemm: CTA-pair tiles need an even number of communication CTAs");
+  if (c.mode == 3) {
+    if (!c.rs_partial_local || !c.rs_partials || !c.rs_flags || !c.rs_my_flags || !c.rs_out || c.world < 1 ||
+        c.M % c.world)
+      return fail("gemm-rs-pull: bad args");
+    const int rows = c.M / c.world;
+    if (rows % kBM || c.N % 256) return fail("gemm-rs-pull: rows per destination % 128 and N % 256 required");
+    if ((c.phase & 2) && c.comm_ctas < 1) return fail("gemm-rs-pull: the reduce phase needs comm_ctas >= 1");
+    if ((reinterpret_cast<uintptr_t>(c.rs_partial_local) | reinterpret_cast<uintptr_t>(c.rs_out)) & 15)
+      return fail("gemm-rs-pull: partial and output must be 16-byte aligned");
+    if (c.rs_residual && (reinterpret_cast<uintptr_t>(c.rs_residual) & 15))
+      return fail("gemm-rs-pull: residual must be 16-byte aligned");
+    if (c.rs_bias && (reinterpret_cast<uintptr_t>(c.rs_bias) & 15))
+      return fail("gemm-rs-pull: bias must be 16-byte aligned");
+    p.rs.flags = c.rs_flags;
+    p.rs.rank = c.rank; p.rs.world = c.world;
+    p.rs.rows_per_dest = rows; p.rs.chunk_rows = c.chunk_rows;
+    p.rs.epoch = c.epoch;
+    if (c.delay_ns > 100000000ull) return fail("gemm-rs: diagnostic delay above 100 ms");
+    p.rs.delay_tile = c.delay_tile; p.rs.delay_ns = c.delay_ns;
+    p.pull.partial = c.rs_partials;
+    p.pull.my_flags = c.rs_my_flags;
+    p.pull.order = c.rs_consumer_order;
+    p.pull.tiles_n = c.N / tile_n;
+    p.pull.tiles_per_dest = (rows / kBM) * p.pull.tiles_n;
+    p.pull.out = static_cast<__nv_bfloat16*>(c.rs_out);
+    p.pull.residual = static_cast<const __nv_bfloat16*>(c.rs_residual);
+    p.pull.bias = static_cast<const __nv_bfloat16*>(c.rs_bias);
+    p.pull.stamps = c.rs_stamps;
+    p.pull.produced = c.rs_produced;
+  } else if (c.mode != 0) {
     if (!c.rs_recv || !c.rs_flags || c.world < 1 || c.M % c.world) return fail("gemm-rs: bad args");
     const int rows = c.M / c.world;
     if (rows % kBM) return fail("gemm-rs: rows per destination must be a multiple of 128");
@@ -214,16 +260,31 @@ int run(const GemmCall& c, cudaStream_t stream) {
     p.rs.delay_tile = c.delay_tile; p.rs.delay_ns = c.delay_ns;
   }
   if (c.ag) {
-    if (!c.ag_chunk_flags || !c.ag_gather || !c.ag_peer_flags || !c.ag_shard || c.M % c.world)
+    if (!c.ag_shard || !c.ag_gather || !c.ag_published || !c.ag_pulled || !c.ag_published_local ||
+        !c.ag_pulled_local || !c.ag_ready || !c.ag_own_done || c.world < 2 || c.M % c.world || c.a_mn)
       return fail("ag-gemm: bad args");
-    if ((c.M / c.world) % kBM) return fail("ag-gemm: rows per source must be a multiple of 128");
-    if (c.ag_shard_bytes % 16 || reinterpret_cast<uintptr_t>(c.ag_shard) & 15)
-      return fail("ag-gemm: shard must be 16-byte aligned and sized");
-    p.ag.chunk_flags = c.ag_chunk_flags; p.ag.target = c.ag_target;
-    p.ag.rank = c.rank; p.ag.world = c.world; p.ag.rows_per_src = c.M / c.world;
-    p.ag.shard = static_cast<const uint8_t*>(c.ag_shard);
-    p.ag.shard_bytes = c.ag_shard_bytes;
-    p.ag.gather = c.ag_gather; p.ag.peer_flags = c.ag_peer_flags;
+    const int rows = c.M / c.world;
+    if (rows % kBM) return fail("ag-gemm: rows per source must be a multiple of 128");
+    if (reinterpret_cast<uintptr_t>(c.ag_shard) & 15 || c.lda != c.K)
+      return fail("ag-gemm: shard must be 16-byte aligned and the gather buffer dense [M, K]");
+    if ((c.phase & 3) && c.comm_ctas < 1) return fail("ag-gemm: the gather phases need comm_ctas >= 1");
+    GatherArgs& g = p.gather;
+    g.gather = c.ag_gather;
+    g.published = c.ag_published;
+    g.pulled = c.ag_pulled;
+    g.published_local = c.ag_published_local;
+    g.pulled_local = c.ag_pulled_local;
+    g.ready = c.ag_ready;
+    g.own_done = c.ag_own_done;
+    g.shard = static_cast<const uint8_t*>(c.ag_shard);
+    g.chunk_bytes = int64_t(rows) * c.K * 2;
+    g.rank = c.rank; g.world = c.world; g.rows_per_src = rows; g.K = c.K;
+    g.epoch = c.ag_epoch;
+    g.own_target = c.ag_own_target;
+    g.pulled_target = c.ag_pulled_target;
+    g.ready_target = c.ag_ready_target;
+    g.phase = c.phase;
+    g.block_stamps = c.ag_block_stamps;
   }
   CUtensorMap ma, mb;
   const bool ok_a = c.a_mn ? make_map(&ma, c.A, c.M, c.K, c.lda, 64, 64)
@@ -231,28 +292,42 @@ int run(const GemmCall& c, cudaStream_t stream) {
   const bool ok_b = c.b_mn ? make_map(&mb, c.B, c.N, c.K, c.ldb, 64, 64)
                            : make_map(&mb, c.B, c.K, c.N, c.ldb, 64, pair ? bn / 2 : bn);
   if (!ok_a || !ok_b) return fail("gemm: cuTensorMapEncodeTiled failed");
-  // Output tensor map for the TMA-store epilogue (local mode, aligned output).
+  // Output tensor map for the TMA-store epilogue (local mode, aligned output);
+  // in the pull reduce-scatter it maps this rank's partial buffer as a
+  // [M/128 * N/64 * 128, 64] matrix of 128 x 64 pieces.
   CUtensorMap mo = ma;
   p.tma_store = 0;
-  if (c.mode == 0 && c.out && !(reinterpret_cast<uintptr_t>(c.out) & 15) && c.ldo % 8 == 0 &&
-      make_map(&mo, c.out, c.N, c.M, c.ldo, 64, 32))
+  if (c.mode == 3) {
+    const uint64_t piece_rows = uint64_t(c.M / kBM) * uint64_t(c.N / 64) * kBM;
+    if (!make_map(&mo, c.rs_partial_local, 64, piece_rows, 64, 64, 32))
+      return fail("gemm-rs-pull: partial tensor map");
     p.tma_store = 1;
+  } else if (c.mode == 0 && c.out && !(reinterpret_cast<uintptr_t>(c.out) & 15) && c.ldo % 8 == 0 &&
+             make_map(&mo, c.out, c.N, c.M, c.ldo, 64, 32)) {
+    p.tma_store = 1;
+  }
+  // AG: the own chunk is read straight from the shard ([M/W, K]).
+  CUtensorMap ma2 = ma;
+  if (c.ag && !make_map(&ma2, c.ag_shard, c.K, c.M / c.world, c.K, 64, kBM))
+    return fail("ag-gemm: shard tensor map");
   const int grid = grid_ctas(c);
   if (c.ag) {
-    if (pair) return launch<256, 6, 64, kModeLocal, true, true>(c, p, ma, mb, mo, grid, stream);
-    if (bn == 256) return launch<256, 4, 64, kModeLocal, true>(c, p, ma, mb, mo, grid, stream);
-    return launch<128, 6, 64, kModeLocal, true>(c, p, ma, mb, mo, grid, stream);
+    if (pair) return launch<256, 6, 64, kModeLocal, true, true>(c, p, ma, mb, mo, ma2, grid, stream);
+    if (bn == 256) return launch<256, 4, 64, kModeLocal, true>(c, p, ma, mb, mo, ma2, grid, stream);
+    return launch<128, 6, 64, kModeLocal, true>(c, p, ma, mb, mo, ma2, grid, stream);
   }
   switch (c.mode) {
     case 0:
-      if (kind == kWide) return launch<256, 4, 64, kModeLocal, false, true, true>(c, p, ma, mb, mo, grid, stream);
-      if (pair) return launch<256, 6, 64, kModeLocal, false, true>(c, p, ma, mb, mo, grid, stream);
-      if (bn == 256) return launch<256, 4, 64, kModeLocal, false>(c, p, ma, mb, mo, grid, stream);
-      return launch<128, 6, 64, kModeLocal, false>(c, p, ma, mb, mo, grid, stream);
+      if (kind == kWide) return launch<256, 4, 64, kModeLocal, false, true, true>(c, p, ma, mb, mo, ma2, grid, stream);
+      if (pair) return launch<256, 6, 64, kModeLocal, false, true>(c, p, ma, mb, mo, ma2, grid, stream);
+      if (bn == 256) return launch<256, 4, 64, kModeLocal, false>(c, p, ma, mb, mo, ma2, grid, stream);
+      return launch<128, 6, 64, kModeLocal, false>(c, p, ma, mb, mo, ma2, grid, stream);
     case 1:
-      return launch<256, 4, 64, kModeRsPush, false>(c, p, ma, mb, mo, grid, stream);
+      return launch<256, 4, 64, kModeRsPush, false>(c, p, ma, mb, mo, ma2, grid, stream);
     case 2:
-      return launch<256, 4, 128, kModeRsTaco, false>(c, p, ma, mb, mo, grid, stream);
+      return launch<256, 4, 128, kModeRsTaco, false>(c, p, ma, mb, mo, ma2, grid, stream);
+    case 3:
+      return launch<256, 4, 64, kModeRsPull, false>(c, p, ma, mb, mo, ma2, grid, stream);
     default:
       return fail("gemm: unknown mode");
   }

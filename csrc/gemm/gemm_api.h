@@ -38,22 +38,47 @@ struct GemmCall {
   int64_t slot_bytes = 0;
   int delay_tile = -1;         // diagnostic: bounded publication delay of one tile
   uint64_t delay_ns = 0;
-  // all-gather
+  // Communication role (pull transports): CTAs [gemm_ctas, grid) move data over
+  // NVLink inside the same launch.  `phase` selects what a launch runs:
+  // bit0 AG own chunk + publish, bit1 AG peer pulls / RS reduce, bit2 the GEMM
+  // (7: everything in one launch; tests emulating several ranks on one GPU run
+  // the phases as separate launches so that no launch waits on another).
+  int comm_ctas = 0;
+  int phase = 7;
+  // GEMM -> reduce-scatter, pull (mode 3)
+  void* rs_partial_local = nullptr;               // this rank's partial buffer [M/128][N/64][128][64]
+  const uint8_t* const* rs_partials = nullptr;    // device array [world]: every rank's partial buffer
+  const uint32_t* rs_my_flags = nullptr;          // this rank's flags [world][tiles_per_dest]
+  const int* rs_consumer_order = nullptr;         // consumption order of local flag tiles
+  void* rs_out = nullptr;                         // [M/world, N]
+  const void* rs_residual = nullptr;              // optional [M/world, N]
+  const void* rs_bias = nullptr;                  // optional [N]
+  unsigned long long* rs_stamps = nullptr;        // optional per-local-tile completion times
+  unsigned long long* rs_produced = nullptr;      // optional per-produced-tile publication times
+  // all-gather -> GEMM, pull: A is this rank's gather buffer [M, K]
   int ag = 0;
-  const uint32_t* ag_chunk_flags = nullptr;
-  uint32_t ag_target = 0;
-  const void* ag_shard = nullptr;
-  int64_t ag_shard_bytes = 0;
-  uint8_t* const* ag_gather = nullptr;
-  uint32_t* const* ag_peer_flags = nullptr;
+  const void* ag_shard = nullptr;                 // [M/world, K] local shard (contiguous)
+  uint8_t* const* ag_gather = nullptr;            // device array [world]: gather buffers
+  uint32_t* const* ag_published = nullptr;        // device array [world]: published[world] flags
+  uint32_t* const* ag_pulled = nullptr;           // device array [world]: pulled counters
+  const uint32_t* ag_published_local = nullptr;
+  const uint32_t* ag_pulled_local = nullptr;
+  uint32_t* ag_ready = nullptr;                   // local [world][M/world/128]
+  uint32_t* ag_own_done = nullptr;                // local [1]
+  uint32_t ag_epoch = 0, ag_own_target = 0, ag_pulled_target = 0, ag_ready_target = 0;
+  unsigned long long* ag_block_stamps = nullptr;  // optional: arrival time of every gathered block
+  unsigned long long* cta_stamps = nullptr;       // optional [grid][2]: start / end of every CTA
   // status / bounded waits
   int* status = nullptr;
   uint64_t timeout_ns = 10ull * 1000 * 1000 * 1000;
   unsigned long long* debug = nullptr;  // optional per-CTA cycle counters (4 per CTA)
 };
 
-// Number of CTAs the persistent kernel will launch for this call.
+// Number of CTAs the persistent kernel will launch for this call (GEMM CTAs
+// plus communication CTAs).
 int grid_ctas(const GemmCall& c);
+// GEMM-role CTAs of this call (0 when the call runs communication phases only).
+int gemm_ctas(const GemmCall& c);
 int run(const GemmCall& c, cudaStream_t stream);
 std::string last_error();
 

@@ -55,6 +55,8 @@ enum Mode : int {
   kModeLocal = 0,      // plain store into C
   kModeRsPush = 1,     // GEMM -> reduce-scatter: BF16 tile pushed to its owner rank
   kModeRsTaco = 2,     // GEMM -> reduce-scatter: remote tiles TACO-encoded, then pushed
+  kModeRsPull = 3,     // GEMM -> reduce-scatter: partial tiles stored locally and published;
+                       // the owner's reducer CTAs (same launch) pull and reduce them
 };
 
 struct RsArgs {
@@ -73,16 +75,40 @@ struct RsArgs {
   uint64_t delay_ns;
 };
 
-struct AgArgs {
-  // AG->GEMM: A rows [c*rows_per_src, (c+1)*rows_per_src) arrive from rank c.
-  const uint32_t* chunk_flags;   // local counters [world]
-  uint32_t target;               // wait until chunk_flags[c] >= target
-  int rank, world, rows_per_src;
-  // push side (comm warp): copy local shard to every rank's gather buffer
-  const uint8_t* shard;          // local [rows_per_src, K] bf16 rows (contiguous)
-  int64_t shard_bytes;
-  uint8_t* const* gather;        // device array [world] of gather buffer bases
-  uint32_t* const* peer_flags;   // device array [world] of chunk_flags bases
+// All-gather -> GEMM (pull): chunk c of the gathered A ([M/W rows, K] of rank
+// c) arrives in this rank's gather buffer in 16 KB pieces; ready[c][block]
+// counts the arrived pieces of each 128-row block (cumulative over calls).
+struct GatherArgs {
+  uint8_t* const* gather;          // device array [world]: every rank's gather buffer ([M, K] bf16)
+  uint32_t* const* published;      // device array [world]: every rank's published[world] flags
+  uint32_t* const* pulled;         // device array [world]: every rank's pulled counter
+  const uint32_t* published_local; // this rank's published[world]
+  const uint32_t* pulled_local;    // this rank's pulled counter
+  uint32_t* ready;                 // local [world][rows_per_src / 128] arrived-piece counters
+  uint32_t* own_done;              // local counter of gatherer CTAs done with the own chunk
+  const uint8_t* shard;            // local shard [rows_per_src, K] bf16 (contiguous)
+  int64_t chunk_bytes;             // rows_per_src * K * 2
+  int rank, world, rows_per_src, K;
+  uint32_t epoch;                  // this call's epoch (published flags)
+  uint32_t own_target;             // own_done value once every gatherer CTA of this call is done
+  uint32_t pulled_target;          // pulled value once every peer finished reading the previous call
+  uint32_t ready_target;           // ready[c][b] once block b of chunk c has fully arrived
+  int phase;                       // communication CTAs: bit0 own chunk + publish, bit1 pull peers
+  unsigned long long* block_stamps; // optional [world * rows_per_src / 128]: when each block fully arrived
+};
+
+// GEMM -> reduce-scatter (pull): the reducer CTAs' view.  Flags are per
+// "flag tile" of 128 rows x tile_n columns of the owner's rows.
+struct PullRsArgs {
+  const uint8_t* const* partial;   // device array [world]: partial buffers, [M/128][N/64][128][64] bf16
+  const uint32_t* my_flags;        // local [world][tiles_per_dest]
+  const int* order;                // consumption order of local flag tiles (null: 0, 1, ...)
+  int tiles_per_dest, tiles_n;     // flag tiles per destination / per row
+  __nv_bfloat16* out;              // [rows_per_dest, N]
+  const __nv_bfloat16* residual;   // optional [rows_per_dest, N]
+  const __nv_bfloat16* bias;       // optional [N]
+  unsigned long long* stamps;      // optional: %globaltimer at each local flag tile's completion
+  unsigned long long* produced;    // optional: %globaltimer at each produced flag tile's publication
 };
 
 struct Params {
@@ -97,7 +123,11 @@ struct Params {
   const __nv_bfloat16* bias;
   const __nv_bfloat16* residual; int64_t ld_res;
   RsArgs rs;
-  AgArgs ag;
+  GatherArgs gather;
+  PullRsArgs pull;
+  int comm_ctas;                 // CTAs [0, comm_ctas) run the communication role (dispatched first:
+                                 // GEMM CTAs may wait on them, never the reverse)
+  int gemm_ctas;                 // CTAs [comm_ctas, comm_ctas + gemm_ctas) compute
   int tma_store;                 // local mode: store the output tile with TMA (tmap_out)
   int* status;
   uint64_t timeout_ns;
@@ -106,6 +136,8 @@ struct Params {
   // [3] epilogue wait for an accumulator (summed over its warps), [4] MMA wait
   // for a drained accumulator.
   unsigned long long* debug;
+  // Optional [grid][2] %globaltimer stamps: start and end of every CTA (profiling).
+  unsigned long long* cta_stamps;
 };
 
 template <int BN, int STAGES, int EPI_COLS, bool PAIR = false, bool WIDE = false, int STG_BUFS = 1>
@@ -256,16 +288,31 @@ __device__ __forceinline__ uint32_t code(float x, float quant) {
 // the next tile's MMAs wait for the epilogue (used for long K loops).
 // Local-mode epilogues store the output tile with TMA (double-buffered staging
 // per warp: the store of one 32 x EPI_COLS chunk overlaps the next chunk).
-template <int MODE>
-constexpr int kStagingBuffers = MODE == kModeLocal ? 2 : 1;
+template <int BN, bool WIDE>
+constexpr int kTileNOf = BN * (WIDE ? 2 : 1);
 
+template <int MODE>
+constexpr int kStagingBuffers = (MODE == kModeLocal || MODE == kModeRsPull) ? 2 : 1;
+
+}  // namespace gemm
+}  // namespace tn5b
+#include "comm_roles.cuh"
+namespace tn5b {
+namespace gemm {
+
+// AG: the A rows of chunk `rank` are read from the local shard (tmap_a2), the
+// other chunks from the local gather buffer (tmap_a) once they have arrived.
+// kModeRsPull: tmap_out maps the local partial buffer as a [M/128 * N/64 * 128, 64]
+// matrix (tile-major pieces the reducer pulls with single bulk loads).
 template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false, bool WIDE = false>
-__global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_out,
-                const __grid_constant__ Params p, int a_mn, int b_mn) {
+                const __grid_constant__ CUtensorMap tmap_a2, const __grid_constant__ Params p, int a_mn,
+                int b_mn) {
   using L = SmemLayout<BN, STAGES, EPI_COLS, PAIR, WIDE, kStagingBuffers<MODE>>;
-  static_assert(!PAIR || MODE == kModeLocal, "CTA pairs serve the local-store epilogue");
+  static_assert(!PAIR || MODE == kModeLocal || MODE == kModeRsPull,
+                "CTA pairs serve the local-store epilogues (plain and reduce-scatter partial)");
   static_assert(!WIDE || PAIR, "the wide tile is a CTA-pair tile");
   constexpr int kSub = WIDE ? 2 : 1;               // N=BN MMAs per K step
   constexpr int kTileN = BN * kSub;
@@ -276,9 +323,21 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
   constexpr int kBRows = PAIR ? BN / 2 : BN;
   static_assert(BN % EPI_COLS == 0, "epilogue chunks must tile BN");
   static_assert(MODE != kModeRsTaco || EPI_COLS == 128, "TACO groups are 128 columns");
+  static_assert(MODE != kModeRsPull || EPI_COLS == 64, "partial pieces are 64 columns wide");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  if (p.cta_stamps && threadIdx.x == 0) p.cta_stamps[2 * blockIdx.x] = globaltimer_ns();
+  if (int(blockIdx.x) < p.comm_ctas) {
+    // Communication role (no TMEM, no cluster barriers).
+    if constexpr (MODE == kModeRsPull) rs_reducer<kTileNOf<BN, WIDE> / 64>(p, smem);
+    else if constexpr (AG) ag_gatherer(p, smem);
+    if (p.cta_stamps) {
+      __syncthreads();
+      if (threadIdx.x == 0) p.cta_stamps[2 * blockIdx.x + 1] = globaltimer_ns();
+    }
+    return;
+  }
   uint8_t* stage_base = smem;
   uint8_t* staging = smem + STAGES * L::kStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(staging + L::kStagingBytes);
@@ -294,8 +353,9 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
   const int lane = threadIdx.x % 32;
   const uint32_t cta_rank = PAIR ? cluster_ctarank() : 0u;
   const bool leader = cta_rank == 0;
-  const int cluster_id = PAIR ? int(blockIdx.x / 2) : int(blockIdx.x);
-  const int clusters = PAIR ? int(gridDim.x / 2) : int(gridDim.x);
+  const int gid = int(blockIdx.x) - p.comm_ctas;  // GEMM CTA index (comm_ctas is even with CTA pairs)
+  const int cluster_id = PAIR ? gid / 2 : gid;
+  const int clusters = PAIR ? p.gemm_ctas / 2 : p.gemm_ctas;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -313,6 +373,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if constexpr (AG) tma_prefetch_desc(&tmap_a2);
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -344,17 +405,28 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         tile_coords(p, t, tm, tn);
         const int row_a = tm * kTileM + int(cta_rank) * kBM;   // this CTA's A rows
         const int row_b = tn * kTileN + int(cta_rank) * kBRows;  // this CTA's B rows (sub-tile 0)
+        // A operand of this tile: AG reads its own chunk from the shard and waits
+        // (bounded) until a peer chunk's 128-row block has fully arrived locally.
+        const CUtensorMap* ta = &tmap_a;
+        int ya = row_a;
         if constexpr (AG) {
-          const int chunk = row_a / p.ag.rows_per_src;
-          if (chunk != waited_chunk) {
-            if (!wait_flag_geq(p.ag.chunk_flags + chunk, p.ag.target, p.timeout_ns, p.status,
-                               kTimeoutAgChunk)) {
-              *abort_flag = 1;
-              ok = false;
-              break;
+          const int chunk = row_a / p.gather.rows_per_src;
+          const int in_chunk = row_a - chunk * p.gather.rows_per_src;
+          if (chunk == p.gather.rank) {
+            ta = &tmap_a2;
+            ya = in_chunk;
+          } else {
+            const int blk = chunk * (p.gather.rows_per_src / 128) + in_chunk / 128;
+            if (blk != waited_chunk) {
+              if (!wait_flag_geq(p.gather.ready + blk, p.gather.ready_target, p.timeout_ns, p.status,
+                                 kTimeoutAgChunk)) {
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+              fence_proxy_async_global();
+              waited_chunk = blk;
             }
-            fence_proxy_async_global();
-            waited_chunk = chunk;
           }
         }
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
@@ -375,7 +447,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
             const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
             if (!a_mn) {
-              tma_load_2d_pair(sa, &tmap_a, fb, k0, row_a);
+              tma_load_2d_pair(sa, ta, fb, k0, ya);
             } else {
 #pragma unroll
               for (int c = 0; c < kBM / 64; ++c) tma_load_2d_pair(sa + c * 8192, &tmap_a, fb, row_a + c * 64, k0);
@@ -394,7 +466,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
           } else {
             mbar_arrive_expect_tx(&full[s], L::kStageBytes);
             if (!a_mn) {
-              tma_load_2d(sa, &tmap_a, &full[s], k0, row_a);
+              tma_load_2d(sa, ta, &full[s], k0, ya);
             } else {
 #pragma unroll
               for (int c = 0; c < kBM / 64; ++c)
@@ -411,7 +483,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
           last_parity[s] = int(ph);
         }
       }
-      if (p.debug) p.debug[blockIdx.x * 8 + 2] = (unsigned long long)dbg_empty;
+      if (p.debug) p.debug[gid * 8 + 2] = (unsigned long long)dbg_empty;
       if (!ok) {
         // Abort path: let every issued TMA load land before the CTA can exit.
         if (!PAIR) {
@@ -496,9 +568,9 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         umma_commit(drain);
       mbar_wait(drain, 0, p.timeout_ns, p.status, kTimeoutDrain, nullptr);
       if (p.debug) {
-        p.debug[blockIdx.x * 8 + 0] = (unsigned long long)dbg_full;
-        p.debug[blockIdx.x * 8 + 1] = (unsigned long long)(clock64() - dbg_t0);
-        p.debug[blockIdx.x * 8 + 4] = (unsigned long long)dbg_tempty;
+        p.debug[gid * 8 + 0] = (unsigned long long)dbg_full;
+        p.debug[gid * 8 + 1] = (unsigned long long)(clock64() - dbg_t0);
+        p.debug[gid * 8 + 4] = (unsigned long long)dbg_tempty;
       }
     }
   } else if (warp < kEpiFirstWarp + kEpiWarps) {
@@ -507,7 +579,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
     const int ew = warp - kEpiFirstWarp;          // staging buffer
     uint8_t* stg_base = staging + ew * L::kStagingPerWarp;
     int chunk_seq = 0;  // TMA-store chunks issued by this warp (staging buffer = parity)
-    const bool tma_out = MODE == kModeLocal && p.tma_store;
+    const bool tma_out = (MODE == kModeLocal && p.tma_store) || MODE == kModeRsPull;
     int local = 0;
     for (int t = cluster_id; t < p.num_tiles; t += clusters, ++local) {
       int tm, tn;
@@ -519,7 +591,7 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         const long long we = p.debug ? clock64() : 0;
         ok = mbar_wait(&tfull[b], use & 1, p.timeout_ns, p.status, kTimeoutEpiTmemFull,
                        abort_flag);
-        if (p.debug) atomicAdd(p.debug + blockIdx.x * 8 + 3, (unsigned long long)(clock64() - we));
+        if (p.debug) atomicAdd(p.debug + gid * 8 + 3, (unsigned long long)(clock64() - we));
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
@@ -719,7 +791,10 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmap_out, stg_addr, col0, row_w);
+            if constexpr (MODE == kModeRsPull)  // piece (row block, column chunk), rows q*32..+31
+              tma_store_2d(&tmap_out, stg_addr, 0, ((row_w / 128) * (p.N / 64) + col0 / 64) * 128 + row_w % 128);
+            else
+              tma_store_2d(&tmap_out, stg_addr, col0, row_w);
             bulk_commit_group();
           }
           ++chunk_seq;
@@ -755,7 +830,32 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
         __syncwarp();
       }
 
-      if constexpr (MODE != kModeLocal) {
+      if constexpr (MODE == kModeRsPull) {
+        // Publish this CTA's 128-row flag tile to its owner once all four
+        // epilogue warps' TMA stores have completed in local memory: a
+        // system-scope release of flag[source][flag tile] = epoch on the owner.
+        if (lane == 0) {
+          bulk_wait_group_all();
+          fence_proxy_async_global();
+        }
+        __syncwarp();
+        named_barrier_sync(1, kEpiWarps * 32);
+        if (warp == kEpiFirstWarp && lane == 0) {
+          const int row = tm * kTileM + int(cta_rank) * kBM;
+          const int d = row / p.rs.rows_per_dest;
+          const int tiles_n = p.N / kTileN;
+          const int local_tile = ((row - d * p.rs.rows_per_dest) / kBM) * tiles_n + tn;
+          const int per_dest = (p.rs.rows_per_dest / kBM) * tiles_n;
+          if (p.rs.delay_ns && tm * p.tiles_n + tn == p.rs.delay_tile) {
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < p.rs.delay_ns) __nanosleep(1000);
+          }
+          fence_acq_rel_sys();
+          st_release_sys(p.rs.flags[d] + int64_t(p.rs.rank) * per_dest + local_tile, p.rs.epoch);
+          if (p.pull.produced) p.pull.produced[(row / kBM) * tiles_n + tn] = globaltimer_ns();
+        }
+      }
+      if constexpr (MODE == kModeRsPush || MODE == kModeRsTaco) {
         // Publish the tile to its owner: all four epilogue warps' stores, then
         // one system-scope release of flag[source][tile] = epoch on the owner.
         named_barrier_sync(1, kEpiWarps * 32);
@@ -774,43 +874,12 @@ __global__ void __launch_bounds__(kThreads + (AG ? 32 : 0), 1)
       }
     }
     if (tma_out && lane == 0) bulk_wait_group_all();  // stores complete before the CTA exits
-  } else {
-    // ------------------------------------------- AG push warp (AG mode only)
-    if constexpr (AG) {
-      // This CTA copies its slice of the local shard into every rank's gather
-      // buffer (peers first, own buffer last), then bumps each owner's counter.
-      const int64_t units = p.ag.shard_bytes / 16;
-      const int64_t per = (units + gridDim.x - 1) / gridDim.x;
-      const int64_t lo = int64_t(blockIdx.x) * per;
-      const int64_t hi = min(units, lo + per);
-      for (int step = 1; step <= p.ag.world; ++step) {
-        const int dst = (p.ag.rank + step) % p.ag.world;
-        uint8_t* out = p.ag.gather[dst] + int64_t(p.ag.rank) * p.ag.shard_bytes;
-        // Eight independent 16-byte loads in flight per lane before their stores
-        // (a load->store chain per unit would pay one HBM latency per 512 bytes).
-        constexpr int kUnroll = 8;
-        int64_t u = lo + lane;
-        for (; u + (kUnroll - 1) * 32 < hi; u += kUnroll * 32) {
-          uint4 v[kUnroll];
-#pragma unroll
-          for (int i = 0; i < kUnroll; ++i) v[i] = ld_global_nc_v4(p.ag.shard + (u + i * 32) * 16);
-#pragma unroll
-          for (int i = 0; i < kUnroll; ++i) st_global_v4(out + (u + i * 32) * 16, v[i]);
-        }
-        for (; u < hi; u += 32) st_global_v4(out + u * 16, ld_global_nc_v4(p.ag.shard + u * 16));
-        __syncwarp();
-        if (lane == 0) {
-          fence_acq_rel_sys();
-          red_release_sys_add(p.ag.peer_flags[dst] + p.ag.rank, 1u);
-        }
-        __syncwarp();
-      }
-    }
   }
 
   // ------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
+  if (p.cta_stamps && threadIdx.x == 0) p.cta_stamps[2 * blockIdx.x + 1] = globaltimer_ns();
   if constexpr (PAIR) cluster_sync();  // the leader's MMAs into this CTA's TMEM are done
   if (warp == 1) {
     tc_fence_after();

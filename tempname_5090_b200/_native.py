@@ -7,8 +7,12 @@ be imported, so no CUDA code path silently runs anything else.  CPU-only hosts
 from __future__ import annotations
 
 import threading
+import weakref
 
 _LOCK = threading.Lock()
+# Live fused operators and exchange workspaces (objects with a `failed`
+# attribute): a device-side bounded-wait failure poisons all of them.
+_OPERATORS: "weakref.WeakSet" = weakref.WeakSet()
 _LIB = None
 _ERROR: Exception | None = None
 _STATUS: dict = {}
@@ -71,8 +75,26 @@ def status_tensor(device):
     return t
 
 
+def register_operator(op) -> None:
+    """Track a fused operator or exchange workspace for device-failure poisoning."""
+    _OPERATORS.add(op)
+
+
+def poison_operators() -> int:
+    """Mark every live fused operator and workspace failed; returns how many.
+    After a bounded wait gave up, a peer's late pushes or pulls of that epoch
+    may still be in flight, and cumulative counters are out of step: these
+    objects must be rebuilt, not called again."""
+    n = 0
+    for op in list(_OPERATORS):
+        op.failed = True
+        n += 1
+    return n
+
+
 def check_status(device=None, clear: bool = True) -> None:
-    """Synchronise and raise if any kernel recorded a bounded-wait failure."""
+    """Synchronise and raise if any kernel recorded a bounded-wait failure;
+    every live fused operator and workspace is poisoned first."""
     import torch
     index = torch.cuda.current_device() if device is None else torch.device(device).index
     t = _STATUS.get(index)
@@ -80,9 +102,11 @@ def check_status(device=None, clear: bool = True) -> None:
         return
     code = int(t[0].item())
     if code:
+        poisoned = poison_operators()
         if clear:
             t.zero_()
-        raise RuntimeError(f"device status {code}: {STATUS_MESSAGES.get(code, 'unknown')}")
+        raise RuntimeError(f"device status {code}: {STATUS_MESSAGES.get(code, 'unknown')} "
+                           f"({poisoned} fused operators/workspaces poisoned: rebuild them)")
 
 
 def count_launch(n: int = 1) -> None:

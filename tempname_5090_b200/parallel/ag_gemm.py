@@ -2,40 +2,55 @@
 
     out[M, N] = gather_rows(x_shard)[M, K] @ B[N, K]^T   (+ bias, GeLU, GeLU-backward)
 
-ONE persistent tcgen05 launch per call.  An extra warp in every CTA copies
-that CTA's slice of the local shard into every rank's symmetric gather buffer
-over NVLink (peers first) and bumps the owner's per-source counter with a
-system-scope release; the TMA producer of each CTA waits (bounded) until the
-row chunk of its next tile has fully arrived in LOCAL memory, then loads it
-with TMA -- no TMA load ever reads another GPU's memory.  Tiles of the local
-shard come first, then rank+1, rank+2, ... so the math starts immediately.
+ONE persistent launch per call with two kinds of CTAs:
+
+* `comm_ctas` gatherer CTAs first copy this rank's shard into its own chunk of
+  its symmetric gather buffer and publish it (a system-scope release of
+  `published[rank] = epoch` on every peer), then pull every peer's chunk
+  (rank+1 first) from the peer's gather buffer with bulk loads -- no multicast
+  -- into the local gather buffer, counting the arrived 16 KB pieces of each
+  128-row block;
+* the other CTAs run the tcgen05 GEMM: tiles of the own chunk first, read
+  straight from the shard, then each peer chunk's tiles once their block count
+  is complete (bounded wait), with TMA loads of LOCAL memory only.
+
+Buffer reuse: peers only read this rank's own chunk; every gatherer CTA of a
+peer adds 1 to this rank's `pulled` counter after its last load from it, and
+this rank overwrites its own chunk at call t+1 only once the counter shows
+that every peer finished reading call t's -- a bounded wait inside the kernel,
+so back-to-back calls of one operator are safe without any host barrier.  No
+peer ever writes into this rank's buffer, so `gathered` stays valid until this
+rank's own next call.
 
 The gather buffer doubles as the saved full input of the layer (the
 reference's ColumnLinear saves `gather_rows(x)` for dW, model.py:110-117).
-Counter targets accumulate the sender grid sizes of every call, identical on
-all ranks because every rank issues the same sequence of shapes.
-Buffer reuse across calls follows the same chain argument as GemmRS: a peer
-can overwrite rank r's gather buffer for call t+1 only after r's own call t+1
-push, which r issues after every stream-ordered reader of call t.
+Cumulative counter targets (pieces per block, gatherer CTAs per call) are kept
+on the host; every rank issues the same sequence of calls per operator.
 """
 from __future__ import annotations
 
+import os
 import threading
 
 import torch
 import torch.distributed as dist
 
-from .._native import count_launch, lib, status_tensor
+from .._native import count_launch, lib, register_operator, status_tensor
 from ..ops import gemm as G
 from .symmetric import SymmetricBuffer
 from ..utils import tracing
 
 DEFAULT_TIMEOUT_NS = 10_000_000_000
+DEFAULT_COMM_CTAS = int(os.environ.get("TN5B_AG_COMM_CTAS", "20"))
+PIECE_BYTES = 16384
+CTRL_BYTES = 512          # published[world] u32 at byte 0, pulled u32 at byte 256
+PULLED_OFFSET = 256
 
 
 def ag_tile_order(m: int, n: int, world: int, rank: int, bn: int) -> list:
-    """Own chunk first, then rank+1, ...; inside a chunk, column tiles outer so a
-    weight panel is reused by all row tiles of the chunk."""
+    """Own chunk first, then rank+1, ... (the order chunks arrive in); inside a
+    chunk, column tiles outer so a weight panel is reused by all row tiles of
+    the chunk."""
     rows = m // world
     tm_per = rows // 128
     tn = (n + bn - 1) // bn
@@ -50,28 +65,41 @@ def ag_tile_order(m: int, n: int, world: int, rank: int, bn: int) -> list:
 
 class AGGemm:
     def __init__(self, m: int, k: int, group=None, timeout_ns: int = DEFAULT_TIMEOUT_NS,
-                 _emulate: tuple | None = None, device: torch.device | None = None):
+                 comm_ctas: int | None = None, _emulate: tuple | None = None,
+                 device: torch.device | None = None):
         if _emulate is not None:
-            self.rank, self.world, self.gather, self.flags = _emulate
+            self.rank, self.world, self.gather, self.ctrl = _emulate
         else:
             self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world < 2 or self.world > 64:
+            raise ValueError("the fused all-gather needs 2..64 ranks")
         if m % self.world or (m // self.world) % 128:
             raise ValueError("rows per rank must be a multiple of 128")
         if k % 8:
             raise ValueError("K must be a multiple of 8")
         self.m, self.k, self.group = m, k, group
+        self.comm_ctas = DEFAULT_COMM_CTAS if comm_ctas is None else int(comm_ctas)
+        if not 1 <= self.comm_ctas <= 64:
+            raise ValueError("comm_ctas must be in [1, 64]")
         # `device` defaults to the current CUDA device; CPU serves host-logic tests.
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.timeout_ns = int(timeout_ns)
         if _emulate is None:
             self.gather = SymmetricBuffer(m * k * 2, group)
-            self.flags = SymmetricBuffer(self.world * 4, group)
-        self.flag_total = 0
-        self.calls = 0
+            self.ctrl = SymmetricBuffer(CTRL_BYTES, group)
+        self.blocks = (m // self.world) // 128
+        self.pieces_per_block = -(-(128 * k * 2) // PIECE_BYTES)
+        self.ready = torch.zeros(self.world * self.blocks, dtype=torch.int32, device=self.device)
+        self.own_done = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._published_ptrs = torch.tensor([p for p in self.ctrl.peers], dtype=torch.int64, device=self.device)
+        self._pulled_ptrs = torch.tensor([p + PULLED_OFFSET for p in self.ctrl.peers], dtype=torch.int64,
+                                         device=self.device)
+        self.calls = 0            # completed epochs
         self.failed = False
         self._lock = threading.Lock()
         self._orders: dict = {}
         self.status = status_tensor(self.device)
+        register_operator(self)
 
     @property
     def gathered(self) -> torch.Tensor:
@@ -85,23 +113,45 @@ class AGGemm:
             self._orders[key] = torch.tensor(ids, dtype=torch.int32, device=self.device)
         return self._orders[key]
 
-    def forward(self, shard: torch.Tensor, w: torch.Tensor, *, b_mn: bool = False, bias=None,
-                gelu_aux=None, gelu_grad_of=None, out=None, bn: int = 0) -> torch.Tensor:
-        if self.failed:
-            raise RuntimeError("this AG->GEMM operator previously failed (its chunk counters are out of step)")
+    def targets(self, epoch: int) -> dict:
+        """Counter targets of call `epoch` (1-based): gatherer CTAs done with the
+        own chunk, peers' finished readers of the previous call, arrived pieces
+        per block."""
+        return dict(own_target=self.comm_ctas * epoch,
+                    pulled_target=(self.world - 1) * self.comm_ctas * (epoch - 1),
+                    ready_target=self.pieces_per_block * epoch)
+
+    def _check(self, shard, w, b_mn, bias, gelu_aux, gelu_grad_of, out):
         n = w.shape[1] if b_mn else w.shape[0]
-        if shard.shape != (self.m // self.world, self.k):
+        if tuple(shard.shape) != (self.m // self.world, self.k):
             raise ValueError(f"shard must be [{self.m // self.world}, {self.k}]")
         if w.dim() != 2 or (w.shape[0] if b_mn else w.shape[1]) != self.k or w.stride(-1) != 1:
             raise ValueError(f"w must be 2-D with K={self.k} ({'[K, N]' if b_mn else '[N, K]'}) and unit inner stride")
         for t, name in ((shard, "shard"), (w, "w")):
             if t.dtype != torch.bfloat16 or t.device != self.device:
                 raise ValueError(f"{name} must be bf16 on {self.device}")
-        if bias is not None and tuple(bias.shape) != (n,):
-            raise ValueError(f"bias must have shape [{n}]")
+        if bias is not None and (tuple(bias.shape) != (n,) or bias.dtype != torch.bfloat16
+                                 or not bias.is_contiguous() or bias.device != self.device):
+            raise ValueError(f"bias must be a contiguous bf16 [{n}] on {self.device}")
         for t, name in ((gelu_aux, "gelu_aux"), (gelu_grad_of, "gelu_grad_of"), (out, "out")):
-            if t is not None and tuple(t.shape) != (self.m, n):
-                raise ValueError(f"{name} must have shape [{self.m}, {n}]")
+            if t is None:
+                continue
+            if tuple(t.shape) != (self.m, n) or t.dtype != torch.bfloat16 or t.stride(-1) != 1 \
+                    or t.device != self.device:
+                raise ValueError(f"{name} must be a bf16 [{self.m}, {n}] with unit inner stride on {self.device}")
+        return n
+
+    def forward(self, shard: torch.Tensor, w: torch.Tensor, *, b_mn: bool = False, bias=None,
+                gelu_aux=None, gelu_grad_of=None, out=None, bn: int = 0, phase: int = 7,
+                _stamps: tuple | None = None) -> torch.Tensor:
+        """One call (phase 7).  Single-GPU emulation of several ranks runs each
+        call as three launches per rank -- phase 1 (own chunk), 2 (pull peers),
+        4 (GEMM) -- over all ranks in turn, so no launch waits on a later one."""
+        if self.failed:
+            raise RuntimeError("this AG->GEMM operator previously failed (its counters are out of step)")
+        n = self._check(shard, w, b_mn, bias, gelu_aux, gelu_grad_of, out)
+        if phase not in (1, 2, 4, 7):
+            raise ValueError("phase must be 7 (one launch) or 1, 2, 4 (emulation)")
         out = torch.empty((self.m, n), dtype=torch.bfloat16, device=self.device) if out is None else out
         if bn == 0:
             bn = 256 if n >= 256 and (self.m // 128) * ((n + 255) // 256) >= 148 else 128
@@ -115,27 +165,53 @@ class AGGemm:
         if gelu_grad_of is not None:
             epi |= G.EPI_GELU_BWD
             aux = gelu_grad_of
-        # The counter target is cumulative over calls (every CTA of every call bumps
-        # each owner's counter once): a launch that fails leaves it out of step, so
-        # the operator refuses further calls; the lock keeps target and launch paired.
+        # Counter targets are cumulative over calls: a launch that fails leaves
+        # them out of step, so the operator refuses further calls; the lock keeps
+        # targets and launch paired when threads share the operator.
         with self._lock:
+            epoch = self.calls + 1 if phase & 1 else self.calls
             try:
-                grid = lib().gemm_grid(self.m, n, bn, 0)
-                target = self.flag_total + grid
+                t = self.targets(epoch)
                 with tracing.scope("ag_gemm"):
                     lib().ag_gemm(shard.contiguous(), self.gathered, w, b_mn, out, epi, bias, aux,
-                                  self.gather.ptrs.data_ptr(), self.flags.ptrs.data_ptr(), self.flags.local,
-                                  self.rank, self.world, target, self._order(n, bn), self.status,
-                                  self.timeout_ns, bn)
-                self.flag_total = target
+                                  self.gather.ptrs.data_ptr(), self._published_ptrs.data_ptr(),
+                                  self._pulled_ptrs.data_ptr(), self.ctrl.local, self.ready, self.own_done,
+                                  self.rank, self.world, epoch, t["own_target"], t["pulled_target"],
+                                  t["ready_target"], self._order(n, bn), self.status, self.timeout_ns, bn,
+                                  self.comm_ctas, phase, *(_stamps or (None, None)))
             except BaseException:
                 self.failed = True
                 raise
+            if phase & 1:
+                self.calls = epoch
             count_launch()
-            self.calls += 1
         return out
+
+    def stage_profile(self, shard, w, **kw) -> dict:
+        """Untimed diagnostic call with device timestamps (%globaltimer of this
+        GPU): start / end of every gatherer and GEMM CTA, and the time each
+        peer block had fully arrived.  Tells whether the GEMM waited for data
+        (blocks arriving after the GEMM CTAs became free) or the reverse."""
+        n = w.shape[1] if kw.get("b_mn") else w.shape[0]
+        bn = kw.get("bn", 0) or (256 if n >= 256 and (self.m // 128) * ((n + 255) // 256) >= 148 else 128)
+        grid = lib().fused_grid(self.m, n, self.k, 0, 1, bn, self.comm_ctas, 7)
+        ctas = torch.zeros(2 * grid, dtype=torch.int64, device=self.device)
+        blocks = torch.zeros(self.world * self.blocks, dtype=torch.int64, device=self.device)
+        out = self.forward(shard, w, _stamps=(ctas, blocks), **kw)
+        torch.cuda.synchronize()
+        k = ctas.cpu().view(grid, 2)
+        b = blocks.cpu().view(self.world, self.blocks)
+        t0 = int(k[:, 0].min())
+        comm, gemm = k[:self.comm_ctas], k[self.comm_ctas:]
+        peers = [c for c in range(self.world) if c != self.rank]
+        return dict(out=out, kernel_ns=int(k[:, 1].max()) - t0, gemm_ctas=int(gemm.shape[0]),
+                    gather_end_ns=int(comm[:, 1].max()) - t0, gemm_end_ns=int(gemm[:, 1].max()) - t0,
+                    gemm_first_end_ns=int(gemm[:, 1].min()) - t0,
+                    own_chunk_ready_ns=int(b[self.rank].max()) - t0,
+                    peer_chunk_ready_ns={c: int(b[c].max()) - t0 for c in peers},
+                    first_peer_block_ns=min(int(b[c].min()) - t0 for c in peers))
 
     def close(self):
         if isinstance(self.gather, SymmetricBuffer) and self.gather._owned:
             self.gather.close()
-            self.flags.close()
+            self.ctrl.close()

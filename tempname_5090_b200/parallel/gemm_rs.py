@@ -19,26 +19,42 @@ python/flux_5090/runtime.py:161-241) as the baseline: the same GEMM writes the
 full partial, each physical block is exchanged with a sparse all_to_all on one
 of two lane communicators, and the owner runs the ordered (decode+)reduce.
 
-Receive slots are double-buffered by call parity.  Safety of reuse: the call
-t+2 push from rank s into rank r's parity slot happens after s's call t+1
-reduce, which waited for r's call t+1 GEMM tiles, which r issued after its own
-call t reduce (stream order) -- so r never reads a slot being overwritten.
+The BF16 arm on NVLink uses the pull transport (`pull=True`, the default
+there): ONE launch whose GEMM CTAs TMA-store every partial tile into this
+rank's own partial buffer and release-store the tile's flag on its owner,
+while `comm_ctas` reducer CTAs of the same launch wait for their own tiles'
+flags, pull the tiles from every source with bulk loads (no multicast) and
+reduce them in source order into the output, fusing residual + bias.  Sources
+produce destinations interleaved one tile at a time (rank+1 first), so every
+destination's tiles complete on all sources at the same pace and the
+reduction overlaps the GEMM.  The quantized arms keep the push transport
+(epilogue-encoded packets pushed into the owner's slots, separate receiver).
+
+Receive slots (push) and partial buffers (pull) are double-buffered by call
+parity.  Safety of reuse: rank s overwrites a parity buffer at call t+2 only
+after its call t+1 finished; that call waited for every peer r's call t+1
+tiles, which r produced after its own call t (stream order), so no peer still
+reads (pull) or is yet to read (push) call t's data when it is overwritten.
 """
 from __future__ import annotations
 
 import contextlib
+import os
 import threading
 
 import torch
 import torch.distributed as dist
 
-from .._native import count_launch, lib, status_tensor
+from .._native import count_launch, lib, register_operator, status_tensor
 from . import mapping
 from .symmetric import SymmetricBuffer
 from ..utils import tracing
 
 TILE_N = 256
 DEFAULT_TIMEOUT_NS = 10_000_000_000
+# Reducer CTAs of the pull transport (the rest of the SMs run the GEMM); bulk
+# loads from a peer reach the NVLink ceiling with 16-24 CTAs on B200.
+DEFAULT_COMM_CTAS = int(os.environ.get("TN5B_COMM_CTAS", "20"))
 
 
 class _Lanes:
@@ -59,19 +75,22 @@ class _Lanes:
 
 
 class RSWorkspace:
-    """Receive slots (2 parities x W sources), tile flags and the epoch sequence
-    shared by every GemmRS operator of one (M, N) on one group.  Any number of
-    operators may share it: each call is a full exchange, so the parity chain
-    argument holds across operators."""
+    """Exchange buffers shared by every GemmRS operator of one (M, N) on one
+    group: the tile flags and the epoch sequence, plus (allocated on first use)
+    the push transport's receive slots (2 parities x W sources) and the pull
+    transport's partial buffers (2 parities x [M, N]).  Any number of operators
+    may share it: each call is a full exchange, so the parity chain argument
+    holds across operators."""
 
-    def __init__(self, m: int, n: int, world: int, group=None, *, recv=None, flags=None, device=None):
+    def __init__(self, m: int, n: int, world: int, group=None, *, recv=None, flags=None, partial=None,
+                 device=None):
+        self.m, self.n, self.world, self.group = m, n, world, group
         self.rows = m // world
         self.slot_bytes = self.rows * n * 2
         self.tiles_per_dest = (self.rows // 128) * (n // TILE_N)
-        if recv is None:
-            recv = [SymmetricBuffer(world * self.slot_bytes, group) for _ in range(2)]
+        if flags is None:
             flags = SymmetricBuffer(world * self.tiles_per_dest * 4, group)
-        self.recv, self.flags = recv, flags
+        self.recv, self.flags, self.partial = recv, flags, partial
         # A failed exchange leaves slots and flags of an unfinished epoch: every
         # operator sharing this workspace refuses further calls.  The lock keeps
         # each call's epoch, push and reduce together when threads share operators.
@@ -80,9 +99,22 @@ class RSWorkspace:
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
         self.claims = torch.zeros(self.tiles_per_dest, dtype=torch.int32, device=device)
         self.epoch = 0
+        register_operator(self)
+
+    def slots(self):
+        """Receive slots of the push transport (allocated on first use, collectively)."""
+        if self.recv is None:
+            self.recv = [SymmetricBuffer(self.world * self.slot_bytes, self.group) for _ in range(2)]
+        return self.recv
+
+    def partials(self):
+        """Partial buffers of the pull transport (allocated on first use, collectively)."""
+        if self.partial is None:
+            self.partial = [SymmetricBuffer(self.m * self.n * 2, self.group) for _ in range(2)]
+        return self.partial
 
     def close(self):
-        for b in self.recv:
+        for b in (self.recv or []) + (self.partial or []):
             if isinstance(b, SymmetricBuffer) and b._owned:
                 b.close()
         if isinstance(self.flags, SymmetricBuffer) and self.flags._owned:
@@ -93,7 +125,8 @@ class GemmRS:
     def __init__(self, m: int, n: int, k: int, group=None, arm: str = "flux", chunk_rows: int = 128,
                  plan=None, transport: str = "nvlink", timeout_ns: int = DEFAULT_TIMEOUT_NS,
                  b_mn: bool = False, workspace: RSWorkspace | None = None,
-                 _emulate: tuple | None = None, device: torch.device | None = None):
+                 _emulate: tuple | None = None, device: torch.device | None = None,
+                 pull: bool | None = None, comm_ctas: int | None = None):
         if arm not in mapping.ARMS:
             raise ValueError(f"unknown arm {arm}")
         if transport not in ("nvlink", "nccl"):
@@ -112,6 +145,14 @@ class GemmRS:
         self.arrival = arm in mapping.ARRIVAL_ARMS
         self.rows = m // self.world
         self.timeout_ns = int(timeout_ns)
+        # Pull transport: the BF16 arm on NVLink (the quantized arms push packets).
+        self.pull = (transport == "nvlink" and not self.quantized) if pull is None else bool(pull)
+        if self.pull and (transport != "nvlink" or self.quantized):
+            raise ValueError("the pull transport serves the BF16 arm on NVLink")
+        self.comm_ctas = DEFAULT_COMM_CTAS if comm_ctas is None else int(comm_ctas)
+        if self.pull and not 1 <= self.comm_ctas <= 64:
+            raise ValueError("comm_ctas must be in [1, 64]")
+        self._last_operands = None
         # `device` defaults to the current CUDA device; CPU is for host-logic tests
         # (NCCL transport on Gloo ranks, or a recording stand-in for the kernels).
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -126,10 +167,13 @@ class GemmRS:
         self.calls = 0
         self.failed = False
         self.status = status_tensor(self.device)
+        register_operator(self)
         self.workspace = None
         if transport == "nvlink":
             if _emulate is not None:
-                workspace = RSWorkspace(m, n, self.world, recv=_emulate[2], flags=_emulate[3], device=self.device)
+                # (rank, world, receive slots or partial buffers [2 parities], flags)
+                bufs = dict(partial=_emulate[2]) if self.pull else dict(recv=_emulate[2])
+                workspace = RSWorkspace(m, n, self.world, flags=_emulate[3], device=self.device, **bufs)
             self.workspace = workspace if workspace is not None else RSWorkspace(m, n, self.world, group)
         else:
             self.lanes, self.lane_streams = _Lanes.get(group)
@@ -147,6 +191,9 @@ class GemmRS:
         """Tile order of `rank`'s producer GEMM.  In-kernel pushes start on
         destination rank+1 (no incast); the NCCL transport keeps the reference
         CTA map."""
+        if self.pull:
+            return mapping.pull_production_ids(self.m, self.n, self.k, self.world, self.chunk_rows, self.arm,
+                                               rank, self.plan, tile_n=TILE_N)
         shift = rank + 1 if self.transport == "nvlink" else 0
         return mapping.linear_tile_ids(self.m, self.n, self.k, self.world, self.chunk_rows, self.arm, self.plan,
                                        tile_n=TILE_N, shift=shift)
@@ -164,7 +211,7 @@ class GemmRS:
 
     @property
     def recv(self):
-        return self.workspace.recv
+        return self.workspace.slots()
 
     @property
     def flags(self):
@@ -189,7 +236,10 @@ class GemmRS:
                 raise RuntimeError("epoch exhausted; create a new operator")
             self.epoch += 1
             try:
-                if self.transport == "nvlink":
+                if self.pull:
+                    with tracing.scope("gemm_rs.pull"):
+                        self._launch_pull(x, w, b_mn, out, residual, bias, phase=6)
+                elif self.transport == "nvlink":
                     with tracing.scope("gemm_rs.push"):
                         self.push(x, w, b_mn)
                     with tracing.scope("gemm_rs.reduce"):
@@ -222,10 +272,28 @@ class GemmRS:
         if out is not None:
             need(out, (self.rows, self.n), "out")
 
+    def _launch_pull(self, x, w, b_mn, out, residual=None, bias=None, phase=6, stamps=None, produced=None,
+                     delay_tile=-1, delay_ns=0, cta_stamps=None):
+        """Pull transport: one launch running the GEMM (phase bit2) and/or the
+        reducer CTAs (phase bit1) of this call's epoch."""
+        parity = self.epoch & 1
+        part = self.workspace.partials()[parity]
+        lib().gemm_rs_pull(x, False, w, b_mn, part.local, part.ptrs.data_ptr(), self.flags.ptrs.data_ptr(),
+                           self.flags.local, self.rank, self.world, self.epoch, self.tile_order,
+                           self.consumer_order, out, residual, bias, self.status, self.timeout_ns,
+                           self.comm_ctas, phase, stamps, produced, delay_tile, delay_ns, 0, cta_stamps)
+        count_launch()
+
     def push(self, x, w, b_mn: bool | None = None, delay_tile: int = -1, delay_ns: int = 0):
-        """Producer phase: the GEMM whose epilogue pushes tiles to their owners."""
+        """Producer phase: the GEMM whose epilogue pushes tiles to their owners
+        (pull transport: the GEMM that stores and publishes its partial tiles)."""
         b_mn = self.b_mn if b_mn is None else b_mn
         self._check_operands(x, w, b_mn)
+        if self.pull:
+            self._last_operands = (x, w, b_mn)
+            dummy = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device)
+            self._launch_pull(x, w, b_mn, dummy, phase=4, delay_tile=delay_tile, delay_ns=delay_ns)
+            return
         parity = self.epoch & 1
         mode = 2 if self.quantized else 1
         lib().gemm_rs_push(x, False, w, b_mn, mode, self.recv[parity].ptrs.data_ptr(),
@@ -239,13 +307,58 @@ class GemmRS:
         self.epoch += 1
 
     def reduce(self, out, residual=None, bias=None, stamps=None):
-        """Receiver phase: bounded waits on tile flags, ordered (decode +) reduce."""
+        """Receiver phase: bounded waits on tile flags, ordered (decode +) reduce.
+        Pull transport: a launch of the reducer CTAs only (operands of the last push)."""
+        if self.pull:
+            if self._last_operands is None:
+                raise RuntimeError("reduce() of the pull transport follows a push() of the same call")
+            x, w, b_mn = self._last_operands
+            self._launch_pull(x, w, b_mn, out, residual, bias, phase=2, stamps=stamps)
+            return
         parity = self.epoch & 1
         count_launch()
         lib().rs_reduce(self.recv[parity].local, self.flags.local, self.slot_bytes, self.rank, self.world,
                         self.rows, self.n, TILE_N, self.chunk_rows, self.quantized, self.epoch, out,
                         residual, bias, self.consumer_order, self.arrival,
                         self.claims if self.arrival else None, self.status, self.timeout_ns, 0, stamps)
+
+    def stage_profile(self, x, w, residual=None, bias=None) -> dict:
+        """Untimed diagnostic call of the pull transport with device timestamps
+        (%globaltimer, this GPU's clock): when each tile this rank produced was
+        published, and when each of this rank's output tiles was reduced.  Reports
+        how many output tiles were complete before this rank's GEMM published its
+        last tile -- the reduction that overlapped the GEMM (the counterpart of
+        the reference's per-block consumer intervals, runtime.py:243-257)."""
+        if not self.pull:
+            raise RuntimeError("stage_profile needs the pull transport")
+        ws = self.workspace
+        if self.failed or ws.failed:
+            raise RuntimeError("this GemmRS operator (or one sharing its receive workspace) previously failed")
+        out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device)
+        stamps = torch.zeros(self.tiles_per_dest, dtype=torch.int64, device=self.device)
+        produced = torch.zeros((self.m // 128) * (self.n // TILE_N), dtype=torch.int64, device=self.device)
+        grid = lib().fused_grid(self.m, self.n, self.k, 3, 0, 256, self.comm_ctas, 6)
+        ctas = torch.zeros(2 * grid, dtype=torch.int64, device=self.device)
+        with ws.lock:
+            try:
+                self._profiled_call(x, w, out, stamps, 0, 0, produced=produced, cta_stamps=ctas,
+                                    residual=residual, bias=bias)
+            except BaseException:
+                self.failed = ws.failed = True
+                raise
+        torch.cuda.synchronize()
+        p, c, k = produced.cpu(), stamps.cpu(), ctas.cpu().view(grid, 2)
+        t0 = int(k[:, 0].min())
+        gemm_end = int(p.max())
+        comm = k[:self.comm_ctas]
+        gemm = k[self.comm_ctas:]
+        return dict(out=out, kernel_ns=int(k[:, 1].max()) - t0,
+                    gemm_ctas_end_ns=int(gemm[:, 1].max()) - t0, reducer_ctas_end_ns=int(comm[:, 1].max()) - t0,
+                    producer_first_ns=int(p.min()) - t0, producer_last_ns=gemm_end - t0,
+                    consumer_first_ns=int(c.min()) - t0, consumer_last_ns=int(c.max()) - t0,
+                    consumer_tiles=int(c.numel()),
+                    consumer_tiles_completed_before_producer_end=int((c < gemm_end).sum()),
+                    produced_ns=(p - t0).tolist(), consumed_ns=(c - t0).tolist())
 
     def profile_call(self, x, w, *, delay_ns: int = 0, delay_rank: int = 0):
         """Untimed diagnostic call: optionally delays (bounded, <= 100 ms) the flag
@@ -272,7 +385,8 @@ class GemmRS:
         rel = (s - s.min()).tolist()
         return out, rel, delayed_local
 
-    def _profiled_call(self, x, w, out, stamps, delay_ns, delay_rank):
+    def _profiled_call(self, x, w, out, stamps, delay_ns, delay_rank, produced=None, cta_stamps=None,
+                       residual=None, bias=None):
         self.epoch += 1
         delay_tile, delayed_local = -1, None
         if delay_ns:
@@ -288,9 +402,14 @@ class GemmRS:
                     dest = tm // per_dest_m
                     delayed_local = (dest, (tm - dest * per_dest_m) * tiles_n + tid % tiles_n)
                     break
-        self.push(x, w, delay_tile=delay_tile if self.rank == delay_rank else -1,
-                  delay_ns=delay_ns if self.rank == delay_rank else 0)
-        self.reduce(out, stamps=stamps)
+        mine = self.rank == delay_rank
+        if self.pull:
+            self._launch_pull(x, w, self.b_mn, out, residual, bias, phase=6, stamps=stamps, produced=produced,
+                              delay_tile=delay_tile if mine else -1, delay_ns=delay_ns if mine else 0,
+                              cta_stamps=cta_stamps)
+        else:
+            self.push(x, w, delay_tile=delay_tile if mine else -1, delay_ns=delay_ns if mine else 0)
+            self.reduce(out, stamps=stamps)
         self.calls += 1
         return delayed_local
 

@@ -113,6 +113,32 @@ def linear_tile_ids(m, n, k, world, chunk_rows, arm, plan=None, tile_n=256, shif
     return out
 
 
+def destination_tile_ids(m, n, k, world, chunk_rows, arm, plan=None, tile_n=256):
+    """Per destination, its tiles (global linear ids) in the arm's production order."""
+    cols = n // tile_n
+    per_dest = m // world // TILE_M
+    lists = [[] for _ in range(world)]
+    for tm, tn in tile_order(m, n, k, world, chunk_rows, arm, plan, tile_n):
+        lists[tm // per_dest].append(tm * cols + tn)
+    return lists
+
+
+def pull_production_ids(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n=256):
+    """Production order of the pull transport on `rank`: the arm's
+    per-destination tile sequences interleaved across destinations one tile at
+    a time, starting with destination rank+1 and ending each round with the
+    rank's own rows.  A pulled tile can be reduced only when every source has
+    produced it, so every source advances through every destination's tiles at
+    the same pace (balanced all-to-all traffic, reduction overlapping the GEMM);
+    the within-destination order is the arm's."""
+    lists = destination_tile_ids(m, n, k, world, chunk_rows, arm, plan, tile_n)
+    out = []
+    for i in range(len(lists[0])):
+        for j in range(world):
+            out.append(lists[(rank + 1 + j) % world][i])
+    return out
+
+
 def consumer_tile_order(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n=256):
     """Order in which `rank` consumes its own tiles: production order restricted
     to tiles destined to `rank`, as local tile ids (row tile within the

@@ -68,8 +68,29 @@ class Timer:
             dist.all_reduce(med, op=dist.ReduceOp.MAX, group=self.group)
         return float(med.item())
 
+    def back_to_back(self, fn, calls=10) -> float:
+        """Microseconds per call of `calls` consecutive calls (no flush between:
+        host launch gaps hide behind the previous call), max over ranks."""
+        torch = self.torch
+        import torch.distributed as dist
+        fn()
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(calls):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor(s.elapsed_time(e) * 1000.0 / calls, dtype=torch.float64, device="cuda")
+        if self.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        return float(t.item())
 
-def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True, chunk_rows=128):
+
+def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True, chunk_rows=128,
+                comm_sweep=(None,)):
     import torch
     import torch.distributed as dist
     from ..parallel.gemm_rs import GemmRS
@@ -86,14 +107,25 @@ def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True
         if arm.endswith("arrival"):
             plan = planning.make_role(m, n, k, world, chunk_rows)
         for transport in transports:
-            op = GemmRS(m, n, k, arm=arm, chunk_rows=chunk_rows, plan=plan, transport=transport)
-            us = timer.run(lambda: op.forward(x, w))
-            wire = (world - 1) * (m // world) * n * (136 / 128 if arm != "flux" else 2.0)
-            roof = max(flops / (pk["bf16_tflops"] * 1e12), wire / (pk["nvlink_gbs"] * 1e9)) * 1e6
-            rows.append(dict(op="gemmrs", arm=arm, transport=transport, m=m, n=n, k=k, world=world, us=us,
-                             roofline_us=roof, roofline_fraction=roof / us, tflops=flops / us / 1e6,
-                             nvlink_bytes_per_rank=wire, peaks=pk["source"]))
-            op.close()
+            sweep = comm_sweep if (transport == "nvlink" and arm == "flux") else (None,)
+            for comm in sweep:
+                op = GemmRS(m, n, k, arm=arm, chunk_rows=chunk_rows, plan=plan, transport=transport,
+                            comm_ctas=comm)
+                us = timer.run(lambda: op.forward(x, w))
+                wire = (world - 1) * (m // world) * n * (136 / 128 if arm != "flux" else 2.0)
+                roof = max(flops / (pk["bf16_tflops"] * 1e12), wire / (pk["nvlink_gbs"] * 1e9)) * 1e6
+                row = dict(op="gemmrs", arm=arm, transport=transport + ("-pull" if op.pull else ""), m=m, n=n,
+                           k=k, world=world, us=us, roofline_us=roof, roofline_fraction=roof / us,
+                           tflops=flops / us / 1e6, nvlink_bytes_per_rank=wire, peaks=pk["source"])
+                row["back_to_back_us"] = timer.back_to_back(lambda: op.forward(x, w))
+                if op.pull:
+                    row["comm_ctas"] = op.comm_ctas
+                    prof = op.stage_profile(x, w)
+                    row["stage"] = {key: prof[key] for key in ("producer_last_ns", "consumer_first_ns",
+                                                                "consumer_last_ns", "consumer_tiles",
+                                                                "consumer_tiles_completed_before_producer_end")}
+                rows.append(row)
+                op.close()
     # GEMM alone (no communication) and the library-only baseline
     out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
     rows.append(dict(op="gemm_only", m=m, n=n, k=k, us=timer.run(lambda: G.matmul(x, w, out=out))))
@@ -159,7 +191,15 @@ def attention_case(rank, world, timer, heads=32, hidden=4096, seq=2048, batch=4)
         lib_out_gemm=lambda: torch.mm(attn, wo.t()),
     )
     for name, fn in stages.items():
-        rows.append(dict(op="attention_stage", stage=name, world=world, us=timer.run(fn)))
+        rows.append(dict(op="attention_stage", stage=name, world=world, us=timer.run(fn),
+                         back_to_back_us=timer.back_to_back(fn)))
+    if world > 1:
+        prof = tp.ag_operator(("bench_qkv", 0), m, hidden).stage_profile(xs, wqkv, bias=bqkv)
+        rows.append(dict(op="stage_profile", stage="ag_gemm", world=world,
+                         **{k: v for k, v in prof.items() if k != "out"}))
+        prof = tp.rs_operator(m, hidden, hidden // world, "attn").stage_profile(attn, wo, residual=xs, bias=bo)
+        rows.append(dict(op="stage_profile", stage="gemm_rs", world=world,
+                         **{k: v for k, v in prof.items() if k not in ("out", "produced_ns", "consumed_ns")}))
     tp.close()
     return rows
 
@@ -249,34 +289,66 @@ def attention_kernel_case(timer, shapes=((4, 2048, 4), (1, 2048, 32), (4, 2048, 
 
 
 def nvlink_case(rank, world, timer, mib=64):
-    """Egress bandwidth of SM-issued 16-byte stores into peers' memory (this
-    framework's copy kernel writing through CUDA-IPC mappings): ring (every rank
-    -> rank+1) and all-to-all (every rank -> every peer, one launch per peer),
-    against a local device copy of the same size."""
+    """NVLink transfer mechanisms, ring pattern (every rank moves `mib` MiB
+    between itself and rank+1 at once), swept over the number of CTAs:
+
+    * push:       SM-issued 16-byte stores into the peer's memory (copy kernel)
+    * pull:       SM-issued 16-byte loads from the peer's memory, local stores
+    * bulk_pull:  untiled bulk (TMA-engine) loads from the peer's memory into a
+                  shared-memory ring, bulk stores to local memory; one issuing
+                  thread per CTA, `stages` x `chunk` bytes in flight per CTA
+    * local_copy / bulk_local: the same kernels on this GPU's memory only.
+    """
     import torch
-    from .._native import lib
+    from .._native import lib, status_tensor
     from ..parallel.symmetric import SymmetricBuffer
     nbytes = mib << 20
-    buf = SymmetricBuffer(world * nbytes)
-    src = torch.randn(nbytes // 4, device="cuda")
-    local_dst = torch.empty_like(src)
-    part = (nbytes // (world - 1)) // 16 * 16
-    ring_dst = buf.peers[(rank + 1) % world] + rank * nbytes
-    peers = [buf.peers[p] + rank * nbytes for p in range(world) if p != rank]
-    C = lib()
-
-    def all_to_all():
-        for i, dst in enumerate(peers):
-            C.copy_to_ptr(dst, src[i * part // 4:], part, 0)
-    rows = [dict(op="nvlink", pattern="local_copy", world=world, bytes=nbytes,
-                 us=timer.run(lambda: C.copy_to_ptr(local_dst.data_ptr(), src, nbytes, 0)))]
-    rows.append(dict(op="nvlink", pattern="ring", world=world, bytes=nbytes,
-                     us=timer.run(lambda: C.copy_to_ptr(ring_dst, src, nbytes, 0))))
-    rows.append(dict(op="nvlink", pattern="all_to_all", world=world, bytes=part * (world - 1),
-                     us=timer.run(all_to_all)))
-    for r in rows:
-        r["gbs_per_rank"] = r["bytes"] / r["us"] / 1e3
+    buf = SymmetricBuffer(2 * nbytes)
+    def data(r):
+        return torch.randn(nbytes // 4, device="cuda", generator=torch.Generator(device="cuda").manual_seed(99 + r))
+    src = data(rank)
+    buf.local_view((nbytes // 4,), torch.float32).copy_(src)
     torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    local_dst = torch.empty_like(src)
+    peer = (rank + 1) % world
+    peer_src = buf.peers[peer]                    # the peer's first half (its data)
+    peer_dst = buf.peers[peer] + nbytes           # the peer's second half (landing zone)
+    status = status_tensor(torch.device("cuda", torch.cuda.current_device()))
+    C = lib()
+    rows = []
+
+    def row(pattern, fn, **kw):
+        us = timer.run(fn)
+        rows.append(dict(op="nvlink", pattern=pattern, world=world, bytes=nbytes, us=us,
+                         gbs_per_rank=nbytes / us / 1e3, **kw))
+
+    row("local_copy", lambda: C.copy_ptr(local_dst.data_ptr(), src.data_ptr(), nbytes, 0), ctas=4 * 148)
+    for ctas in (32, 64, 148, 296, 592):
+        row("push", lambda c=ctas: C.copy_ptr(peer_dst, src.data_ptr(), nbytes, c), ctas=ctas)
+    for ctas in (32, 64, 148, 296, 592):
+        row("pull", lambda c=ctas: C.copy_ptr(local_dst.data_ptr(), peer_src, nbytes, c), ctas=ctas)
+    for chunk, stages in ((16384, 8), (32768, 6), (65536, 3)):
+        for ctas in (8, 16, 24, 32, 48, 64, 148):
+            row("bulk_pull", lambda c=ctas, k=chunk, s=stages: C.bulk_copy(local_dst.data_ptr(), peer_src, nbytes,
+                                                                          c, k, s, 10 ** 9, status),
+                ctas=ctas, chunk=chunk, stages=stages)
+    for ctas in (16, 32, 148):
+        row("bulk_local", lambda c=ctas: C.bulk_copy(local_dst.data_ptr(), src.data_ptr(), nbytes, c, 32768, 6,
+                                                     10 ** 9, status), ctas=ctas, chunk=32768, stages=6)
+    # Data check: one more bulk pull and one SM pull must reproduce the peer's data.
+    local_dst.zero_()
+    C.bulk_copy(local_dst.data_ptr(), peer_src, nbytes, 32, 32768, 6, 10 ** 9, status)
+    torch.cuda.synchronize()
+    expect = data(peer)
+    bulk_ok = bool(torch.equal(local_dst, expect))
+    local_dst.zero_()
+    C.copy_ptr(local_dst.data_ptr(), peer_src, nbytes, 148)
+    torch.cuda.synchronize()
+    rows.append(dict(op="nvlink_check", status=int(status[0].item()), bulk_pull_equal=bulk_ok,
+                     pull_equal=bool(torch.equal(local_dst, expect))))
     buf.close()
     return rows
 
@@ -291,6 +363,7 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--arms", default="all")
     ap.add_argument("--transports", default="nvlink,nccl")
+    ap.add_argument("--comm-ctas", default="", help="gemmrs: comma list of reducer CTA counts (pull transport)")
     ap.add_argument("--out", type=Path)
     args = ap.parse_args(argv)
     import torch
@@ -306,8 +379,9 @@ def main(argv=None):
     arms = ARMS if args.arms == "all" else tuple(args.arms.split(","))
     transports = tuple(args.transports.split(","))
     rows = []
+    comm_sweep = tuple(int(c) for c in args.comm_ctas.split(",")) if args.comm_ctas else (None,)
     if args.op == "gemmrs":
-        rows += gemmrs_case(args.m, args.n, args.k, rank, world, timer, arms, transports)
+        rows += gemmrs_case(args.m, args.n, args.k, rank, world, timer, arms, transports, comm_sweep=comm_sweep)
     elif args.op == "gemm":
         rows += gemm_case(GEMM_SHAPES, timer)
     elif args.op == "gemm_once":

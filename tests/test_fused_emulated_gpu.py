@@ -98,47 +98,153 @@ def test_gemm_rs_fused_residual_bias():
 @pytest.mark.parametrize("world,bn", [(2, 128), (4, 256), (8, 256)])
 @pytest.mark.parametrize("epi", ["plain", "bias_gelu", "mn_major"])
 def test_ag_gemm_emulated(world, bn, epi):
-    from tempname_5090_b200.parallel.ag_gemm import AGGemm
+    """Pull all-gather -> GEMM, W ranks emulated on one GPU: every rank's call
+    runs as three launches (own chunk + publish, pull peers, GEMM) over all ranks
+    in turn.  Three calls with changing inputs exercise the cumulative counters
+    and the `pulled` handshake that guards the own chunk between calls."""
+    from tempname_5090_b200.parallel.ag_gemm import AGGemm, CTRL_BYTES
     from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
     from tempname_5090_b200.ops import gemm as G
-    from tempname_5090_b200._native import check_status, lib
-    m, k, n = world * 256, 256, 768
+    from tempname_5090_b200._native import check_status
+    m, k, n = world * 256, 320, 768
     rows = m // world
     gather = SymmetricBuffer.emulated(m * k * 2, world)
-    flags = SymmetricBuffer.emulated(world * 4, world)
-    shards = [torch.randn((rows, k), generator=_gen(r), device="cuda").to(torch.bfloat16) for r in range(world)]
-    full = torch.cat(shards)
+    ctrl = SymmetricBuffer.emulated(CTRL_BYTES, world)
+    ops = [AGGemm(m, k, comm_ctas=3, _emulate=(r, world, gather.as_rank(r), ctrl.as_rank(r))) for r in range(world)]
     w = (0.05 * torch.randn((n, k), generator=_gen(77), device="cuda")).to(torch.bfloat16)
     w_mn = w.t().contiguous()
     bias = torch.randn((n,), generator=_gen(78), device="cuda").to(torch.bfloat16)
-    grid = lib().gemm_grid(m, n, bn, 0)
-    for r in range(world):
-        op = AGGemm(m, k, _emulate=(r, world, gather.as_rank(r), flags.as_rank(r)))
-        gview = gather.view(r, (m, k), torch.bfloat16)
-        fview = flags.view(r, (world,), torch.int32)
-        for c in range(world):
-            if c != r:
-                gview[c * rows:(c + 1) * rows].copy_(shards[c])
-        fview.fill_(grid)
-        fview[r] = 0
-        aux = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
-        if epi == "plain":
-            out = op.forward(shards[r], w, bn=bn)
-            expect = G.matmul(full, w, bn=bn)
-        elif epi == "bias_gelu":
-            out = op.forward(shards[r], w, bias=bias, gelu_aux=aux, bn=bn)
-            aux_ref = torch.empty_like(aux)
-            expect = G.matmul(full, w, bias=bias, gelu_aux=aux_ref, bn=bn)
-        else:
-            out = op.forward(shards[r], w_mn, b_mn=True, bn=bn)
-            expect = G.matmul(full, w_mn, b_t=True, bn=bn)
+    for call in range(3):
+        shards = [torch.randn((rows, k), generator=_gen(10 * call + r), device="cuda").to(torch.bfloat16)
+                  for r in range(world)]
+        full = torch.cat(shards)
+        weight = w_mn if epi == "mn_major" else w
+        kw = dict(b_mn=epi == "mn_major", bn=bn)
+        if epi == "bias_gelu":
+            kw["bias"] = bias
+        for phase in (1, 2):
+            for r in range(world):
+                ops[r].forward(shards[r], weight, phase=phase, **kw)
+        outs, auxs = [], []
+        for r in range(world):
+            aux = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+            extra = dict(gelu_aux=aux) if epi == "bias_gelu" else {}
+            outs.append(ops[r].forward(shards[r], weight, phase=4, **kw, **extra))
+            auxs.append(aux)
         torch.cuda.synchronize()
         check_status()
-        assert torch.equal(op.gathered, full)
-        assert torch.equal(out, expect)
-        if epi == "bias_gelu":
-            assert torch.equal(aux, aux_ref)
-        assert int(fview[r].item()) == grid
+        aux_ref = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+        extra = dict(gelu_aux=aux_ref) if epi == "bias_gelu" else {}
+        expect = G.matmul(full, weight, b_t=epi == "mn_major", bias=kw.get("bias"), bn=bn, **extra)
+        for r in range(world):
+            assert torch.equal(ops[r].gathered, full), (r, call)
+            assert torch.equal(outs[r], expect), (r, call)
+            if epi == "bias_gelu":
+                assert torch.equal(auxs[r], aux_ref)
+        # every peer signalled once per gatherer CTA per call
+        pulled = [int(ctrl.view(r, (CTRL_BYTES // 4,), torch.int32)[64].item()) for r in range(world)]
+        assert pulled == [(world - 1) * 3 * (call + 1)] * world, pulled
+
+
+@pytest.mark.parametrize("world", [2, 8])
+@pytest.mark.parametrize("comm_ctas", [1, 5, 20])
+def test_gemm_rs_pull_emulated_matches_push(world, comm_ctas):
+    """Pull transport (GEMM launch, then reducer launch, per emulated rank) is
+    bitwise equal to the push transport and to the ordered reduce of the
+    partials, with residual + bias, over calls of both buffer parities."""
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    from tempname_5090_b200.ops import gemm as G, taco
+    from tempname_5090_b200._native import check_status
+    m, n, k = world * 384, 768, 448
+    rows = m // world
+    tiles = (rows // 128) * (n // 256)
+    bufs = {}
+    ops = {}
+    for pull in (True, False):
+        data = [SymmetricBuffer.emulated(m * n * 2, world) for _ in range(2)]
+        flags = SymmetricBuffer.emulated(world * tiles * 4, world)
+        bufs[pull] = data + [flags]
+        ops[pull] = [GemmRS(m, n, k, pull=pull, comm_ctas=comm_ctas,
+                            _emulate=(r, world, [b.as_rank(r) for b in data], flags.as_rank(r)))
+                     for r in range(world)]
+    res = torch.randn((rows, n), generator=_gen(5), device="cuda").to(torch.bfloat16)
+    bias = torch.randn((n,), generator=_gen(6), device="cuda").to(torch.bfloat16)
+    for call in range(3):
+        xs = [torch.randn((m, k), generator=_gen(40 * call + r), device="cuda").to(torch.bfloat16)
+              for r in range(world)]
+        ws = [(0.05 * torch.randn((n, k), generator=_gen(200 + r), device="cuda")).to(torch.bfloat16)
+              for r in range(world)]
+        outs = {}
+        for pull, group in ops.items():
+            for op in group:
+                op.begin()
+            for r, op in enumerate(group):
+                op.push(xs[r], ws[r])
+            outs[pull] = []
+            for r, op in enumerate(group):
+                out = torch.empty((rows, n), dtype=torch.bfloat16, device="cuda")
+                op.reduce(out, residual=res if call else None, bias=bias if call else None)
+                outs[pull].append(out)
+        torch.cuda.synchronize()
+        check_status()
+        partials = [G.matmul(xs[s], ws[s], bn=256) for s in range(world)]
+        for r in range(world):
+            local = partials[r][r * rows:(r + 1) * rows].contiguous()
+            remote = torch.cat([partials[s][r * rows:(r + 1) * rows] for s in range(world) if s != r])
+            y = taco.ordered_reduce(local, remote, r, world)
+            if call:
+                y = ((res.float() + y.float()).to(torch.bfloat16).float() + bias.float()).to(torch.bfloat16)
+            assert torch.equal(outs[True][r], y), (world, comm_ctas, call, r)
+            assert torch.equal(outs[True][r], outs[False][r])
+    for group in bufs.values():
+        for b in group:
+            b.close()
+
+
+def test_gemm_rs_pull_signed_zero_and_order():
+    """The BF16 adds of the pull reducer keep the reference's rounding and
+    signed-zero behaviour: sources holding -0.0 and values that cancel or round
+    differently in another order."""
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    from tempname_5090_b200.ops import taco
+    from tempname_5090_b200._native import check_status
+    world, m, n, k = 4, 512, 256, 64
+    rows = m // world
+    data = [SymmetricBuffer.emulated(m * n * 2, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(world * (rows // 128) * (n // 256) * 4, world)
+    ops = [GemmRS(m, n, k, pull=True, comm_ctas=2, _emulate=(r, world, [b.as_rank(r) for b in data], flags.as_rank(r)))
+           for r in range(world)]
+    # x = e_0 (one-hot K) so each partial row equals a chosen weight column: partial[r, c] = w[c, 0]
+    vals = [torch.tensor([-0.0, 1.0, 2.0 ** -9, -1.0], dtype=torch.float32),
+            torch.tensor([-0.0, 2.0 ** -9, 2.0 ** -9, 1.0], dtype=torch.float32),
+            torch.tensor([-0.0, 2.0 ** -9, -1.0, 3.0e38], dtype=torch.float32),
+            torch.tensor([-0.0, -1.0, 1.0, -3.0e38], dtype=torch.float32)]
+    x = torch.zeros((m, k), dtype=torch.bfloat16, device="cuda")
+    x[:, 0] = 1
+    ws = []
+    for s in range(world):
+        w = torch.zeros((n, k), dtype=torch.float32)
+        w[:, 0] = vals[s].repeat(n // 4)
+        ws.append(w.to(torch.bfloat16).cuda())
+    for op in ops:
+        op.begin()
+    for r, op in enumerate(ops):
+        op.push(x, ws[r])
+    outs = []
+    for op in ops:
+        out = torch.empty((rows, n), dtype=torch.bfloat16, device="cuda")
+        op.reduce(out)
+        outs.append(out)
+    torch.cuda.synchronize()
+    check_status()
+    from tempname_5090_b200.ops import gemm as G
+    parts = [G.matmul(x, ws[s], bn=256) for s in range(world)]  # the same tile kind as the fused GEMM
+    for r in range(world):
+        expect = taco.ordered_sum_cpu([p[r * rows:(r + 1) * rows].cpu() for p in parts])
+        got = outs[r].cpu()
+        assert torch.equal(got.view(torch.int16), expect.view(torch.int16)), r
 
 
 def test_bounded_wait_times_out_and_context_survives():

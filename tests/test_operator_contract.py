@@ -44,6 +44,17 @@ class _FakeLib:
                                         order=tile_order.tolist(), rank=rank, world=world,
                                         delay=(delay_tile, delay_ns))))
 
+    def gemm_rs_pull(self, x, a_mn, w, b_mn, partial_local, partial_ptrs, flag_ptrs, my_flags, rank, world, epoch,
+                     tile_order, consumer_order, out, residual, bias, status, timeout_ns, comm_ctas, phase, stamps,
+                     produced, delay_tile, delay_ns, max_ctas, cta_stamps):
+        if self.fail_push:
+            raise RuntimeError("injected launch failure")
+        self.calls.append(("pull", dict(partial=partial_local, partials=partial_ptrs, flags=flag_ptrs,
+                                        my_flags=my_flags, epoch=epoch, order=tile_order.tolist(),
+                                        consumer=consumer_order.tolist(), rank=rank, world=world,
+                                        comm_ctas=comm_ctas, phase=phase, residual=residual is not None,
+                                        bias=bias is not None, delay=(delay_tile, delay_ns))))
+
     def rs_reduce(self, recv, flags, slot_bytes, rank, world, rows, n, tile_n, chunk_rows, quantized, epoch,
                   out, residual, bias, order, arrival, claims, status, timeout_ns, max_ctas, stamps):
         self.calls.append(("reduce", dict(recv=recv, flags=flags, epoch=epoch, quantized=quantized,
@@ -65,8 +76,35 @@ def test_nvlink_transport_launch_contract(monkeypatch, arm, rank, world):
     x = torch.zeros((M, K), dtype=torch.bfloat16)
     w = torch.zeros((N, K), dtype=torch.bfloat16)
     quantized = arm in mapping.QUANTIZED_ARMS
-    production = mapping.linear_tile_ids(M, N, K, world, CHUNK, arm, plan, tile_n=256, shift=rank + 1)
     consumer = mapping.consumer_tile_order(M, N, K, world, CHUNK, arm, rank, plan, 256)
+    if not quantized:
+        # BF16 arm: the pull transport, ONE launch per call (GEMM + reducer CTAs),
+        # destinations interleaved one tile at a time starting with rank+1.
+        production = mapping.pull_production_ids(M, N, K, world, CHUNK, arm, rank, plan, tile_n=256)
+        tiles_n = N // 256
+        per_dest = M // world // 128
+        assert [tid // tiles_n // per_dest for tid in production[:world]] == [(rank + 1 + j) % world
+                                                                              for j in range(world)]
+        assert sorted(production) == list(range(len(production)))
+        for call in range(1, 5):
+            out = op.forward(x, w, residual=torch.zeros((M // world, N), dtype=torch.bfloat16))
+            assert out.shape == (M // world, N) and len(fake.calls) == call
+            kind, c = fake.calls[-1]
+            assert kind == "pull" and c["phase"] == 6 and c["epoch"] == call
+            assert c["partial"] == recv[call & 1].local and c["partials"] == recv[call & 1].ptrs.data_ptr()
+            assert c["flags"] == flags.ptrs.data_ptr() and c["my_flags"] == flags.local
+            assert c["order"] == production and c["consumer"] == consumer
+            assert c["residual"] and not c["bias"] and c["delay"] == (-1, 0) and c["comm_ctas"] == op.comm_ctas
+        fake.fail_push = True
+        with pytest.raises(RuntimeError, match="injected"):
+            op.forward(x, w)
+        fake.fail_push = False
+        before = len(fake.calls)
+        with pytest.raises(RuntimeError, match="previously failed"):
+            op.forward(x, w)
+        assert len(fake.calls) == before and op.failed
+        return
+    production = mapping.linear_tile_ids(M, N, K, world, CHUNK, arm, plan, tile_n=256, shift=rank + 1)
     for call in range(1, 5):
         out = op.forward(x, w, residual=torch.zeros((M // world, N), dtype=torch.bfloat16))
         assert out.shape == (M // world, N)
@@ -154,24 +192,23 @@ def test_nccl_transport_two_gloo_ranks_match_ordered_sum(arm):
 
 
 class _FakeAGLib:
-    def __init__(self, grid):
-        self.grid = grid
+    def __init__(self):
         self.calls = []
 
-    def gemm_grid(self, m, n, bn, mode):
-        return self.grid
-
-    def ag_gemm(self, shard, gather, w, b_mn, out, epi, bias, aux, gather_ptrs, flag_ptrs, local_flags,
-                rank, world, target, tile_order, status, timeout_ns, bn):
-        self.calls.append(dict(epi=epi, rank=rank, world=world, target=target, order=tile_order.tolist(),
-                               bn=bn, b_mn=b_mn, aux=aux is not None, bias=bias is not None,
-                               local_flags=local_flags, gather_ptrs=gather_ptrs))
+    def ag_gemm(self, shard, gather, w, b_mn, out, epi, bias, aux, gather_ptrs, published_ptrs, pulled_ptrs,
+                ctrl_local, ready, own_done, rank, world, epoch, own_target, pulled_target, ready_target,
+                tile_order, status, timeout_ns, bn, comm_ctas, phase, cta_stamps, block_stamps):
+        self.calls.append(dict(epi=epi, rank=rank, world=world, epoch=epoch, own=own_target,
+                               pulled=pulled_target, ready=ready_target, order=tile_order.tolist(),
+                               bn=bn, b_mn=b_mn, aux=aux is not None, bias=bias is not None, ctrl=ctrl_local,
+                               gather_ptrs=gather_ptrs, comm_ctas=comm_ctas, phase=phase))
 
 
 class _AGBuf(_Buf):
     def __init__(self, tag, m=1, k=1):
         super().__init__(tag)
         self._m, self._k = m, k
+        self.peers = [tag + 10 * r for r in range(8)]
 
     def local_view(self, shape, dtype, offset=0):
         return torch.zeros(shape, dtype=dtype)
@@ -181,12 +218,12 @@ class _AGBuf(_Buf):
 def test_ag_gemm_launch_contract(monkeypatch, rank, world):
     from tempname_5090_b200.parallel import ag_gemm
     from tempname_5090_b200.ops import gemm as G
-    fake = _FakeAGLib(grid=148)
+    fake = _FakeAGLib()
     monkeypatch.setattr(ag_gemm, "lib", lambda: fake)
     monkeypatch.setattr(ag_gemm, "count_launch", lambda n=1: None)
     m, k, n = 128 * world * 2, 256, 1024
-    gather, flags = _AGBuf(500), _AGBuf(600)
-    op = ag_gemm.AGGemm(m, k, _emulate=(rank, world, gather, flags), device="cpu")
+    gather, ctrl = _AGBuf(500), _AGBuf(600)
+    op = ag_gemm.AGGemm(m, k, comm_ctas=7, _emulate=(rank, world, gather, ctrl), device="cpu")
     shard = torch.zeros((m // world, k), dtype=torch.bfloat16)
     w = torch.zeros((n, k), dtype=torch.bfloat16)
     aux = torch.zeros((m, n), dtype=torch.bfloat16)
@@ -194,8 +231,13 @@ def test_ag_gemm_launch_contract(monkeypatch, rank, world):
     op.forward(shard, w, gelu_aux=aux)
     op.forward(shard, w.t().contiguous(), b_mn=True, gelu_grad_of=aux)
     c = fake.calls
-    # Cumulative chunk-flag targets: every CTA of every call bumps each owner's counter once.
-    assert [x["target"] for x in c] == [148, 296, 444]
+    # One launch per call; cumulative counter targets: 7 gatherer CTAs per call on
+    # every rank, (W-1) * 7 finished readers per previous call, 4 pieces (16 KB)
+    # per 128-row block of K=256 per call.
+    assert [x["epoch"] for x in c] == [1, 2, 3] and all(x["phase"] == 7 for x in c)
+    assert [x["own"] for x in c] == [7, 14, 21]
+    assert [x["pulled"] for x in c] == [0, 7 * (world - 1), 14 * (world - 1)]
+    assert op.pieces_per_block == 4 and [x["ready"] for x in c] == [4, 8, 12]
     assert [x["epi"] for x in c] == [G.EPI_BIAS, G.EPI_GELU, G.EPI_GELU_BWD]
     assert [x["aux"] for x in c] == [False, True, True] and [x["b_mn"] for x in c] == [False, False, True]
     # Own chunk first, then rank+1, ...: the first tiles need no peer data.
@@ -205,9 +247,14 @@ def test_ag_gemm_launch_contract(monkeypatch, rank, world):
     first_rows = {tid // tiles_n for tid in order[:per * tiles_n]}
     assert first_rows == set(range(rank * per, (rank + 1) * per))
     assert sorted(order) == list(range(len(order)))
-    assert all(x["local_flags"] == flags.local and x["gather_ptrs"] == gather.ptrs.data_ptr() for x in c)
+    assert all(x["ctrl"] == ctrl.local and x["gather_ptrs"] == gather.ptrs.data_ptr() for x in c)
     with pytest.raises(ValueError):
         op.forward(torch.zeros((m // world + 128, k), dtype=torch.bfloat16), w)
+    # Emulation phases: 1 opens a new epoch, 2 and 4 reuse it.
+    op.forward(shard, w, phase=1)
+    op.forward(shard, w, phase=2)
+    op.forward(shard, w, phase=4)
+    assert [x["epoch"] for x in c[3:]] == [4, 4, 4] and [x["phase"] for x in c[3:]] == [1, 2, 4]
 
 
 @pytest.mark.parametrize("bad", ["x_rows", "x_dtype", "w_k", "w_layout", "residual", "bias", "out"])
@@ -240,10 +287,10 @@ def test_gemm_rs_rejects_mismatched_operands_before_launching(monkeypatch, bad):
     assert fake.calls == [] and not op.failed and op.epoch == 0
 
 
-@pytest.mark.parametrize("bad", ["w_k", "bias", "aux", "dtype"])
+@pytest.mark.parametrize("bad", ["w_k", "bias", "bias_dtype", "aux", "dtype"])
 def test_ag_gemm_rejects_mismatched_operands_before_launching(monkeypatch, bad):
     from tempname_5090_b200.parallel import ag_gemm
-    fake = _FakeAGLib(grid=148)
+    fake = _FakeAGLib()
     monkeypatch.setattr(ag_gemm, "lib", lambda: fake)
     monkeypatch.setattr(ag_gemm, "count_launch", lambda n=1: None)
     world, m, k, n = 2, 512, 256, 512
@@ -254,13 +301,15 @@ def test_ag_gemm_rejects_mismatched_operands_before_launching(monkeypatch, bad):
         w = torch.zeros((n, k + 8), dtype=bf)
     elif bad == "bias":
         kw["bias"] = torch.zeros((n - 1,), dtype=bf)
+    elif bad == "bias_dtype":
+        kw["bias"] = torch.zeros((n,), dtype=torch.float32)
     elif bad == "aux":
         kw["gelu_aux"] = torch.zeros((m // world, n), dtype=bf)
     elif bad == "dtype":
         shard = shard.float()
     with pytest.raises(ValueError):
         op.forward(shard, w, **kw)
-    assert fake.calls == [] and op.flag_total == 0
+    assert fake.calls == [] and op.calls == 0
 
 
 def test_role_plans_reach_their_operators(monkeypatch):
@@ -294,20 +343,22 @@ def test_role_plans_reach_their_operators(monkeypatch):
     assert made[0]["plan"] is None
 
 
-def test_failure_poisons_every_operator_sharing_the_workspace(monkeypatch):
+@pytest.mark.parametrize("arm", ["flux", "flux_taco"])  # pull and push transports
+def test_failure_poisons_every_operator_sharing_the_workspace(monkeypatch, arm):
     from tempname_5090_b200.parallel import gemm_rs
     fake = _FakeLib()
     monkeypatch.setattr(gemm_rs, "lib", lambda: fake)
     monkeypatch.setattr(gemm_rs, "count_launch", lambda n=1: None)
     recv, flags = [_Buf(1), _Buf(2)], _Buf(3)
-    a = gemm_rs.GemmRS(M, N, K, _emulate=(0, 2, recv, flags), device="cpu")
-    b = gemm_rs.GemmRS(M, N, 2 * K, _emulate=(0, 2, recv, flags), device="cpu")
+    a = gemm_rs.GemmRS(M, N, K, arm=arm, _emulate=(0, 2, recv, flags), device="cpu")
+    b = gemm_rs.GemmRS(M, N, 2 * K, arm=arm, _emulate=(0, 2, recv, flags), device="cpu")
     b.workspace = a.workspace  # two projections of one (M, N) share slots, flags and epochs
     x, w = torch.zeros((M, K), dtype=torch.bfloat16), torch.zeros((N, K), dtype=torch.bfloat16)
     x2, w2 = torch.zeros((M, 2 * K), dtype=torch.bfloat16), torch.zeros((N, 2 * K), dtype=torch.bfloat16)
     a.forward(x, w)
     b.forward(x2, w2)
-    assert [c[1]["epoch"] for c in fake.calls] == [1, 1, 2, 2]  # one epoch sequence per workspace
+    per_call = 1 if arm == "flux" else 2  # pull: one launch per call; push: producer + receiver
+    assert [c[1]["epoch"] for c in fake.calls] == [e for e in (1, 2) for _ in range(per_call)]
     fake.fail_push = True
     with pytest.raises(RuntimeError, match="injected"):
         a.forward(x, w)
@@ -318,7 +369,8 @@ def test_failure_poisons_every_operator_sharing_the_workspace(monkeypatch):
     assert len(fake.calls) == n
 
 
-def test_concurrent_calls_keep_each_epoch_together(monkeypatch):
+@pytest.mark.parametrize("arm", ["flux", "flux_taco"])
+def test_concurrent_calls_keep_each_epoch_together(monkeypatch, arm):
     import threading
     import time
     from tempname_5090_b200.parallel import gemm_rs
@@ -328,10 +380,15 @@ def test_concurrent_calls_keep_each_epoch_together(monkeypatch):
             time.sleep(0)  # invite a thread switch between the two phases of one call
             super().gemm_rs_push(*a, **k)
             time.sleep(0)
+
+        def gemm_rs_pull(self, *a, **k):
+            time.sleep(0)
+            super().gemm_rs_pull(*a, **k)
+            time.sleep(0)
     fake = Yielding()
     monkeypatch.setattr(gemm_rs, "lib", lambda: fake)
     monkeypatch.setattr(gemm_rs, "count_launch", lambda n=1: None)
-    op = gemm_rs.GemmRS(M, N, K, _emulate=(0, 2, [_Buf(1), _Buf(2)], _Buf(3)), device="cpu")
+    op = gemm_rs.GemmRS(M, N, K, arm=arm, _emulate=(0, 2, [_Buf(1), _Buf(2)], _Buf(3)), device="cpu")
     x, w = torch.zeros((M, K), dtype=torch.bfloat16), torch.zeros((N, K), dtype=torch.bfloat16)
     threads = [threading.Thread(target=lambda: [op.forward(x, w) for _ in range(40)]) for _ in range(3)]
     for t in threads:
@@ -339,6 +396,9 @@ def test_concurrent_calls_keep_each_epoch_together(monkeypatch):
     for t in threads:
         t.join()
     calls = fake.calls
+    if arm == "flux":
+        assert [c[1]["epoch"] for c in calls] == list(range(1, 121)) and op.epoch == 120
+        return
     assert len(calls) == 2 * 120 and op.epoch == 120
     for i in range(0, len(calls), 2):
         assert calls[i][0] == "push" and calls[i + 1][0] == "reduce"
@@ -355,7 +415,7 @@ def test_ag_gemm_failed_launch_poisons_the_operator(monkeypatch):
             if self.fail:
                 raise RuntimeError("injected launch failure")
             super().ag_gemm(*a, **k)
-    fake = Failing(grid=148)
+    fake = Failing()
     monkeypatch.setattr(ag_gemm, "lib", lambda: fake)
     monkeypatch.setattr(ag_gemm, "count_launch", lambda n=1: None)
     m, k, n = 512, 256, 512
@@ -365,7 +425,7 @@ def test_ag_gemm_failed_launch_poisons_the_operator(monkeypatch):
     fake.fail = True
     with pytest.raises(RuntimeError, match="injected"):
         op.forward(shard, w)
-    assert op.flag_total == 148 and op.failed  # the failed call did not advance the target
+    assert op.calls == 1 and op.failed  # the failed call did not advance the epoch
     fake.fail = False
     with pytest.raises(RuntimeError, match="previously failed"):
         op.forward(shard, w)
@@ -400,3 +460,26 @@ def test_lane_skew_diagnostic_names_the_same_tile_on_every_rank(monkeypatch):
         else:
             assert (delay_tile, delay_ns) == (-1, 0)
     assert len(set(named)) == 1
+
+
+def test_device_failure_poisons_every_live_fused_operator(monkeypatch):
+    """A bounded-wait failure reported by the device poisons every live fused
+    operator and exchange workspace: none of them launches again."""
+    from tempname_5090_b200 import _native
+    from tempname_5090_b200.parallel import gemm_rs, ag_gemm
+    fake, fake_ag = _FakeLib(), _FakeAGLib()
+    monkeypatch.setattr(gemm_rs, "lib", lambda: fake)
+    monkeypatch.setattr(gemm_rs, "count_launch", lambda n=1: None)
+    monkeypatch.setattr(ag_gemm, "lib", lambda: fake_ag)
+    monkeypatch.setattr(ag_gemm, "count_launch", lambda n=1: None)
+    rs = gemm_rs.GemmRS(M, N, K, _emulate=(0, 2, [_Buf(1), _Buf(2)], _Buf(3)), device="cpu")
+    ag = ag_gemm.AGGemm(512, 256, _emulate=(0, 2, _AGBuf(4), _AGBuf(5)), device="cpu")
+    x, w = torch.zeros((M, K), dtype=torch.bfloat16), torch.zeros((N, K), dtype=torch.bfloat16)
+    rs.forward(x, w)
+    assert _native.poison_operators() >= 3  # the operator, its workspace and the AG operator
+    assert rs.failed and rs.workspace.failed and ag.failed
+    with pytest.raises(RuntimeError, match="previously failed"):
+        rs.forward(x, w)
+    with pytest.raises(RuntimeError, match="previously failed"):
+        ag.forward(torch.zeros((256, 256), dtype=torch.bfloat16), torch.zeros((512, 256), dtype=torch.bfloat16))
+    assert len(fake.calls) == 1 and fake_ag.calls == []
