@@ -44,7 +44,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--arm", default="flux")
-    ap.add_argument("--transport", default="nvlink", choices=("nvlink", "nccl"))
+    ap.add_argument("--transport", default="nvlink", choices=("nvlink", "nccl", "nccl_plain"),
+                    help="nvlink: fused operators (product); nccl: the reference's per-block sparse all_to_all; "
+                         "nccl_plain: our GEMMs with plain NCCL all_gather / reduce_scatter (unfused control)")
     ap.add_argument("--config", default="bench", choices=("bench", "small"))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling only)")
@@ -136,6 +138,16 @@ def main():
         cfg.update(hidden=512, heads=4, ffn=2048, sequence=512, micro_batch=4, vocab=4096)
     if args.layers:
         cfg["layers"] = args.layers
+    check = None
+    if world > 1 and args.transport == "nvlink":
+        # Untimed, before the model exists: the fused operators at this model's
+        # layer shapes, bitwise against NCCL collectives + the same GEMM.
+        from tempname_5090_b200.runner.validation import fused_operator_check
+        M0 = cfg["sequence"] * cfg["micro_batch"]
+        check = fused_operator_check(M0, cfg["hidden"], cfg["ffn"])
+        torch.cuda.synchronize()
+        if not (check["ag_bitwise_all_ranks"] and check["rs_bitwise_all_ranks"]):
+            raise SystemExit(f"fused operator check failed: {check}")
     model = GPT(cfg, arm=args.arm, device=dev, transport=args.transport)
     trainer = Trainer(model)
     c = model.config
@@ -214,6 +226,7 @@ def main():
                        "arm": args.arm, "transport": args.transport, "optimizer": "AdamW fp32 master lr 1e-4",
                        "l2": "inputs larger than L2 (weights alone exceed 126 MB)"},
             "gpu_launches": int(launched),
+            "check": check,
             "warmup_loss": round(warm_loss, 4),
         }
         if e2e_ms is not None:

@@ -118,7 +118,7 @@ void gemm_rs_pull(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn
                   const at::Tensor& status, int64_t timeout_ns, int64_t comm_ctas, int64_t phase,
                   const c10::optional<at::Tensor>& stamps, const c10::optional<at::Tensor>& produced,
                   int64_t delay_tile, int64_t delay_ns, int64_t max_ctas,
-                  const c10::optional<at::Tensor>& cta_stamps) {
+                  const c10::optional<at::Tensor>& cta_stamps, int64_t pair) {
   check_bf16(A, "A"); check_bf16(B, "B"); check_rows(A, "A"); check_rows(B, "B");
   check_bf16(out, "out");
   TORCH_CHECK(out.is_contiguous(), "gemm_rs_pull: out must be contiguous");
@@ -173,6 +173,7 @@ void gemm_rs_pull(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn
   c.delay_tile = int(delay_tile);
   c.delay_ns = uint64_t(delay_ns);
   c.max_ctas = int(max_ctas);
+  c.pair = int(pair);
   if (cta_stamps) {
     TORCH_CHECK(cta_stamps->is_cuda() && cta_stamps->scalar_type() == at::kLong &&
                     cta_stamps->numel() >= 2 * int64_t(tn5b::gemm::grid_ctas(c)),
@@ -185,16 +186,16 @@ void gemm_rs_pull(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn
 // All-gather -> GEMM, pull transport: out = epilogue(gather(shards) * B^T).
 // `gather` is this rank's symmetric gather buffer [M, K]; its gatherer CTAs
 // pull the peers' chunks into it while the GEMM CTAs consume arrived blocks
-// (the own chunk straight from `shard`).  `ctrl_ptrs` are the peers' control
-// blocks: published[world] flags at byte 0, the pulled counter at byte 256.
+// (the own chunk straight from `shard`).  published_* are the ranks' block
+// flags [world][M / world / 128], pulled_* their "finished reading" counters.
 void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor& B, bool b_mn,
              at::Tensor& out, int64_t epi, const c10::optional<at::Tensor>& bias,
              const c10::optional<at::Tensor>& aux, int64_t gather_ptrs, int64_t published_ptrs,
-             int64_t pulled_ptrs, int64_t ctrl_local, const at::Tensor& ready, const at::Tensor& own_done,
-             int64_t rank, int64_t world, int64_t epoch, int64_t own_target, int64_t pulled_target,
-             int64_t ready_target, const at::Tensor& tile_order, const at::Tensor& status, int64_t timeout_ns,
-             int64_t bn, int64_t comm_ctas, int64_t phase, const c10::optional<at::Tensor>& cta_stamps,
-             const c10::optional<at::Tensor>& block_stamps) {
+             int64_t pulled_ptrs, int64_t published_local, int64_t pulled_local, const at::Tensor& ready,
+             int64_t rank, int64_t world, int64_t epoch, int64_t pulled_target, int64_t ready_target,
+             const at::Tensor& tile_order, const at::Tensor& status, int64_t timeout_ns, int64_t bn,
+             int64_t comm_ctas, int64_t phase, const c10::optional<at::Tensor>& cta_stamps,
+             const c10::optional<at::Tensor>& block_stamps, int64_t pair) {
   check_bf16(shard, "shard"); check_bf16(gather, "gather"); check_bf16(B, "B"); check_bf16(out, "out");
   TORCH_CHECK(shard.is_contiguous() && gather.is_contiguous(), "shard/gather must be contiguous");
   check_rows(B, "B"); check_rows(out, "out");
@@ -217,19 +218,16 @@ void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor
   if (aux) { check_bf16(*aux, "aux"); check_rows(*aux, "aux"); c.aux = aux->data_ptr(); c.ld_aux = aux->stride(0); }
   TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == at::kInt && ready.numel() >= world * (c.M / world / 128),
               "ag_gemm: ready must be int32 [world * blocks]");
-  TORCH_CHECK(own_done.is_cuda() && own_done.scalar_type() == at::kInt, "ag_gemm: own_done must be int32");
   c.ag = 1;
   c.rank = int(rank); c.world = int(world);
   c.ag_shard = shard.data_ptr();
   c.ag_gather = reinterpret_cast<uint8_t* const*>(gather_ptrs);
   c.ag_published = reinterpret_cast<uint32_t* const*>(published_ptrs);
   c.ag_pulled = reinterpret_cast<uint32_t* const*>(pulled_ptrs);
-  c.ag_published_local = reinterpret_cast<const uint32_t*>(ctrl_local);
-  c.ag_pulled_local = reinterpret_cast<const uint32_t*>(ctrl_local + 256);
+  c.ag_published_local = reinterpret_cast<const uint32_t*>(published_local);
+  c.ag_pulled_local = reinterpret_cast<const uint32_t*>(pulled_local);
   c.ag_ready = reinterpret_cast<uint32_t*>(ready.data_ptr<int>());
-  c.ag_own_done = reinterpret_cast<uint32_t*>(own_done.data_ptr<int>());
   c.ag_epoch = uint32_t(epoch);
-  c.ag_own_target = uint32_t(own_target);
   c.ag_pulled_target = uint32_t(pulled_target);
   c.ag_ready_target = uint32_t(ready_target);
   check_cuda(tile_order, "tile_order");
@@ -239,6 +237,7 @@ void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor
   c.bn = int(bn);
   c.comm_ctas = int(comm_ctas);
   c.phase = int(phase);
+  c.pair = int(pair);
   if (cta_stamps) {
     TORCH_CHECK(cta_stamps->is_cuda() && cta_stamps->scalar_type() == at::kLong &&
                     cta_stamps->numel() >= 2 * int64_t(tn5b::gemm::grid_ctas(c)),
@@ -256,11 +255,15 @@ void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor
 
 // Grid of a fused launch (GEMM CTAs + communication CTAs) for profiling buffers.
 int64_t fused_grid(int64_t M, int64_t N, int64_t K, int64_t mode, int64_t ag, int64_t bn, int64_t comm_ctas,
-                   int64_t phase) {
+                   int64_t phase, int64_t pair) {
   tn5b::gemm::GemmCall c;
   c.M = int(M); c.N = int(N); c.K = int(K); c.mode = int(mode); c.ag = int(ag); c.bn = int(bn);
-  c.comm_ctas = int(comm_ctas); c.phase = int(phase);
+  c.comm_ctas = int(comm_ctas); c.phase = int(phase); c.pair = int(pair);
   return tn5b::gemm::grid_ctas(c);
+}
+
+int64_t fused_tile_kind(int64_t M, int64_t N, int64_t K, int64_t comm_ctas) {
+  return tn5b::gemm::fused_tile_kind(int(M), int(N), int(K), int(comm_ctas));
 }
 
 // Number of SMs of the current device.
@@ -285,6 +288,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ag_gemm", &ag_gemm, "all-gather (in-launch pull) fused into a tcgen05 GEMM", nogil());
   m.def("sm_count", &sm_count, "number of SMs of the current device");
   m.def("fused_grid", &fused_grid, "grid of a fused GEMM launch (GEMM + communication CTAs)");
+  m.def("fused_tile_kind", &fused_tile_kind, "tile kind the wave model picks for a fused launch");
   register_kernels(m);
   register_comm(m);
 }

@@ -11,12 +11,13 @@
 //                multicast) into a shared-memory ring and reduce them in source
 //                order 0..W-1 with BF16 rounding after every source, fusing
 //                residual + bias, while the GEMM is still producing later tiles.
-//   ag_gatherer  (all-gather -> GEMM)  each rank first copies its own shard into
-//                its own chunk of its gather buffer and publishes it to every
-//                peer; then every rank pulls the peers' chunks (bulk loads from
-//                the peers' memory) into its local gather buffer and counts the
-//                arrived 16 KB pieces per 128-row block; the GEMM CTAs wait for
-//                a block's count before their TMA loads read it (local memory).
+//   ag_gatherer  (all-gather -> GEMM)  each rank copies its own shard into its
+//                own chunk of its gather buffer and publishes every 128-row
+//                block to every peer as soon as the block is complete; every
+//                rank pulls the peers' published blocks (bulk loads from the
+//                peers' memory) into its local gather buffer and counts the
+//                arrived 16 KB pieces per block; the GEMM CTAs wait for a
+//                block's count before their TMA loads read it (local memory).
 //                After its last load from a peer a gatherer CTA adds 1 to that
 //                peer's `pulled` counter; a rank overwrites its own chunk only
 //                after every peer's CTAs have signalled for the previous call,
@@ -70,8 +71,11 @@ __device__ __forceinline__ uint32_t atom_acq_rel_gpu_add(uint32_t* p, uint32_t v
 // Flag tiles are 128 rows x TILE_CC 64-column chunks of this rank's rows (one
 // GEMM CTA's share of a tile); the flag of (source s, local flag tile t) is
 // my_flags[s * tiles + t].
+// `tres` maps the residual [rows_per_dest, N] (box 64 x 128, 128-byte swizzle):
+// with a residual, the loader brings each piece's residual tile into the ring
+// ahead of the piece's sources, so it never waits on a global load.
 template <int TILE_CC>
-__device__ void rs_reducer(const Params& p, uint8_t* smem) {
+__device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tres) {
   constexpr int TILE_RB = 1;
   const PullRsArgs& a = p.pull;
   uint8_t* ring = smem;
@@ -111,6 +115,18 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem) {
       for (int pr = 0; pr < TILE_RB && ok; ++pr) {
         for (int pc = 0; pc < TILE_CC && ok; ++pc) {
           const int64_t off = piece_offset(rb_base + ltm * TILE_RB + pr, tn * TILE_CC + pc, n_chunks);
+          if (a.residual) {
+            const int st = int(seq % kCommStages);
+            const uint32_t ph = (seq / kCommStages) & 1u;
+            if (!mbar_wait(&empty[st], ph ^ 1u, p.timeout_ns, p.status, kTimeoutProducerEmpty, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[st], kPiece);
+            tma_load_2d(ring + st * kPiece, tres, &full[st], (tn * TILE_CC + pc) * 64, (ltm * TILE_RB + pr) * 128);
+            last_parity[st] = int(ph);
+            ++seq;
+          }
           for (int s = 0; s < world; ++s) {
             if (!((waited >> s) & 1u)) {
               if (!wait_flag_geq(a.my_flags + int64_t(s) * tiles + lt, p.rs.epoch, p.timeout_ns, p.status,
@@ -153,6 +169,31 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem) {
     const int ltm = lt / tiles_n, tn = lt % tiles_n;
     for (int pr = 0; pr < TILE_RB; ++pr) {
       for (int pc = 0; pc < TILE_CC; ++pc) {
+        // This thread's eight 16-byte units: unit rt + 128u is row rt/8 + 16u,
+        // columns (rt % 8) * 8 .. +8 of the piece.  The residual tile arrives in
+        // the ring first (swizzled: unit c of row r sits at c ^ (r & 7)); the
+        // bias load is issued here and completes during the source loop.
+        const int col = (tn * TILE_CC + pc) * 64 + (rt % 8) * 8;
+        const int row0 = (ltm * TILE_RB + pr) * 128 + rt / 8;
+        uint4 bias4 = make_uint4(0, 0, 0, 0);
+        if (a.bias) bias4 = ld_global_nc_v4(a.bias + col);
+        uint4 res[8];
+        if (a.residual) {
+          const int st = int(seq % kCommStages);
+          const uint32_t ph = (seq / kCommStages) & 1u;
+          if (!warp_wait(&full[st], ph, p.timeout_ns, p.status, kTimeoutMmaFull, abort_flag)) return;
+          const uint32_t buf = smem_u32(ring + st * kPiece);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int r = rt / 8 + 16 * u;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(res[u].x), "=r"(res[u].y), "=r"(res[u].z), "=r"(res[u].w)
+                         : "r"(buf + uint32_t(r * 128 + (((rt % 8) ^ (r & 7)) << 4))));
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[st]);
+          ++seq;
+        }
         uint32_t acc[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = zero;
@@ -177,16 +218,12 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem) {
           ++seq;
         }
         // Epilogue: out = bf16(bf16(residual + y) + bias), written to this rank's rows.
-        const int col = (tn * TILE_CC + pc) * 64 + (rt % 8) * 8;
-        uint4 bias4 = make_uint4(0, 0, 0, 0);
-        if (a.bias) bias4 = *reinterpret_cast<const uint4*>(a.bias + col);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const int row = (ltm * TILE_RB + pr) * 128 + (rt + 128 * u) / 8;
-          const int64_t idx = int64_t(row) * p.N + col;
+          const int64_t idx = int64_t(row0 + 16 * u) * p.N + col;
           uint32_t* q = acc + 4 * u;
           if (a.residual) {
-            const uint4 r = *reinterpret_cast<const uint4*>(a.residual + idx);
+            const uint4 r = res[u];
             q[0] = add_bf16x2(r.x, q[0]);
             q[1] = add_bf16x2(r.y, q[1]);
             q[2] = add_bf16x2(r.z, q[2]);
@@ -211,22 +248,28 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem) {
 
 // --------------------------------------------------------------- gatherer
 // The single issuing thread streams a sequence of pieces (source address, local
-// destination, completion counter) through the ring: loads run up to
-// kCommStages ahead, each landed piece is bulk-stored to local memory, and the
-// piece's counter is incremented (release, GPU scope) once its store has
-// completed; store completions are confirmed with a lag of kLag bulk groups.
-// A piece may carry a remote counter to bump (release, system scope) as soon as
-// it has landed in shared memory: the "no longer reading" signal to its source.
+// destination) through the ring: up to kLoads loads are in flight, each landed
+// piece is bulk-stored to local memory.  Pieces travel in runs (consecutive
+// pieces of one 128-row block): synchronisation happens once per run, not per
+// piece -- when a run's last store has completed (confirmed kLag bulk groups
+// late, so the engine never waits for a write to land) the block's counter is
+// advanced by the run's length.  The ring keeps kCommStages - kLoads stages of
+// slack, so reusing a stage never waits for the store just issued to finish
+// reading shared memory.  A piece may carry a remote counter to bump (release,
+// system scope) once it has landed: the "no longer reading" signal to its source.
 struct PieceStream {
-  static constexpr int kLag = 4;
+  static constexpr int kLoads = kCommStages - 2;
+  static constexpr int kLag = 24;
   uint8_t* ring;
   uint64_t* full;
   const Params* p;
   uint32_t issued, stored;            // pieces loaded / stored
-  uint32_t* pending[kLag + 1];        // counters of stored pieces awaiting completion, by store index
+  uint32_t* pending[kLag + 1];        // run counters to advance, by store index of the run's last piece
+  uint32_t pending_n[kLag + 1];
   int last_parity[kCommStages];
   uint8_t* q_dst[kCommStages];
-  uint32_t* q_ctr[kCommStages];
+  uint32_t* q_ctr[kCommStages];       // set on a run's last piece
+  uint32_t q_n[kCommStages];          // that run's length
   uint32_t* q_landed[kCommStages];
   uint32_t q_bytes[kCommStages];
 
@@ -246,25 +289,32 @@ struct PieceStream {
     if (q_landed[st]) red_release_sys_add(q_landed[st], 1u);
     bulk_store(q_dst[st], smem_u32(ring + st * kPiece), q_bytes[st]);
     bulk_commit_group();
-    // The store issued kLag groups ago has completed: publish its counter.
-    bulk_wait_group<kLag>();
-    const int done_slot = int((stored + 1) % (kLag + 1));  // store index stored - kLag
-    if (pending[done_slot]) {
-      fence_proxy_async_global();
-      count(pending[done_slot]);
-    }
-    pending[done_slot] = nullptr;
-    pending[stored % (kLag + 1)] = q_ctr[st];
+    const int slot = int(stored % (kLag + 1));
+    pending[slot] = q_ctr[st];
+    pending_n[slot] = q_n[st];
     ++stored;
+    // The store issued kLag groups ago has completed: advance its run's counter.
+    const int done = int(stored % (kLag + 1));  // store index stored - 1 - kLag
+    if (pending[done]) {
+      bulk_wait_group<kLag>();
+      fence_proxy_async_global();
+      count(pending[done], pending_n[done]);
+      pending[done] = nullptr;
+    }
     return true;
   }
-  // Queue one piece; stores the oldest piece first when the ring is full.
-  __device__ bool push(const uint8_t* src, uint8_t* dst, uint32_t bytes, uint32_t* ctr, uint32_t* landed) {
-    if (issued - stored == uint32_t(kCommStages) && !store_one()) return false;
+  // Queue one piece (ctr/n on a run's last piece); stores the oldest piece first
+  // when kLoads are in flight.
+  __device__ bool push(const uint8_t* src, uint8_t* dst, uint32_t bytes, uint32_t* ctr, uint32_t n,
+                       uint32_t* landed) {
+    if (issued - stored == uint32_t(kLoads) && !store_one()) return false;
     const int st = int(issued % kCommStages);
-    if (issued >= uint32_t(kCommStages)) bulk_wait_group_read<0>();  // the stage's last store has read it
+    // The stage's previous piece (issued - kCommStages) was stored at least
+    // kCommStages - kLoads stores ago: all but the newest store have read their stage.
+    if (issued >= uint32_t(kCommStages)) bulk_wait_group_read<kCommStages - kLoads - 1>();
     q_dst[st] = dst;
     q_ctr[st] = ctr;
+    q_n[st] = n;
     q_landed[st] = landed;
     q_bytes[st] = bytes;
     mbar_arrive_expect_tx(&full[st], bytes);
@@ -273,28 +323,40 @@ struct PieceStream {
     ++issued;
     return true;
   }
-  // Store everything queued and publish every counter.
+  // Store everything queued and advance every counter.
   __device__ bool finish() {
     while (stored < issued)
       if (!store_one()) return false;
     bulk_wait_group_all();
     fence_proxy_async_global();
     for (int j = 0; j <= kLag; ++j) {
-      if (pending[j]) count(pending[j]);
+      if (pending[j]) count(pending[j], pending_n[j]);
       pending[j] = nullptr;
     }
     return true;
   }
-  // One more stored piece of a block; with block stamps, the piece completing
-  // the block records the time.
-  __device__ void count(uint32_t* ctr) {
-    unsigned long long* stamps = p->gather.block_stamps;
-    if (!stamps) {
-      red_release_gpu_add(ctr, 1u);
+  // A run of n pieces of one block is stored.  The run that completes an
+  // own-chunk block publishes the block to every peer; with block stamps the
+  // completing run also records the time.
+  __device__ void count(uint32_t* ctr, uint32_t n) {
+    const GatherArgs& g = p->gather;
+    const int64_t idx = ctr - g.ready;
+    const int blocks = g.rows_per_src / 128;
+    const bool own = idx / blocks == g.rank;
+    if (!own && !g.block_stamps) {
+      red_release_gpu_add(ctr, n);
       return;
     }
-    if (atom_acq_rel_gpu_add(ctr, 1u) + 1u == p->gather.ready_target)
-      stamps[ctr - p->gather.ready] = globaltimer_ns();
+    if (atom_acq_rel_gpu_add(ctr, n) + n != g.ready_target) return;
+    if (g.block_stamps) g.block_stamps[idx] = globaltimer_ns();
+    if (own) {
+      // Every piece of own block idx % blocks is in local memory (acquired through
+      // the counter): release it to the peers at system scope.
+      fence_acq_rel_sys();
+      const int b = int(idx % blocks);
+      for (int d = 0; d < g.world; ++d)
+        if (d != g.rank) st_release_sys(g.published[d] + g.rank * blocks + b, g.epoch);
+    }
   }
   // Abort path: wait (bounded) for every load in flight, then for the stores.
   __device__ void drain() {
@@ -304,6 +366,8 @@ struct PieceStream {
     bulk_wait_group_all();
   }
 };
+
+constexpr int kRunPieces = 8;  // pieces per run (128 KB): one counter update per run
 
 __device__ void ag_gatherer(const Params& p, uint8_t* smem) {
   if (threadIdx.x != 0) return;
@@ -316,58 +380,68 @@ __device__ void ag_gatherer(const Params& p, uint8_t* smem) {
   const int ctas = p.comm_ctas;
   const int rank = g.rank, world = g.world;
   const int64_t block_bytes = int64_t(128) * g.K * 2;
-  const int64_t pieces_per_block = (block_bytes + kPiece - 1) / kPiece;
+  const int pieces_per_block = int((block_bytes + kPiece - 1) / kPiece);
+  const int runs_per_block = (pieces_per_block + kRunPieces - 1) / kRunPieces;
   const int blocks = g.rows_per_src / 128;
-  const int64_t pieces = pieces_per_block * blocks;  // per chunk
+  const int runs = runs_per_block * blocks;  // per chunk
   uint8_t* local = g.gather[rank];
   PieceStream ps;
   ps.init(ring, full, &p);
   bool ok = true;
+  // Queue run r of a chunk (src / dst chunk bases); `landed` on its last piece.
+  auto queue_run = [&](const uint8_t* src, uint8_t* dst, int chunk, int r, uint32_t* landed) -> bool {
+    const int b = r / runs_per_block;
+    const int first = (r % runs_per_block) * kRunPieces;
+    const int n = min(kRunPieces, pieces_per_block - first);
+    uint32_t* ctr = g.ready + int64_t(chunk) * blocks + b;
+    for (int k = first; k < first + n; ++k) {
+      const int64_t off = b * block_bytes + int64_t(k) * kPiece;
+      const uint32_t bytes = uint32_t(min(int64_t(kPiece), block_bytes - int64_t(k) * kPiece));
+      const bool last = k == first + n - 1;
+      if (!ps.push(src + off, dst + off, bytes, last ? ctr : nullptr, last ? uint32_t(n) : 0u,
+                   last ? landed : nullptr))
+        return false;
+    }
+    return true;
+  };
 
   if (g.phase & 1) {
     // Own shard -> own chunk of the gather buffer, once every peer has finished
-    // reading this chunk's previous contents; then publish it to every peer.
+    // reading this chunk's previous contents.  Each block is published to the
+    // peers as soon as its last run is stored (PieceStream::count).
     if (!wait_flag_geq(g.pulled_local, g.pulled_target, p.timeout_ns, p.status, kTimeoutPeerFlag)) return;
     fence_proxy_async_global();
     uint8_t* own = local + int64_t(rank) * g.chunk_bytes;
-    for (int64_t j = cta; j < pieces && ok; j += ctas) {
-      const int64_t b = j / pieces_per_block, k = j % pieces_per_block;
-      const int64_t off = b * block_bytes + k * kPiece;
-      const uint32_t bytes = uint32_t(min(int64_t(kPiece), block_bytes - k * kPiece));
-      ok = ps.push(g.shard + off, own + off, bytes, g.ready + int64_t(rank) * blocks + b, nullptr);
-    }
+    for (int r = cta; r < runs && ok; r += ctas) ok = queue_run(g.shard, own, rank, r, nullptr);
     if (ok) ok = ps.finish();
     if (!ok) {
       ps.drain();
       return;
     }
-    // The last CTA to finish its part publishes the chunk to every peer.
-    if (atom_acq_rel_gpu_add(g.own_done, 1u) + 1u == g.own_target) {
-      fence_acq_rel_sys();
-      for (int d = 0; d < world; ++d)
-        if (d != rank) st_release_sys(g.published[d] + rank, g.epoch);
-    }
   }
   if (g.phase & 2) {
-    // Peers' chunks, rank+1 first (every rank reads a different peer at a time).
+    // Peers' chunks, rank+1 first (every rank reads a different peer at a
+    // time), each 128-row block once its owner has published it.
     for (int step = 1; step < world && ok; ++step) {
       const int c = (rank + step) % world;
-      if (!wait_flag_geq(g.published_local + c, g.epoch, p.timeout_ns, p.status, kTimeoutAgChunk)) {
-        ok = false;
-        break;
-      }
-      fence_proxy_async_global();
       const uint8_t* src = g.gather[c] + int64_t(c) * g.chunk_bytes;
       uint8_t* dst = local + int64_t(c) * g.chunk_bytes;
-      int64_t last = -1;  // this CTA's last piece of chunk c
-      for (int64_t j = cta; j < pieces; j += ctas) last = j;
+      int last = -1;  // this CTA's last run of chunk c
+      for (int r = cta; r < runs; r += ctas) last = r;
       if (last < 0) red_release_sys_add(g.pulled[c], 1u);  // nothing to read from c
-      for (int64_t j = cta; j < pieces && ok; j += ctas) {
-        const int64_t b = j / pieces_per_block, k = j % pieces_per_block;
-        const int64_t off = b * block_bytes + k * kPiece;
-        const uint32_t bytes = uint32_t(min(int64_t(kPiece), block_bytes - k * kPiece));
-        ok = ps.push(src + off, dst + off, bytes, g.ready + int64_t(c) * blocks + b,
-                     j == last ? g.pulled[c] : nullptr);
+      int waited = -1;
+      for (int r = cta; r < runs && ok; r += ctas) {
+        const int b = r / runs_per_block;
+        if (b != waited) {
+          if (!wait_flag_geq(g.published_local + c * blocks + b, g.epoch, p.timeout_ns, p.status,
+                             kTimeoutAgChunk)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+          waited = b;
+        }
+        ok = queue_run(src, dst, c, r, r == last ? g.pulled[c] : nullptr);
       }
     }
     if (ok) ok = ps.finish();

@@ -115,21 +115,25 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
 // not overlapped and its 4x larger tiles quantise into fewer, coarser waves.
 enum TileKind { kSingle = 0, kPair = 1, kWide = 2 };
 
-int tile_kind(const GemmCall& c, int bn) {
-  if (c.mode != 0 || bn != 256) return kSingle;
-  if (c.pair >= 0) {
-    if (c.pair == kWide && c.ag) return kPair;  // no all-gather wide instantiation
-    return c.pair <= kWide ? c.pair : kSingle;
-  }
-  if (c.ag || c.tile_order || c.K < 1024) return kSingle;  // explicit orders index single-CTA tiles
-  const double sms = sm_count();
-  const double tiles_s = double((c.M + 127) / 128) * double((c.N + 255) / 256);
-  const double tiles_w = double((c.M + 255) / 256) * double((c.N + 511) / 512);
-  const double waves_s = std::ceil(tiles_s / sms), waves_w = std::ceil(tiles_w / (sms / 2));
+// Wave-model choice between the single-CTA and the wide tile on `sms` SMs.
+int auto_kind(int M, int N, int K, double sms) {
+  if (K < 1024 || sms < 2) return kSingle;
+  const double tiles_s = double((M + 127) / 128) * double((N + 255) / 256);
+  const double tiles_w = double((M + 255) / 256) * double((N + 511) / 512);
+  const double waves_s = std::ceil(tiles_s / sms), waves_w = std::ceil(tiles_w / std::floor(sms / 2));
   // Per-SM work of one wave: 1 unit (128 x 256 x K) single, 2 units wide.
   const double cost_s = waves_s / kEffSingle;
-  const double cost_w = 2.0 * waves_w * (1.0 + kWideEpilogueK / double(c.K)) / kEffWide;
+  const double cost_w = 2.0 * waves_w * (1.0 + kWideEpilogueK / double(K)) / kEffWide;
   return cost_w < cost_s ? kWide : kSingle;
+}
+
+int tile_kind(const GemmCall& c, int bn) {
+  // The push epilogues write 16-byte stores into peers' slots per single-CTA tile.
+  if (bn != 256 || c.mode == 1 || c.mode == 2) return kSingle;
+  if (c.pair >= 0) return c.pair <= kWide ? c.pair : kSingle;  // explicit (tables built in its units)
+  if (c.tile_order) return kSingle;                            // a table without a kind: single-CTA units
+  const bool comm_mode = c.mode == 3 || c.ag;
+  return auto_kind(c.M, c.N, c.K, double(sm_count() - (comm_mode ? c.comm_ctas : 0)));
 }
 
 int pick_bn(const GemmCall& c) {
@@ -145,6 +149,10 @@ int pick_bn(const GemmCall& c) {
 }  // namespace
 
 std::string last_error() { return g_last_error; }
+
+int fused_tile_kind(int M, int N, int K, int comm_ctas) {
+  return auto_kind(M, N, K, double(sm_count() - comm_ctas));
+}
 
 int comm_active(const GemmCall& c) {
   const bool comm_mode = c.mode == 3 || c.ag;
@@ -195,8 +203,6 @@ int run(const GemmCall& c, cudaStream_t stream) {
   const int kind = tile_kind(c, bn);
   const bool pair = kind != kSingle;
   const int tile_n = kind == kWide ? 2 * bn : bn;
-  if (c.tile_order && pair)
-    return fail("gemm: an explicit tile order lists single-CTA tiles; use pair=0 with it");
   Params p{};
   p.M = c.M; p.N = c.N; p.K = c.K;
   p.tiles_m = (c.M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
@@ -222,7 +228,8 @@ int run(const GemmCall& c, cudaStream_t stream) {
         c.M % c.world)
       return fail("gemm-rs-pull: bad args");
     const int rows = c.M / c.world;
-    if (rows % kBM || c.N % 256) return fail("gemm-rs-pull: rows per destination % 128 and N % 256 required");
+    if (rows % (pair ? 2 * kBM : kBM) || c.N % tile_n)
+      return fail("gemm-rs-pull: rows per destination must be a multiple of the tile height and N of its width");
     if ((c.phase & 2) && c.comm_ctas < 1) return fail("gemm-rs-pull: the reduce phase needs comm_ctas >= 1");
     if ((reinterpret_cast<uintptr_t>(c.rs_partial_local) | reinterpret_cast<uintptr_t>(c.rs_out)) & 15)
       return fail("gemm-rs-pull: partial and output must be 16-byte aligned");
@@ -261,10 +268,10 @@ int run(const GemmCall& c, cudaStream_t stream) {
   }
   if (c.ag) {
     if (!c.ag_shard || !c.ag_gather || !c.ag_published || !c.ag_pulled || !c.ag_published_local ||
-        !c.ag_pulled_local || !c.ag_ready || !c.ag_own_done || c.world < 2 || c.M % c.world || c.a_mn)
+        !c.ag_pulled_local || !c.ag_ready || c.world < 2 || c.M % c.world || c.a_mn)
       return fail("ag-gemm: bad args");
     const int rows = c.M / c.world;
-    if (rows % kBM) return fail("ag-gemm: rows per source must be a multiple of 128");
+    if (rows % (pair ? 2 * kBM : kBM)) return fail("ag-gemm: rows per source must be a multiple of the tile height");
     if (reinterpret_cast<uintptr_t>(c.ag_shard) & 15 || c.lda != c.K)
       return fail("ag-gemm: shard must be 16-byte aligned and the gather buffer dense [M, K]");
     if ((c.phase & 3) && c.comm_ctas < 1) return fail("ag-gemm: the gather phases need comm_ctas >= 1");
@@ -275,12 +282,10 @@ int run(const GemmCall& c, cudaStream_t stream) {
     g.published_local = c.ag_published_local;
     g.pulled_local = c.ag_pulled_local;
     g.ready = c.ag_ready;
-    g.own_done = c.ag_own_done;
     g.shard = static_cast<const uint8_t*>(c.ag_shard);
     g.chunk_bytes = int64_t(rows) * c.K * 2;
     g.rank = c.rank; g.world = c.world; g.rows_per_src = rows; g.K = c.K;
     g.epoch = c.ag_epoch;
-    g.own_target = c.ag_own_target;
     g.pulled_target = c.ag_pulled_target;
     g.ready_target = c.ag_ready_target;
     g.phase = c.phase;
@@ -306,12 +311,16 @@ int run(const GemmCall& c, cudaStream_t stream) {
              make_map(&mo, c.out, c.N, c.M, c.ldo, 64, 32)) {
     p.tma_store = 1;
   }
-  // AG: the own chunk is read straight from the shard ([M/W, K]).
+  // AG: the own chunk is read straight from the shard ([M/W, K]); pull RS: the
+  // reducer CTAs load the residual [M/W, N] in 128 x 64 tiles.
   CUtensorMap ma2 = ma;
   if (c.ag && !make_map(&ma2, c.ag_shard, c.K, c.M / c.world, c.K, 64, kBM))
     return fail("ag-gemm: shard tensor map");
+  if (c.mode == 3 && c.rs_residual && !make_map(&ma2, c.rs_residual, c.N, c.M / c.world, c.N, 64, kBM))
+    return fail("gemm-rs-pull: residual tensor map");
   const int grid = grid_ctas(c);
   if (c.ag) {
+    if (kind == kWide) return launch<256, 4, 64, kModeLocal, true, true, true>(c, p, ma, mb, mo, ma2, grid, stream);
     if (pair) return launch<256, 6, 64, kModeLocal, true, true>(c, p, ma, mb, mo, ma2, grid, stream);
     if (bn == 256) return launch<256, 4, 64, kModeLocal, true>(c, p, ma, mb, mo, ma2, grid, stream);
     return launch<128, 6, 64, kModeLocal, true>(c, p, ma, mb, mo, ma2, grid, stream);
@@ -327,6 +336,8 @@ int run(const GemmCall& c, cudaStream_t stream) {
     case 2:
       return launch<256, 4, 128, kModeRsTaco, false>(c, p, ma, mb, mo, ma2, grid, stream);
     case 3:
+      if (kind == kWide) return launch<256, 4, 64, kModeRsPull, false, true, true>(c, p, ma, mb, mo, ma2, grid, stream);
+      if (pair) return launch<256, 6, 64, kModeRsPull, false, true>(c, p, ma, mb, mo, ma2, grid, stream);
       return launch<256, 4, 64, kModeRsPull, false>(c, p, ma, mb, mo, ma2, grid, stream);
     default:
       return fail("gemm: unknown mode");

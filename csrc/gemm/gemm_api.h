@@ -59,13 +59,12 @@ struct GemmCall {
   int ag = 0;
   const void* ag_shard = nullptr;                 // [M/world, K] local shard (contiguous)
   uint8_t* const* ag_gather = nullptr;            // device array [world]: gather buffers
-  uint32_t* const* ag_published = nullptr;        // device array [world]: published[world] flags
+  uint32_t* const* ag_published = nullptr;        // device array [world]: published[world][blocks] flags
   uint32_t* const* ag_pulled = nullptr;           // device array [world]: pulled counters
   const uint32_t* ag_published_local = nullptr;
   const uint32_t* ag_pulled_local = nullptr;
   uint32_t* ag_ready = nullptr;                   // local [world][M/world/128]
-  uint32_t* ag_own_done = nullptr;                // local [1]
-  uint32_t ag_epoch = 0, ag_own_target = 0, ag_pulled_target = 0, ag_ready_target = 0;
+  uint32_t ag_epoch = 0, ag_pulled_target = 0, ag_ready_target = 0;
   unsigned long long* ag_block_stamps = nullptr;  // optional: arrival time of every gathered block
   unsigned long long* cta_stamps = nullptr;       // optional [grid][2]: start / end of every CTA
   // status / bounded waits
@@ -79,6 +78,9 @@ struct GemmCall {
 int grid_ctas(const GemmCall& c);
 // GEMM-role CTAs of this call (0 when the call runs communication phases only).
 int gemm_ctas(const GemmCall& c);
+// Tile kind (0 single CTA 128x256, 2 wide CTA pair 256x512) the wave model picks
+// for a fused launch whose GEMM runs on all SMs but `comm_ctas`.
+int fused_tile_kind(int M, int N, int K, int comm_ctas);
 int run(const GemmCall& c, cudaStream_t stream);
 std::string last_error();
 

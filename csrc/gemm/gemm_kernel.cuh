@@ -80,17 +80,15 @@ struct RsArgs {
 // counts the arrived pieces of each 128-row block (cumulative over calls).
 struct GatherArgs {
   uint8_t* const* gather;          // device array [world]: every rank's gather buffer ([M, K] bf16)
-  uint32_t* const* published;      // device array [world]: every rank's published[world] flags
+  uint32_t* const* published;      // device array [world]: every rank's published[world][blocks] flags
   uint32_t* const* pulled;         // device array [world]: every rank's pulled counter
-  const uint32_t* published_local; // this rank's published[world]
+  const uint32_t* published_local; // this rank's published[world][blocks]
   const uint32_t* pulled_local;    // this rank's pulled counter
   uint32_t* ready;                 // local [world][rows_per_src / 128] arrived-piece counters
-  uint32_t* own_done;              // local counter of gatherer CTAs done with the own chunk
   const uint8_t* shard;            // local shard [rows_per_src, K] bf16 (contiguous)
   int64_t chunk_bytes;             // rows_per_src * K * 2
   int rank, world, rows_per_src, K;
-  uint32_t epoch;                  // this call's epoch (published flags)
-  uint32_t own_target;             // own_done value once every gatherer CTA of this call is done
+  uint32_t epoch;                  // this call's epoch (published block flags)
   uint32_t pulled_target;          // pulled value once every peer finished reading the previous call
   uint32_t ready_target;           // ready[c][b] once block b of chunk c has fully arrived
   int phase;                       // communication CTAs: bit0 own chunk + publish, bit1 pull peers
@@ -303,7 +301,8 @@ namespace gemm {
 // AG: the A rows of chunk `rank` are read from the local shard (tmap_a2), the
 // other chunks from the local gather buffer (tmap_a) once they have arrived.
 // kModeRsPull: tmap_out maps the local partial buffer as a [M/128 * N/64 * 128, 64]
-// matrix (tile-major pieces the reducer pulls with single bulk loads).
+// matrix (tile-major pieces the reducer pulls with single bulk loads) and
+// tmap_a2 the residual [M/W, N] that the reducer CTAs load tile by tile.
 template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false, bool WIDE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -330,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (p.cta_stamps && threadIdx.x == 0) p.cta_stamps[2 * blockIdx.x] = globaltimer_ns();
   if (int(blockIdx.x) < p.comm_ctas) {
     // Communication role (no TMEM, no cluster barriers).
-    if constexpr (MODE == kModeRsPull) rs_reducer<kTileNOf<BN, WIDE> / 64>(p, smem);
+    if constexpr (MODE == kModeRsPull) rs_reducer<kTileNOf<BN, WIDE> / 64>(p, smem, &tmap_a2);
     else if constexpr (AG) ag_gatherer(p, smem);
     if (p.cta_stamps) {
       __syncthreads();

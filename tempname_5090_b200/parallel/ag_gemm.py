@@ -4,12 +4,12 @@
 
 ONE persistent launch per call with two kinds of CTAs:
 
-* `comm_ctas` gatherer CTAs first copy this rank's shard into its own chunk of
-  its symmetric gather buffer and publish it (a system-scope release of
-  `published[rank] = epoch` on every peer), then pull every peer's chunk
-  (rank+1 first) from the peer's gather buffer with bulk loads -- no multicast
-  -- into the local gather buffer, counting the arrived 16 KB pieces of each
-  128-row block;
+* `comm_ctas` gatherer CTAs copy this rank's shard into its own chunk of its
+  symmetric gather buffer, publishing each 128-row block as soon as it is
+  complete (a system-scope release of `published[rank][block] = epoch` on
+  every peer), and pull every peer's published blocks (rank+1 first) from the
+  peer's gather buffer with bulk loads -- no multicast -- into the local gather
+  buffer, counting the arrived 16 KB pieces of each block;
 * the other CTAs run the tcgen05 GEMM: tiles of the own chunk first, read
   straight from the shard, then each peer chunk's tiles once their block count
   is complete (bounded wait), with TMA loads of LOCAL memory only.
@@ -43,16 +43,23 @@ from ..utils import tracing
 DEFAULT_TIMEOUT_NS = 10_000_000_000
 DEFAULT_COMM_CTAS = int(os.environ.get("TN5B_AG_COMM_CTAS", "20"))
 PIECE_BYTES = 16384
-CTRL_BYTES = 512          # published[world] u32 at byte 0, pulled u32 at byte 256
-PULLED_OFFSET = 256
 
 
-def ag_tile_order(m: int, n: int, world: int, rank: int, bn: int) -> list:
+def control_layout(m: int) -> tuple:
+    """Byte layout of a rank's control block: published[world][M/W/128] u32 block
+    flags at 0, the pulled counter at the next 256-byte boundary.
+    Returns (pulled offset, total bytes)."""
+    flags = (m // 128) * 4
+    pulled = (flags + 255) // 256 * 256
+    return pulled, pulled + 256
+
+
+def ag_tile_order(m: int, n: int, world: int, rank: int, bn: int, tile_m: int = 128) -> list:
     """Own chunk first, then rank+1, ... (the order chunks arrive in); inside a
     chunk, column tiles outer so a weight panel is reused by all row tiles of
-    the chunk."""
+    the chunk.  Tiles are tile_m x bn (256 x 512 for the wide CTA pair)."""
     rows = m // world
-    tm_per = rows // 128
+    tm_per = rows // tile_m
     tn = (n + bn - 1) // bn
     out = []
     for step in range(world):
@@ -66,7 +73,7 @@ def ag_tile_order(m: int, n: int, world: int, rank: int, bn: int) -> list:
 class AGGemm:
     def __init__(self, m: int, k: int, group=None, timeout_ns: int = DEFAULT_TIMEOUT_NS,
                  comm_ctas: int | None = None, _emulate: tuple | None = None,
-                 device: torch.device | None = None):
+                 device: torch.device | None = None, tile_kind: int | None = None):
         if _emulate is not None:
             self.rank, self.world, self.gather, self.ctrl = _emulate
         else:
@@ -78,21 +85,24 @@ class AGGemm:
         if k % 8:
             raise ValueError("K must be a multiple of 8")
         self.m, self.k, self.group = m, k, group
+        if tile_kind not in (None, 0, 2) or (tile_kind == 2 and (m // self.world) % 256):
+            raise ValueError("tile_kind is 0 (single CTA) or 2 (wide CTA pair, rows per rank % 256 == 0)")
+        self._kind = tile_kind
         self.comm_ctas = DEFAULT_COMM_CTAS if comm_ctas is None else int(comm_ctas)
         if not 1 <= self.comm_ctas <= 64:
             raise ValueError("comm_ctas must be in [1, 64]")
         # `device` defaults to the current CUDA device; CPU serves host-logic tests.
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.timeout_ns = int(timeout_ns)
+        self.pulled_offset, ctrl_bytes = control_layout(m)
         if _emulate is None:
             self.gather = SymmetricBuffer(m * k * 2, group)
-            self.ctrl = SymmetricBuffer(CTRL_BYTES, group)
+            self.ctrl = SymmetricBuffer(ctrl_bytes, group)
         self.blocks = (m // self.world) // 128
         self.pieces_per_block = -(-(128 * k * 2) // PIECE_BYTES)
         self.ready = torch.zeros(self.world * self.blocks, dtype=torch.int32, device=self.device)
-        self.own_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._published_ptrs = torch.tensor([p for p in self.ctrl.peers], dtype=torch.int64, device=self.device)
-        self._pulled_ptrs = torch.tensor([p + PULLED_OFFSET for p in self.ctrl.peers], dtype=torch.int64,
+        self._pulled_ptrs = torch.tensor([p + self.pulled_offset for p in self.ctrl.peers], dtype=torch.int64,
                                          device=self.device)
         self.calls = 0            # completed epochs
         self.failed = False
@@ -106,19 +116,31 @@ class AGGemm:
         """This rank's gathered [M, K] input of the most recent call."""
         return self.gather.local_view((self.m, self.k), torch.bfloat16)
 
-    def _order(self, n: int, bn: int) -> torch.Tensor:
-        key = (n, bn)
+    def _order(self, n: int, bn: int, kind: int) -> torch.Tensor:
+        key = (n, bn, kind)
         if key not in self._orders:
-            ids = ag_tile_order(self.m, n, self.world, self.rank, bn)
+            tile_n = 2 * bn if kind == 2 else bn
+            ids = ag_tile_order(self.m, n, self.world, self.rank, tile_n, 256 if kind else 128)
             self._orders[key] = torch.tensor(ids, dtype=torch.int32, device=self.device)
         return self._orders[key]
 
+    def tile_kind(self, n: int, bn: int) -> int:
+        """0 single CTA 128 x bn, 2 wide CTA pair 256 x 512 (wave model, cached)."""
+        key = ("kind", n, bn)
+        if key not in self._orders:
+            kind = 0
+            if self._kind is not None:
+                kind = self._kind if bn == 256 else 0
+            elif bn == 256 and self.device.type == "cuda" and (self.m // self.world) % 256 == 0:
+                kind = int(lib().fused_tile_kind(self.m, n, self.k, self.comm_ctas))
+            self._orders[key] = kind
+        return self._orders[key]
+
     def targets(self, epoch: int) -> dict:
-        """Counter targets of call `epoch` (1-based): gatherer CTAs done with the
-        own chunk, peers' finished readers of the previous call, arrived pieces
-        per block."""
-        return dict(own_target=self.comm_ctas * epoch,
-                    pulled_target=(self.world - 1) * self.comm_ctas * (epoch - 1),
+        """Counter targets of call `epoch` (1-based): the peers' gatherer CTAs
+        that finished reading the previous call's own chunk, and the arrived
+        pieces per block."""
+        return dict(pulled_target=(self.world - 1) * self.comm_ctas * (epoch - 1),
                     ready_target=self.pieces_per_block * epoch)
 
     def _check(self, shard, w, b_mn, bias, gelu_aux, gelu_grad_of, out):
@@ -172,13 +194,14 @@ class AGGemm:
             epoch = self.calls + 1 if phase & 1 else self.calls
             try:
                 t = self.targets(epoch)
+                kind = self.tile_kind(n, bn)
                 with tracing.scope("ag_gemm"):
                     lib().ag_gemm(shard.contiguous(), self.gathered, w, b_mn, out, epi, bias, aux,
                                   self.gather.ptrs.data_ptr(), self._published_ptrs.data_ptr(),
-                                  self._pulled_ptrs.data_ptr(), self.ctrl.local, self.ready, self.own_done,
-                                  self.rank, self.world, epoch, t["own_target"], t["pulled_target"],
-                                  t["ready_target"], self._order(n, bn), self.status, self.timeout_ns, bn,
-                                  self.comm_ctas, phase, *(_stamps or (None, None)))
+                                  self._pulled_ptrs.data_ptr(), self.ctrl.local,
+                                  self.ctrl.local + self.pulled_offset, self.ready, self.rank, self.world, epoch,
+                                  t["pulled_target"], t["ready_target"], self._order(n, bn, kind), self.status,
+                                  self.timeout_ns, bn, self.comm_ctas, phase, *(_stamps or (None, None)), kind)
             except BaseException:
                 self.failed = True
                 raise
@@ -194,7 +217,7 @@ class AGGemm:
         (blocks arriving after the GEMM CTAs became free) or the reverse."""
         n = w.shape[1] if kw.get("b_mn") else w.shape[0]
         bn = kw.get("bn", 0) or (256 if n >= 256 and (self.m // 128) * ((n + 255) // 256) >= 148 else 128)
-        grid = lib().fused_grid(self.m, n, self.k, 0, 1, bn, self.comm_ctas, 7)
+        grid = lib().fused_grid(self.m, n, self.k, 0, 1, bn, self.comm_ctas, 7, self.tile_kind(n, bn))
         ctas = torch.zeros(2 * grid, dtype=torch.int64, device=self.device)
         blocks = torch.zeros(self.world * self.blocks, dtype=torch.int64, device=self.device)
         out = self.forward(shard, w, _stamps=(ctas, blocks), **kw)

@@ -126,7 +126,7 @@ class GemmRS:
                  plan=None, transport: str = "nvlink", timeout_ns: int = DEFAULT_TIMEOUT_NS,
                  b_mn: bool = False, workspace: RSWorkspace | None = None,
                  _emulate: tuple | None = None, device: torch.device | None = None,
-                 pull: bool | None = None, comm_ctas: int | None = None):
+                 pull: bool | None = None, comm_ctas: int | None = None, tile_kind: int | None = None):
         if arm not in mapping.ARMS:
             raise ValueError(f"unknown arm {arm}")
         if transport not in ("nvlink", "nccl"):
@@ -156,10 +156,23 @@ class GemmRS:
         # `device` defaults to the current CUDA device; CPU is for host-logic tests
         # (NCCL transport on Gloo ranks, or a recording stand-in for the kernels).
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        # GEMM tile kind of the pull transport: 0 single CTA 128 x 256, 2 wide CTA
+        # pair 256 x 512 (flags stay per 128-row slice of a tile).
+        if not self.pull:
+            self.tile_kind = 0
+        elif tile_kind is None:
+            self.tile_kind = 0 if self.device.type != "cuda" else int(lib().fused_tile_kind(m, n, k, self.comm_ctas))
+        else:
+            self.tile_kind = int(tile_kind)
+        if self.tile_kind not in (0, 2) or (self.tile_kind and (self.rows % 256 or n % 512)):
+            raise ValueError(f"tile kind {self.tile_kind} does not fit rows {self.rows} / N {n}")
+        self.tile_m = 256 if self.tile_kind else 128
+        self.tile_n = 512 if self.tile_kind == 2 else TILE_N
         self.order = mapping.schedule(m, n, k, self.world, chunk_rows, arm, plan)
         ids = self.production_ids(self.rank)
         self.tile_order = torch.tensor(ids, dtype=torch.int32, device=self.device)
-        local = mapping.consumer_tile_order(m, n, k, self.world, chunk_rows, arm, self.rank, plan, TILE_N)
+        local = mapping.pull_consumer_ids(m, n, k, self.world, chunk_rows, arm, self.rank, plan, self.tile_n,
+                                          self.tile_m)
         self.consumer_order = torch.tensor(local, dtype=torch.int32, device=self.device)
         self.tiles_per_dest = (self.rows // 128) * (n // TILE_N)
         self.slot_bytes = self.rows * n * 2
@@ -193,7 +206,7 @@ class GemmRS:
         CTA map."""
         if self.pull:
             return mapping.pull_production_ids(self.m, self.n, self.k, self.world, self.chunk_rows, self.arm,
-                                               rank, self.plan, tile_n=TILE_N)
+                                               rank, self.plan, tile_n=self.tile_n, tile_m=self.tile_m)
         shift = rank + 1 if self.transport == "nvlink" else 0
         return mapping.linear_tile_ids(self.m, self.n, self.k, self.world, self.chunk_rows, self.arm, self.plan,
                                        tile_n=TILE_N, shift=shift)
@@ -281,7 +294,8 @@ class GemmRS:
         lib().gemm_rs_pull(x, False, w, b_mn, part.local, part.ptrs.data_ptr(), self.flags.ptrs.data_ptr(),
                            self.flags.local, self.rank, self.world, self.epoch, self.tile_order,
                            self.consumer_order, out, residual, bias, self.status, self.timeout_ns,
-                           self.comm_ctas, phase, stamps, produced, delay_tile, delay_ns, 0, cta_stamps)
+                           self.comm_ctas, phase, stamps, produced, delay_tile, delay_ns, 0, cta_stamps,
+                           self.tile_kind)
         count_launch()
 
     def push(self, x, w, b_mn: bool | None = None, delay_tile: int = -1, delay_ns: int = 0):
@@ -335,9 +349,10 @@ class GemmRS:
         if self.failed or ws.failed:
             raise RuntimeError("this GemmRS operator (or one sharing its receive workspace) previously failed")
         out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device)
-        stamps = torch.zeros(self.tiles_per_dest, dtype=torch.int64, device=self.device)
-        produced = torch.zeros((self.m // 128) * (self.n // TILE_N), dtype=torch.int64, device=self.device)
-        grid = lib().fused_grid(self.m, self.n, self.k, 3, 0, 256, self.comm_ctas, 6)
+        flag_tiles = (self.rows // 128) * (self.n // self.tile_n)
+        stamps = torch.zeros(flag_tiles, dtype=torch.int64, device=self.device)
+        produced = torch.zeros((self.m // 128) * (self.n // self.tile_n), dtype=torch.int64, device=self.device)
+        grid = lib().fused_grid(self.m, self.n, self.k, 3, 0, 256, self.comm_ctas, 6, self.tile_kind)
         ctas = torch.zeros(2 * grid, dtype=torch.int64, device=self.device)
         with ws.lock:
             try:
@@ -373,7 +388,7 @@ class GemmRS:
         if self.failed or ws.failed:
             raise RuntimeError("this GemmRS operator (or one sharing its receive workspace) previously failed")
         out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device)
-        stamps = torch.zeros(self.tiles_per_dest, dtype=torch.int64, device=self.device)
+        stamps = torch.zeros((self.rows // 128) * (self.n // self.tile_n), dtype=torch.int64, device=self.device)
         with ws.lock:
             try:
                 delayed_local = self._profiled_call(x, w, out, stamps, delay_ns, delay_rank)
@@ -392,15 +407,17 @@ class GemmRS:
         if delay_ns:
             # Every rank identifies the same tile: the first lane-0 tile of
             # `delay_rank`'s own production order (orders differ per rank).
-            tiles_n = self.n // TILE_N
-            per_dest_m = self.rows // 128
+            # Local ids count flag tiles (128 rows x tile_n of the owner's rows).
+            tiles_n = self.n // self.tile_n
+            per_dest_m = self.rows // self.tile_m
             for tid in self.production_ids(delay_rank):
                 tm = tid // tiles_n
-                block = (tm * 128 % self.rows) // self.chunk_rows
+                block = (tm * self.tile_m % self.rows) // self.chunk_rows
                 if block % 2 == 0:
                     delay_tile = tid
                     dest = tm // per_dest_m
-                    delayed_local = (dest, (tm - dest * per_dest_m) * tiles_n + tid % tiles_n)
+                    first_row = (tm - dest * per_dest_m) * self.tile_m
+                    delayed_local = (dest, (first_row // 128) * tiles_n + tid % tiles_n)
                     break
         mine = self.rank == delay_rank
         if self.pull:
@@ -453,7 +470,8 @@ class GemmRS:
         return dict(backend=mapping.BACKEND, transport=self.transport, arm=self.arm, rank=self.rank,
                     world=self.world, calls=self.calls, epoch=self.epoch,
                     shape=[self.m, self.n, self.k], chunk_rows=self.chunk_rows,
-                    production_schedule=self.order, tile_n=TILE_N,
+                    production_schedule=self.order, tile_n=self.tile_n, tile_m=self.tile_m,
+                    pull_transport=self.pull, comm_ctas=self.comm_ctas if self.pull else 0,
                     push_destination_rotation=(self.rank + 1) % self.world if self.transport == "nvlink" else 0,
                     quantization="all_remote_h128_e4m3" if self.quantized else "none",
                     remote_wire_bytes_per_source=mapping.wire_bytes(self.m, self.n, self.world, self.quantized),

@@ -123,20 +123,50 @@ def destination_tile_ids(m, n, k, world, chunk_rows, arm, plan=None, tile_n=256)
     return lists
 
 
-def pull_production_ids(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n=256):
+def pull_production_ids(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n=256, tile_m=TILE_M):
     """Production order of the pull transport on `rank`: the arm's
     per-destination tile sequences interleaved across destinations one tile at
     a time, starting with destination rank+1 and ending each round with the
     rank's own rows.  A pulled tile can be reduced only when every source has
     produced it, so every source advances through every destination's tiles at
     the same pace (balanced all-to-all traffic, reduction overlapping the GEMM);
-    the within-destination order is the arm's."""
-    lists = destination_tile_ids(m, n, k, world, chunk_rows, arm, plan, tile_n)
+    the within-destination order is the arm's.  With CTA-pair tiles
+    (tile_m = 256) ids count 256-row tiles; the BF16 arm's destination-major
+    order is row-major inside each destination."""
+    if tile_m == TILE_M:
+        lists = destination_tile_ids(m, n, k, world, chunk_rows, arm, plan, tile_n)
+    else:
+        if arm != "flux":
+            raise ValueError("CTA-pair tiles serve the BF16 arm's pull transport")
+        per_dest, cols = m // world // tile_m, n // tile_n
+        lists = [[(d * per_dest + i) * cols + j for i in range(per_dest) for j in range(cols)]
+                 for d in range(world)]
     out = []
     for i in range(len(lists[0])):
         for j in range(world):
             out.append(lists[(rank + 1 + j) % world][i])
     return out
+
+
+def pull_consumer_ids(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n=256, tile_m=TILE_M):
+    """Flag tiles (128 rows x tile_n of `rank`'s rows, local ids) in the order
+    `rank`'s tiles are produced: each producer tile covers tile_m / 128 of them."""
+    if tile_m == TILE_M:
+        return consumer_tile_order(m, n, k, world, chunk_rows, arm, rank, plan, tile_n)
+    rows, cols = m // world, n // tile_n
+    halves = tile_m // TILE_M
+    out = []
+    for tid in destination_tile_ids_pairs(m, n, world, rank, tile_n, tile_m):
+        tm, tn = tid // cols, tid % cols
+        for h in range(halves):
+            out.append(((tm * tile_m - rank * rows) // TILE_M + h) * cols + tn)
+    return out
+
+
+def destination_tile_ids_pairs(m, n, world, dest, tile_n, tile_m):
+    """Row-major tiles (global ids in tile_m x tile_n units) of one destination."""
+    per_dest, cols = m // world // tile_m, n // tile_n
+    return [(dest * per_dest + i) * cols + j for i in range(per_dest) for j in range(cols)]
 
 
 def consumer_tile_order(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n=256):

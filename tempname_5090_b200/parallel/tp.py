@@ -8,6 +8,10 @@
 
 On CUDA with W > 1 the two linears are the fused NVLink kernels (AGGemm,
 GemmRS).  With W = 1 they are local tcgen05 GEMMs with the same epilogues.
+Transport `nccl_plain` is the unfused control: the same tcgen05 GEMMs with a
+plain NCCL all_gather_into_tensor before / reduce_scatter_tensor after them
+(NCCL's own reduction order, residual and bias added afterwards) -- the
+"library collectives around our GEMMs" step the fused operators must beat.
 On CPU tensors (gloo process groups, unit tests) they are written with
 torch.distributed collectives and the reference arithmetic, including the
 ordered "round to BF16 after every source" reduction, so a CPU run of the
@@ -86,6 +90,10 @@ class TensorParallel:
             y = G.matmul(shard, weight, b_t=b_mn, bias=bias, gelu_aux=gelu_aux,
                          gelu_grad_of=gelu_grad_of, out=out)
             return y, shard
+        if shard.is_cuda and self.transport == "nccl_plain":
+            full = self.gather_rows(shard)
+            y = G.matmul(full, weight, b_t=b_mn, bias=bias, gelu_aux=gelu_aux, gelu_grad_of=gelu_grad_of, out=out)
+            return y, full
         if shard.is_cuda:
             op = self.ag_operator(site, shard.shape[0] * self.world, shard.shape[1])
             y = op.forward(shard, weight, b_mn=b_mn, bias=bias, gelu_aux=gelu_aux,
@@ -117,6 +125,20 @@ class TensorParallel:
             return G.matmul(full, weight, b_t=b_mn, residual=residual, bias=bias, out=out)
         M = full.shape[0]
         N = weight.shape[1] if b_mn else weight.shape[0]
+        if full.is_cuda and self.transport == "nccl_plain":
+            partial = G.matmul(full, weight, b_t=b_mn)
+            y = self.scatter_sum(partial)
+            if residual is not None or bias is not None:
+                z = y.float()
+                if residual is not None:
+                    z = (residual.float() + z).to(torch.bfloat16).float()
+                if bias is not None:
+                    z = z + bias.float()
+                y = z.to(torch.bfloat16)
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
         if full.is_cuda:
             op = self.rs_operator(M, N, full.shape[1], role)
             return op.forward(full, weight, b_mn=b_mn, residual=residual, bias=bias, out=out)

@@ -90,7 +90,7 @@ class Timer:
 
 
 def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True, chunk_rows=128,
-                comm_sweep=(None,)):
+                comm_sweep=(None,), kind_sweep=(None,)):
     import torch
     import torch.distributed as dist
     from ..parallel.gemm_rs import GemmRS
@@ -107,10 +107,11 @@ def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True
         if arm.endswith("arrival"):
             plan = planning.make_role(m, n, k, world, chunk_rows)
         for transport in transports:
-            sweep = comm_sweep if (transport == "nvlink" and arm == "flux") else (None,)
-            for comm in sweep:
+            pull = transport == "nvlink" and arm == "flux"
+            sweep = [(c, kind) for c in comm_sweep for kind in kind_sweep] if pull else [(None, None)]
+            for comm, kind in sweep:
                 op = GemmRS(m, n, k, arm=arm, chunk_rows=chunk_rows, plan=plan, transport=transport,
-                            comm_ctas=comm)
+                            comm_ctas=comm, tile_kind=kind)
                 us = timer.run(lambda: op.forward(x, w))
                 wire = (world - 1) * (m // world) * n * (136 / 128 if arm != "flux" else 2.0)
                 roof = max(flops / (pk["bf16_tflops"] * 1e12), wire / (pk["nvlink_gbs"] * 1e9)) * 1e6
@@ -120,6 +121,7 @@ def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True
                 row["back_to_back_us"] = timer.back_to_back(lambda: op.forward(x, w))
                 if op.pull:
                     row["comm_ctas"] = op.comm_ctas
+                    row["tile_kind"] = op.tile_kind
                     prof = op.stage_profile(x, w)
                     row["stage"] = {key: prof[key] for key in ("producer_last_ns", "consumer_first_ns",
                                                                 "consumer_last_ns", "consumer_tiles",
@@ -364,6 +366,7 @@ def main(argv=None):
     ap.add_argument("--arms", default="all")
     ap.add_argument("--transports", default="nvlink,nccl")
     ap.add_argument("--comm-ctas", default="", help="gemmrs: comma list of reducer CTA counts (pull transport)")
+    ap.add_argument("--tile-kinds", default="", help="gemmrs: comma list of pull GEMM tile kinds (0 single, 2 wide)")
     ap.add_argument("--out", type=Path)
     args = ap.parse_args(argv)
     import torch
@@ -381,7 +384,9 @@ def main(argv=None):
     rows = []
     comm_sweep = tuple(int(c) for c in args.comm_ctas.split(",")) if args.comm_ctas else (None,)
     if args.op == "gemmrs":
-        rows += gemmrs_case(args.m, args.n, args.k, rank, world, timer, arms, transports, comm_sweep=comm_sweep)
+        kinds = tuple(int(c) for c in args.tile_kinds.split(",")) if args.tile_kinds else (None,)
+        rows += gemmrs_case(args.m, args.n, args.k, rank, world, timer, arms, transports, comm_sweep=comm_sweep,
+                            kind_sweep=kinds)
     elif args.op == "gemm":
         rows += gemm_case(GEMM_SHAPES, timer)
     elif args.op == "gemm_once":

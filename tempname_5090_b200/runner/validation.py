@@ -108,3 +108,66 @@ def projection_reference(x, w, rank: int, world: int, group, quantized: bool):
             contrib = taco.decode_cpu(taco.encode_cpu(contrib), contrib.numel()).reshape(contrib.shape)
         indep = (indep + contrib.float()).to(torch.bfloat16).float()
     return plain.to(torch.bfloat16), indep.to(torch.bfloat16)
+
+
+def fused_operator_check(m: int, hidden: int, ffn: int, group=None, seed: int = 11) -> dict:
+    """Untimed bitwise check of the fused NVLink operators at a layer's shapes,
+    MIN-reduced over ranks (every rank reports the same verdict):
+
+    * AG->GEMM (FC1 shape: gather [M/W, h] shards, times W_fc1 [f/W, h]^T) against
+      NCCL all_gather_into_tensor + this framework's GEMM of the same tile kind;
+    * GemmRS (attention out-projection: [M, h/W] x [h, h/W]^T, residual + bias)
+      against a dense all_to_all of the partials + the ordered BF16 reduction.
+    """
+    import torch
+    import torch.distributed as dist
+    from ..ops import gemm as G
+    from ..ops import taco
+    from ..parallel.ag_gemm import AGGemm
+    from ..parallel.gemm_rs import GemmRS
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    rows = m // world
+    g = torch.Generator(device="cuda").manual_seed(seed + 131 * rank)
+    result = dict(world=world, ag_shape=[m, hidden, ffn // world], rs_shape=[m, hidden, hidden // world])
+    # AG -> GEMM
+    shard = torch.randn((rows, hidden), generator=g, device="cuda").to(torch.bfloat16)
+    w1 = (0.02 * torch.randn((ffn // world, hidden), generator=g, device="cuda")).to(torch.bfloat16)
+    ag = AGGemm(m, hidden, group)
+    try:
+        got = ag.forward(shard, w1)
+        full = torch.empty((m, hidden), dtype=torch.bfloat16, device="cuda")
+        dist.all_gather_into_tensor(full, shard, group=group)
+        kind = ag.tile_kind(ffn // world, 256)
+        want = G.matmul(full, w1, bn=256, pair=kind)
+        torch.cuda.synchronize()
+        ag_ok = bool(torch.equal(ag.gathered, full)) and bool(torch.equal(got, want))
+        result["ag_tile_kind"] = kind
+    finally:
+        ag.close()
+    # GEMM -> RS with residual + bias
+    k = hidden // world
+    x = torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16)
+    w2 = (0.02 * torch.randn((hidden, k), generator=g, device="cuda")).to(torch.bfloat16)
+    res = torch.randn((rows, hidden), generator=g, device="cuda").to(torch.bfloat16)
+    bias = torch.randn((hidden,), generator=g, device="cuda").to(torch.bfloat16)
+    rs = GemmRS(m, hidden, k, group)
+    try:
+        got = rs.forward(x, w2, residual=res, bias=bias)
+        partial = G.matmul(x, w2, bn=256, pair=rs.tile_kind)
+        sources = torch.empty_like(partial)
+        dist.all_to_all_single(sources, partial, group=group)
+        sources = sources.view(world, rows, hidden)
+        remote = torch.cat([sources[s] for s in range(world) if s != rank])
+        y = taco.ordered_reduce(sources[rank].contiguous(), remote, rank, world)
+        want = ((res.float() + y.float()).to(torch.bfloat16).float() + bias.float()).to(torch.bfloat16)
+        torch.cuda.synchronize()
+        rs_ok = bool(torch.equal(got, want))
+        result["rs_tile_kind"] = rs.tile_kind
+        result["rs_transport"] = "nvlink-pull" if rs.pull else "nvlink-push"
+    finally:
+        rs.close()
+    flags = torch.tensor([int(ag_ok), int(rs_ok)], dtype=torch.int32, device="cuda")
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN, group=group)
+    result["ag_bitwise_all_ranks"] = bool(flags[0].item())
+    result["rs_bitwise_all_ranks"] = bool(flags[1].item())
+    return result

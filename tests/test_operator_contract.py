@@ -46,7 +46,7 @@ class _FakeLib:
 
     def gemm_rs_pull(self, x, a_mn, w, b_mn, partial_local, partial_ptrs, flag_ptrs, my_flags, rank, world, epoch,
                      tile_order, consumer_order, out, residual, bias, status, timeout_ns, comm_ctas, phase, stamps,
-                     produced, delay_tile, delay_ns, max_ctas, cta_stamps):
+                     produced, delay_tile, delay_ns, max_ctas, cta_stamps, pair):
         if self.fail_push:
             raise RuntimeError("injected launch failure")
         self.calls.append(("pull", dict(partial=partial_local, partials=partial_ptrs, flags=flag_ptrs,
@@ -196,12 +196,13 @@ class _FakeAGLib:
         self.calls = []
 
     def ag_gemm(self, shard, gather, w, b_mn, out, epi, bias, aux, gather_ptrs, published_ptrs, pulled_ptrs,
-                ctrl_local, ready, own_done, rank, world, epoch, own_target, pulled_target, ready_target,
-                tile_order, status, timeout_ns, bn, comm_ctas, phase, cta_stamps, block_stamps):
-        self.calls.append(dict(epi=epi, rank=rank, world=world, epoch=epoch, own=own_target,
+                published_local, pulled_local, ready, rank, world, epoch, pulled_target, ready_target,
+                tile_order, status, timeout_ns, bn, comm_ctas, phase, cta_stamps, block_stamps, pair):
+        self.calls.append(dict(epi=epi, rank=rank, world=world, epoch=epoch,
                                pulled=pulled_target, ready=ready_target, order=tile_order.tolist(),
-                               bn=bn, b_mn=b_mn, aux=aux is not None, bias=bias is not None, ctrl=ctrl_local,
-                               gather_ptrs=gather_ptrs, comm_ctas=comm_ctas, phase=phase))
+                               bn=bn, b_mn=b_mn, aux=aux is not None, bias=bias is not None, ctrl=published_local,
+                               pulled_local=pulled_local, gather_ptrs=gather_ptrs, comm_ctas=comm_ctas,
+                               phase=phase))
 
 
 class _AGBuf(_Buf):
@@ -231,12 +232,14 @@ def test_ag_gemm_launch_contract(monkeypatch, rank, world):
     op.forward(shard, w, gelu_aux=aux)
     op.forward(shard, w.t().contiguous(), b_mn=True, gelu_grad_of=aux)
     c = fake.calls
-    # One launch per call; cumulative counter targets: 7 gatherer CTAs per call on
-    # every rank, (W-1) * 7 finished readers per previous call, 4 pieces (16 KB)
-    # per 128-row block of K=256 per call.
+    # One launch per call; cumulative counter targets: (W-1) peers x 7 gatherer
+    # CTAs finished reading per previous call, 4 pieces (16 KB) per 128-row
+    # block of K=256 per call.
     assert [x["epoch"] for x in c] == [1, 2, 3] and all(x["phase"] == 7 for x in c)
-    assert [x["own"] for x in c] == [7, 14, 21]
     assert [x["pulled"] for x in c] == [0, 7 * (world - 1), 14 * (world - 1)]
+    pulled_offset, _ = ag_gemm.control_layout(m)
+    assert pulled_offset % 256 == 0 and pulled_offset >= 4 * m // 128
+    assert all(x["pulled_local"] == ctrl.local + pulled_offset for x in c)
     assert op.pieces_per_block == 4 and [x["ready"] for x in c] == [4, 8, 12]
     assert [x["epi"] for x in c] == [G.EPI_BIAS, G.EPI_GELU, G.EPI_GELU_BWD]
     assert [x["aux"] for x in c] == [False, True, True] and [x["b_mn"] for x in c] == [False, False, True]
