@@ -216,8 +216,9 @@ void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor
     c.bias = bias->data_ptr();
   }
   if (aux) { check_bf16(*aux, "aux"); check_rows(*aux, "aux"); c.aux = aux->data_ptr(); c.ld_aux = aux->stride(0); }
-  TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == at::kInt && ready.numel() >= world * (c.M / world / 128),
-              "ag_gemm: ready must be int32 [world * blocks]");
+  TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == at::kInt &&
+                  ready.numel() >= world * (c.M / world / 128) * tn5b::gemm::kReadyStride,
+              "ag_gemm: ready must be int32 [world * blocks * ", tn5b::gemm::kReadyStride, "]");
   c.ag = 1;
   c.rank = int(rank); c.world = int(world);
   c.ag_shard = shard.data_ptr();
@@ -266,6 +267,25 @@ int64_t fused_tile_kind(int64_t M, int64_t N, int64_t K, int64_t comm_ctas) {
   return tn5b::gemm::fused_tile_kind(int(M), int(N), int(K), int(comm_ctas));
 }
 
+// Mapping probe: the (tile_m, tile_n) pairs the GEMM kernel's CTAs decode for
+// each linear tile index of a call of this shape, tile kind and tile order.
+at::Tensor gemm_tile_map(int64_t M, int64_t N, int64_t K, int64_t mode, int64_t pair,
+                         const c10::optional<at::Tensor>& tile_order, int64_t device) {
+  const c10::cuda::CUDAGuard guard(c10::Device(c10::kCUDA, int(device)));
+  tn5b::gemm::GemmCall c;
+  c.M = int(M); c.N = int(N); c.K = int(K); c.mode = int(mode); c.pair = int(pair);
+  if (tile_order) {
+    check_cuda(*tile_order, "tile_order");
+    TORCH_CHECK(tile_order->scalar_type() == at::kInt);
+    c.tile_order = tile_order->data_ptr<int>();
+    TORCH_CHECK(tile_order->numel() == tn5b::gemm::tile_count(c), "tile_order length differs from the tile count");
+  }
+  auto out = at::empty({int64_t(tn5b::gemm::tile_count(c)), 2},
+                       at::TensorOptions().dtype(at::kInt).device(at::kCUDA, int(device)));
+  raise_if(tn5b::gemm::tile_map(c, out.data_ptr<int>(), stream()), "gemm_tile_map");
+  return out;
+}
+
 // Number of SMs of the current device.
 int64_t sm_count() {
   int dev = 0, n = 0;
@@ -289,6 +309,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sm_count", &sm_count, "number of SMs of the current device");
   m.def("fused_grid", &fused_grid, "grid of a fused GEMM launch (GEMM + communication CTAs)");
   m.def("fused_tile_kind", &fused_tile_kind, "tile kind the wave model picks for a fused launch");
+  m.def("gemm_tile_map", &gemm_tile_map, "device read-back of the GEMM tile order (mapping probe)");
   register_kernels(m);
   register_comm(m);
 }

@@ -326,6 +326,9 @@ __device__ __forceinline__ uint32_t smid() {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -350,6 +353,28 @@ __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t tar
       }
       __nanosleep(64);
     }
+  }
+}
+
+// Bounded wait on a counter written by other CTAs of THIS GPU (GPU-scope
+// acquire), polling with exponential backoff (64 ns .. 1 us) so that many
+// waiters do not saturate the cache line their producers update.
+__device__ __forceinline__ bool wait_flag_geq_gpu(const uint32_t* flag, uint32_t target, uint64_t timeout_ns,
+                                                  int* status, int code) {
+  uint64_t start = 0;
+  uint32_t backoff = 64;
+  for (uint32_t it = 0;; ++it) {
+    if (int32_t(ld_acquire_gpu(flag) - target) >= 0) return true;
+    if (status && *(volatile int*)status) return false;  // someone else already failed
+    const uint64_t now = globaltimer_ns();
+    if (start == 0) {
+      start = now;
+    } else if (now - start > timeout_ns) {
+      record_status(status, code);
+      return false;
+    }
+    __nanosleep(backoff);
+    if (backoff < 1024) backoff *= 2;
   }
 }
 

@@ -15,9 +15,9 @@
 //                own chunk of its gather buffer and publishes every 128-row
 //                block to every peer as soon as the block is complete; every
 //                rank pulls the peers' published blocks (bulk loads from the
-//                peers' memory) into its local gather buffer and counts the
-//                arrived 16 KB pieces per block; the GEMM CTAs wait for a
-//                block's count before their TMA loads read it (local memory).
+//                peers' memory) into its local gather buffer and flags each
+//                block (epoch) once it is stored; the GEMM CTAs wait for a
+//                block's flag before their TMA loads read it (local memory).
 //                After its last load from a peer a gatherer CTA adds 1 to that
 //                peer's `pulled` counter; a rank overwrites its own chunk only
 //                after every peer's CTAs have signalled for the previous call,
@@ -108,13 +108,22 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
 #pragma unroll
     for (int s = 0; s < kCommStages; ++s) last_parity[s] = -1;
     bool ok = true;
-    for (int i = cta; i < tiles && ok; i += ctas) {
+    // Work unit: one piece (128 rows x 64 columns of a flag tile), assigned
+    // round-robin over the consumption order, so the last tiles of the GEMM are
+    // spread over all reducer CTAs instead of one CTA per tile.
+    int waited_tile = -1;
+    uint32_t waited = 0;
+    for (int q = cta; q < tiles * TILE_CC && ok; q += ctas) {
+      const int i = q / TILE_CC, pc = q % TILE_CC;
       const int lt = a.order ? a.order[i] : i;
       const int ltm = lt / tiles_n, tn = lt % tiles_n;
-      uint32_t waited = 0;
-      for (int pr = 0; pr < TILE_RB && ok; ++pr) {
-        for (int pc = 0; pc < TILE_CC && ok; ++pc) {
-          const int64_t off = piece_offset(rb_base + ltm * TILE_RB + pr, tn * TILE_CC + pc, n_chunks);
+      if (i != waited_tile) {
+        waited_tile = i;
+        waited = 0;
+      }
+      {
+        {
+          const int64_t off = piece_offset(rb_base + ltm, tn * TILE_CC + pc, n_chunks);
           if (a.residual) {
             const int st = int(seq % kCommStages);
             const uint32_t ph = (seq / kCommStages) & 1u;
@@ -123,7 +132,7 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
               break;
             }
             mbar_arrive_expect_tx(&full[st], kPiece);
-            tma_load_2d(ring + st * kPiece, tres, &full[st], (tn * TILE_CC + pc) * 64, (ltm * TILE_RB + pr) * 128);
+            tma_load_2d(ring + st * kPiece, tres, &full[st], (tn * TILE_CC + pc) * 64, ltm * 128);
             last_parity[st] = int(ph);
             ++seq;
           }
@@ -164,11 +173,13 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
   const int rt = threadIdx.x - 64;  // 0..127
   const uint32_t zero = 0u;         // two +0.0 BF16 values
   uint32_t seq = 0;
-  for (int i = cta; i < tiles; i += ctas) {
+  for (int q = cta; q < tiles * TILE_CC; q += ctas) {
+    const int i = q / TILE_CC, pc = q % TILE_CC;
     const int lt = a.order ? a.order[i] : i;
     const int ltm = lt / tiles_n, tn = lt % tiles_n;
-    for (int pr = 0; pr < TILE_RB; ++pr) {
-      for (int pc = 0; pc < TILE_CC; ++pc) {
+    constexpr int pr = 0;
+    {
+      {
         // This thread's eight 16-byte units: unit rt + 128u is row rt/8 + 16u,
         // columns (rt % 8) * 8 .. +8 of the piece.  The residual tile arrives in
         // the ring first (swizzled: unit c of row r sits at c ^ (r & 7)); the
@@ -221,67 +232,92 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int64_t idx = int64_t(row0 + 16 * u) * p.N + col;
-          uint32_t* q = acc + 4 * u;
+          uint32_t* o = acc + 4 * u;
           if (a.residual) {
             const uint4 r = res[u];
-            q[0] = add_bf16x2(r.x, q[0]);
-            q[1] = add_bf16x2(r.y, q[1]);
-            q[2] = add_bf16x2(r.z, q[2]);
-            q[3] = add_bf16x2(r.w, q[3]);
+            o[0] = add_bf16x2(r.x, o[0]);
+            o[1] = add_bf16x2(r.y, o[1]);
+            o[2] = add_bf16x2(r.z, o[2]);
+            o[3] = add_bf16x2(r.w, o[3]);
           }
           if (a.bias) {
-            q[0] = add_bf16x2(q[0], bias4.x);
-            q[1] = add_bf16x2(q[1], bias4.y);
-            q[2] = add_bf16x2(q[2], bias4.z);
-            q[3] = add_bf16x2(q[3], bias4.w);
+            o[0] = add_bf16x2(o[0], bias4.x);
+            o[1] = add_bf16x2(o[1], bias4.y);
+            o[2] = add_bf16x2(o[2], bias4.z);
+            o[3] = add_bf16x2(o[3], bias4.w);
           }
-          *reinterpret_cast<uint4*>(a.out + idx) = make_uint4(q[0], q[1], q[2], q[3]);
+          *reinterpret_cast<uint4*>(a.out + idx) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
     }
     if (a.stamps) {
+      // A flag tile is complete when its last piece is: keep the latest piece time.
       named_barrier_sync(2, kRedWarps * 32);
-      if (rt == 0) a.stamps[lt] = globaltimer_ns();
+      if (rt == 0) atomicMax(a.stamps + lt, (unsigned long long)globaltimer_ns());
     }
   }
 }
 
 // --------------------------------------------------------------- gatherer
-// The single issuing thread streams a sequence of pieces (source address, local
-// destination) through the ring: up to kLoads loads are in flight, each landed
-// piece is bulk-stored to local memory.  Pieces travel in runs (consecutive
-// pieces of one 128-row block): synchronisation happens once per run, not per
-// piece -- when a run's last store has completed (confirmed kLag bulk groups
-// late, so the engine never waits for a write to land) the block's counter is
-// advanced by the run's length.  The ring keeps kCommStages - kLoads stages of
-// slack, so reusing a stage never waits for the store just issued to finish
-// reading shared memory.  A piece may carry a remote counter to bump (release,
-// system scope) once it has landed: the "no longer reading" signal to its source.
-struct PieceStream {
+// Each gatherer CTA moves whole 128-row blocks (own-chunk copies and peer
+// pulls), assigned round-robin over the sequence [own blocks, then every peer
+// block in pull order rank+1, rank+2, ...].  One thread streams a block's
+// 16 KB pieces through the ring (bulk load -> bulk store, up to kLoads loads in
+// flight, two stages of slack for stores still reading), exactly the copy loop
+// of the bulk-copy probe; synchronisation happens once per block: when the
+// block's last store is kLag bulk groups old, the thread waits for it, then
+// release-stores the block's epoch flag -- ready[c][b] (read by this GPU's
+// GEMM CTAs) for a peer block, published[d][rank][b] on every peer d for an
+// own block.  After the last piece this CTA loads from peer c has landed, it
+// adds 1 to c's `pulled` counter.
+struct BlockStream {
   static constexpr int kLoads = kCommStages - 2;
   static constexpr int kLag = 24;
+  static constexpr int kJobs = 8;    // blocks whose completion is pending
   uint8_t* ring;
   uint64_t* full;
   const Params* p;
-  uint32_t issued, stored;            // pieces loaded / stored
-  uint32_t* pending[kLag + 1];        // run counters to advance, by store index of the run's last piece
-  uint32_t pending_n[kLag + 1];
+  uint32_t issued, stored;
   int last_parity[kCommStages];
   uint8_t* q_dst[kCommStages];
-  uint32_t* q_ctr[kCommStages];       // set on a run's last piece
-  uint32_t q_n[kCommStages];          // that run's length
   uint32_t* q_landed[kCommStages];
   uint32_t q_bytes[kCommStages];
+  int q_job[kCommStages];            // block (chunk * blocks + b) finished by this piece, or -1
+  int jobs[kJobs];                   // pending blocks, by completion store index
+  uint32_t job_store[kJobs];
+  int job_head, job_tail;
 
   __device__ void init(uint8_t* r, uint64_t* f, const Params* params) {
     ring = r;
     full = f;
     p = params;
     issued = stored = 0;
+    job_head = job_tail = 0;
     for (int s = 0; s < kCommStages; ++s) last_parity[s] = -1;
-    for (int j = 0; j <= kLag; ++j) pending[j] = nullptr;
   }
-  // Store the oldest landed piece.  Returns false on a timeout.
+  __device__ void finish_block(int blk) {
+    const GatherArgs& g = p->gather;
+    const int blocks = g.rows_per_src / 128;
+    fence_proxy_async_global();
+    if (blk / blocks == g.rank) {
+      // Own block complete in local memory: release it to every peer.
+      fence_acq_rel_sys();
+      for (int d = 0; d < g.world; ++d)
+        if (d != g.rank) st_release_sys(g.published[d] + blk, g.epoch);
+    } else {
+      st_release_gpu(g.ready + int64_t(blk) * kReadyStride, g.epoch);
+    }
+    if (g.block_stamps) g.block_stamps[blk] = globaltimer_ns();
+  }
+  // Publish every pending block whose last store is at least `lag` groups old.
+  template <int LAG>
+  __device__ void retire() {
+    while (job_head != job_tail && job_store[job_head % kJobs] + LAG < stored) {
+      bulk_wait_group<LAG>();
+      finish_block(jobs[job_head % kJobs]);
+      ++job_head;
+    }
+  }
   __device__ bool store_one() {
     const int st = int(stored % kCommStages);
     const uint32_t ph = (stored / kCommStages) & 1u;
@@ -289,76 +325,42 @@ struct PieceStream {
     if (q_landed[st]) red_release_sys_add(q_landed[st], 1u);
     bulk_store(q_dst[st], smem_u32(ring + st * kPiece), q_bytes[st]);
     bulk_commit_group();
-    const int slot = int(stored % (kLag + 1));
-    pending[slot] = q_ctr[st];
-    pending_n[slot] = q_n[st];
-    ++stored;
-    // The store issued kLag groups ago has completed: advance its run's counter.
-    const int done = int(stored % (kLag + 1));  // store index stored - 1 - kLag
-    if (pending[done]) {
-      bulk_wait_group<kLag>();
-      fence_proxy_async_global();
-      count(pending[done], pending_n[done]);
-      pending[done] = nullptr;
+    if (q_job[st] >= 0) {
+      jobs[job_tail % kJobs] = q_job[st];
+      job_store[job_tail % kJobs] = stored;
+      ++job_tail;
     }
+    ++stored;
+    retire<kLag>();
     return true;
   }
-  // Queue one piece (ctr/n on a run's last piece); stores the oldest piece first
-  // when kLoads are in flight.
-  __device__ bool push(const uint8_t* src, uint8_t* dst, uint32_t bytes, uint32_t* ctr, uint32_t n,
-                       uint32_t* landed) {
+  __device__ bool push(const uint8_t* src, uint8_t* dst, uint32_t bytes, int job, uint32_t* landed) {
     if (issued - stored == uint32_t(kLoads) && !store_one()) return false;
+    // A block completion may not be queued while kJobs are pending.
+    if (job >= 0 && job_tail - job_head >= kJobs - 1) {
+      while (stored < issued)
+        if (!store_one()) return false;
+      retire<0>();
+    }
     const int st = int(issued % kCommStages);
-    // The stage's previous piece (issued - kCommStages) was stored at least
-    // kCommStages - kLoads stores ago: all but the newest store have read their stage.
     if (issued >= uint32_t(kCommStages)) bulk_wait_group_read<kCommStages - kLoads - 1>();
     q_dst[st] = dst;
-    q_ctr[st] = ctr;
-    q_n[st] = n;
     q_landed[st] = landed;
     q_bytes[st] = bytes;
+    q_job[st] = job;
     mbar_arrive_expect_tx(&full[st], bytes);
     bulk_load(ring + st * kPiece, src, bytes, &full[st]);
     last_parity[st] = int((issued / kCommStages) & 1u);
     ++issued;
     return true;
   }
-  // Store everything queued and advance every counter.
   __device__ bool finish() {
     while (stored < issued)
       if (!store_one()) return false;
+    retire<0>();
     bulk_wait_group_all();
-    fence_proxy_async_global();
-    for (int j = 0; j <= kLag; ++j) {
-      if (pending[j]) count(pending[j], pending_n[j]);
-      pending[j] = nullptr;
-    }
     return true;
   }
-  // A run of n pieces of one block is stored.  The run that completes an
-  // own-chunk block publishes the block to every peer; with block stamps the
-  // completing run also records the time.
-  __device__ void count(uint32_t* ctr, uint32_t n) {
-    const GatherArgs& g = p->gather;
-    const int64_t idx = ctr - g.ready;
-    const int blocks = g.rows_per_src / 128;
-    const bool own = idx / blocks == g.rank;
-    if (!own && !g.block_stamps) {
-      red_release_gpu_add(ctr, n);
-      return;
-    }
-    if (atom_acq_rel_gpu_add(ctr, n) + n != g.ready_target) return;
-    if (g.block_stamps) g.block_stamps[idx] = globaltimer_ns();
-    if (own) {
-      // Every piece of own block idx % blocks is in local memory (acquired through
-      // the counter): release it to the peers at system scope.
-      fence_acq_rel_sys();
-      const int b = int(idx % blocks);
-      for (int d = 0; d < g.world; ++d)
-        if (d != g.rank) st_release_sys(g.published[d] + g.rank * blocks + b, g.epoch);
-    }
-  }
-  // Abort path: wait (bounded) for every load in flight, then for the stores.
   __device__ void drain() {
     for (int s = 0; s < kCommStages; ++s)
       if (last_parity[s] >= 0)
@@ -366,8 +368,6 @@ struct PieceStream {
     bulk_wait_group_all();
   }
 };
-
-constexpr int kRunPieces = 8;  // pieces per run (128 KB): one counter update per run
 
 __device__ void ag_gatherer(const Params& p, uint8_t* smem) {
   if (threadIdx.x != 0) return;
@@ -380,73 +380,59 @@ __device__ void ag_gatherer(const Params& p, uint8_t* smem) {
   const int ctas = p.comm_ctas;
   const int rank = g.rank, world = g.world;
   const int64_t block_bytes = int64_t(128) * g.K * 2;
-  const int pieces_per_block = int((block_bytes + kPiece - 1) / kPiece);
-  const int runs_per_block = (pieces_per_block + kRunPieces - 1) / kRunPieces;
+  const int pieces = int((block_bytes + kPiece - 1) / kPiece);
   const int blocks = g.rows_per_src / 128;
-  const int runs = runs_per_block * blocks;  // per chunk
   uint8_t* local = g.gather[rank];
-  PieceStream ps;
-  ps.init(ring, full, &p);
+  BlockStream bs;
+  bs.init(ring, full, &p);
   bool ok = true;
-  // Queue run r of a chunk (src / dst chunk bases); `landed` on its last piece.
-  auto queue_run = [&](const uint8_t* src, uint8_t* dst, int chunk, int r, uint32_t* landed) -> bool {
-    const int b = r / runs_per_block;
-    const int first = (r % runs_per_block) * kRunPieces;
-    const int n = min(kRunPieces, pieces_per_block - first);
-    uint32_t* ctr = g.ready + int64_t(chunk) * blocks + b;
-    for (int k = first; k < first + n; ++k) {
-      const int64_t off = b * block_bytes + int64_t(k) * kPiece;
-      const uint32_t bytes = uint32_t(min(int64_t(kPiece), block_bytes - int64_t(k) * kPiece));
-      const bool last = k == first + n - 1;
-      if (!ps.push(src + off, dst + off, bytes, last ? ctr : nullptr, last ? uint32_t(n) : 0u,
-                   last ? landed : nullptr))
-        return false;
+  // Stream one block (pieces in order); the last piece carries the block's
+  // completion and, if given, the landed signal to its source.
+  auto stream_block = [&](const uint8_t* src, uint8_t* dst, int job, uint32_t* landed) -> bool {
+    for (int k = 0; k < pieces; ++k) {
+      const int64_t off = int64_t(k) * kPiece;
+      const uint32_t bytes = uint32_t(min(int64_t(kPiece), block_bytes - off));
+      const bool last = k == pieces - 1;
+      if (!bs.push(src + off, dst + off, bytes, last ? job : -1, last ? landed : nullptr)) return false;
     }
     return true;
   };
-
+  // Job sequence: own blocks 0..blocks-1, then peer (rank+step) block b as job
+  // blocks + (step-1) * blocks + b; this CTA takes jobs cta, cta + ctas, ...
+  const int own_jobs = (g.phase & 1) ? blocks : 0;
+  const int total = own_jobs + ((g.phase & 2) ? (world - 1) * blocks : 0);
   if (g.phase & 1) {
-    // Own shard -> own chunk of the gather buffer, once every peer has finished
-    // reading this chunk's previous contents.  Each block is published to the
-    // peers as soon as its last run is stored (PieceStream::count).
+    // Own chunk: overwrite it only once every peer has finished reading the
+    // previous call's contents.
     if (!wait_flag_geq(g.pulled_local, g.pulled_target, p.timeout_ns, p.status, kTimeoutPeerFlag)) return;
     fence_proxy_async_global();
-    uint8_t* own = local + int64_t(rank) * g.chunk_bytes;
-    for (int r = cta; r < runs && ok; r += ctas) ok = queue_run(g.shard, own, rank, r, nullptr);
-    if (ok) ok = ps.finish();
-    if (!ok) {
-      ps.drain();
-      return;
-    }
   }
-  if (g.phase & 2) {
-    // Peers' chunks, rank+1 first (every rank reads a different peer at a
-    // time), each 128-row block once its owner has published it.
-    for (int step = 1; step < world && ok; ++step) {
-      const int c = (rank + step) % world;
-      const uint8_t* src = g.gather[c] + int64_t(c) * g.chunk_bytes;
-      uint8_t* dst = local + int64_t(c) * g.chunk_bytes;
-      int last = -1;  // this CTA's last run of chunk c
-      for (int r = cta; r < runs; r += ctas) last = r;
-      if (last < 0) red_release_sys_add(g.pulled[c], 1u);  // nothing to read from c
-      int waited = -1;
-      for (int r = cta; r < runs && ok; r += ctas) {
-        const int b = r / runs_per_block;
-        if (b != waited) {
-          if (!wait_flag_geq(g.published_local + c * blocks + b, g.epoch, p.timeout_ns, p.status,
-                             kTimeoutAgChunk)) {
-            ok = false;
-            break;
-          }
-          fence_proxy_async_global();
-          waited = b;
-        }
-        ok = queue_run(src, dst, c, r, r == last ? g.pulled[c] : nullptr);
-      }
+  // This CTA's last job per peer step (its `pulled` signal rides on that block).
+  int last_of_step[64];
+  for (int s = 0; s < world; ++s) last_of_step[s] = -1;
+  for (int j = cta; j < total; j += ctas)
+    if (j >= own_jobs) last_of_step[1 + (j - own_jobs) / blocks] = j;
+  if (g.phase & 2)
+    for (int step = 1; step < world; ++step)
+      if (last_of_step[step] < 0) red_release_sys_add(g.pulled[(rank + step) % world], 1u);  // reads nothing
+  for (int j = cta; j < total && ok; j += ctas) {
+    if (j < own_jobs) {
+      const int64_t off = int64_t(j) * block_bytes;
+      ok = stream_block(g.shard + off, local + int64_t(rank) * g.chunk_bytes + off, rank * blocks + j, nullptr);
+      continue;
     }
-    if (ok) ok = ps.finish();
-    if (!ok) ps.drain();
+    const int step = 1 + (j - own_jobs) / blocks, b = (j - own_jobs) % blocks;
+    const int c = (rank + step) % world;
+    if (!wait_flag_geq(g.published_local + c * blocks + b, g.epoch, p.timeout_ns, p.status, kTimeoutAgChunk)) {
+      ok = false;
+      break;
+    }
+    fence_proxy_async_global();
+    const int64_t off = int64_t(c) * g.chunk_bytes + int64_t(b) * block_bytes;
+    ok = stream_block(g.gather[c] + off, local + off, c * blocks + b, j == last_of_step[step] ? g.pulled[c] : nullptr);
   }
+  if (ok) ok = bs.finish();
+  if (!ok) bs.drain();
 }
 
 }  // namespace gemm

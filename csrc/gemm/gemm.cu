@@ -150,6 +150,44 @@ int pick_bn(const GemmCall& c) {
 
 std::string last_error() { return g_last_error; }
 
+namespace {
+// Reads the tile order back exactly as the GEMM kernel's CTAs see it
+// (tile_coords over the uploaded table or the grouped raster).
+__global__ void tile_map_kernel(const __grid_constant__ Params p, int* out) {
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < p.num_tiles; t += gridDim.x * blockDim.x) {
+    int tm, tn;
+    tile_coords(p, t, tm, tn);
+    out[2 * t] = tm;
+    out[2 * t + 1] = tn;
+  }
+}
+}  // namespace
+
+int tile_map(const GemmCall& c, int* out, cudaStream_t stream) {
+  if (c.M <= 0 || c.N <= 0 || !out) return fail("tile_map: bad args");
+  const int bn = pick_bn(c);
+  const int kind = tile_kind(c, bn);
+  const bool pair = kind != kSingle;
+  const int tile_n = kind == kWide ? 2 * bn : bn;
+  Params p{};
+  p.M = c.M; p.N = c.N; p.K = c.K;
+  p.tiles_m = (c.M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
+  p.tiles_n = (c.N + tile_n - 1) / tile_n;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = c.group_m > 0 ? c.group_m : 8;
+  p.tile_order = c.tile_order;
+  tile_map_kernel<<<(p.num_tiles + 255) / 256, 256, 0, stream>>>(p, out);
+  return int(cudaGetLastError());
+}
+
+int tile_count(const GemmCall& c) {
+  const int bn = pick_bn(c);
+  const int kind = tile_kind(c, bn);
+  const bool pair = kind != kSingle;
+  const int tile_n = kind == kWide ? 2 * bn : bn;
+  return ((c.M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM)) * ((c.N + tile_n - 1) / tile_n);
+}
+
 int fused_tile_kind(int M, int N, int K, int comm_ctas) {
   return auto_kind(M, N, K, double(sm_count() - comm_ctas));
 }

@@ -9,6 +9,9 @@
 namespace tn5b {
 namespace gemm {
 
+// AG->GEMM: u32 words between two per-block arrival counters (one 128-byte line each).
+constexpr int kReadyStride = 32;
+
 struct GemmCall {
   // Operands: A is [M,K] row-major (a_mn=0) or [K,M] row-major (a_mn=1);
   //           B is [N,K] row-major (b_mn=0) or [K,N] row-major (b_mn=1).
@@ -81,6 +84,10 @@ int gemm_ctas(const GemmCall& c);
 // Tile kind (0 single CTA 128x256, 2 wide CTA pair 256x512) the wave model picks
 // for a fused launch whose GEMM runs on all SMs but `comm_ctas`.
 int fused_tile_kind(int M, int N, int K, int comm_ctas);
+// Mapping probe: writes (tile_m, tile_n) of every linear tile index as the
+// kernel's CTAs decode them (explicit table or grouped raster) into out[2 * tiles].
+int tile_map(const GemmCall& c, int* out, cudaStream_t stream);
+int tile_count(const GemmCall& c);
 int run(const GemmCall& c, cudaStream_t stream);
 std::string last_error();
 

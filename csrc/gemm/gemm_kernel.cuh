@@ -31,6 +31,7 @@
 #include <cuda_fp8.h>
 #include <cstdint>
 #include "../common/ptx.cuh"
+#include "gemm_api.h"
 
 namespace tn5b {
 namespace gemm {
@@ -76,23 +77,25 @@ struct RsArgs {
 };
 
 // All-gather -> GEMM (pull): chunk c of the gathered A ([M/W rows, K] of rank
-// c) arrives in this rank's gather buffer in 16 KB pieces; ready[c][block]
-// counts the arrived pieces of each 128-row block (cumulative over calls).
+// c) arrives in this rank's gather buffer block by block (128 rows);
+// ready[c][block] is set to the call's epoch once the block is stored.
+// Counters sit kReadyStride words apart (one 128-byte line each, gemm_api.h),
+// so GEMM CTAs polling one block do not contend with gatherers updating another.
 struct GatherArgs {
   uint8_t* const* gather;          // device array [world]: every rank's gather buffer ([M, K] bf16)
   uint32_t* const* published;      // device array [world]: every rank's published[world][blocks] flags
   uint32_t* const* pulled;         // device array [world]: every rank's pulled counter
   const uint32_t* published_local; // this rank's published[world][blocks]
   const uint32_t* pulled_local;    // this rank's pulled counter
-  uint32_t* ready;                 // local [world][rows_per_src / 128] arrived-piece counters
+  uint32_t* ready;                 // local [world][rows_per_src / 128] counters, kReadyStride apart
   const uint8_t* shard;            // local shard [rows_per_src, K] bf16 (contiguous)
   int64_t chunk_bytes;             // rows_per_src * K * 2
   int rank, world, rows_per_src, K;
   uint32_t epoch;                  // this call's epoch (published block flags)
   uint32_t pulled_target;          // pulled value once every peer finished reading the previous call
-  uint32_t ready_target;           // ready[c][b] once block b of chunk c has fully arrived
+  uint32_t ready_target;           // ready[c][b] once block b of chunk c has arrived (the epoch)
   int phase;                       // communication CTAs: bit0 own chunk + publish, bit1 pull peers
-  unsigned long long* block_stamps; // optional [world * rows_per_src / 128]: when each block fully arrived
+  unsigned long long* block_stamps; // optional [world * rows_per_src / 128]: when each block was stored
 };
 
 // GEMM -> reduce-scatter (pull): the reducer CTAs' view.  Flags are per
@@ -417,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             const int blk = chunk * (p.gather.rows_per_src / 128) + in_chunk / 128;
             if (blk != waited_chunk) {
-              if (!wait_flag_geq(p.gather.ready + blk, p.gather.ready_target, p.timeout_ns, p.status,
-                                 kTimeoutAgChunk)) {
+              if (!wait_flag_geq_gpu(p.gather.ready + int64_t(blk) * kReadyStride, p.gather.ready_target,
+                                     p.timeout_ns, p.status, kTimeoutAgChunk)) {
                 *abort_flag = 1;
                 ok = false;
                 break;

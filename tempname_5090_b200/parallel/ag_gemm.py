@@ -9,10 +9,10 @@ ONE persistent launch per call with two kinds of CTAs:
   complete (a system-scope release of `published[rank][block] = epoch` on
   every peer), and pull every peer's published blocks (rank+1 first) from the
   peer's gather buffer with bulk loads -- no multicast -- into the local gather
-  buffer, counting the arrived 16 KB pieces of each block;
+  buffer, flagging each 128-row block with the call's epoch once it is stored;
 * the other CTAs run the tcgen05 GEMM: tiles of the own chunk first, read
   straight from the shard, then each peer chunk's tiles once their block count
-  is complete (bounded wait), with TMA loads of LOCAL memory only.
+  flag is set (bounded wait), with TMA loads of LOCAL memory only.
 
 Buffer reuse: peers only read this rank's own chunk; every gatherer CTA of a
 peer adds 1 to this rank's `pulled` counter after its last load from it, and
@@ -41,8 +41,11 @@ from .symmetric import SymmetricBuffer
 from ..utils import tracing
 
 DEFAULT_TIMEOUT_NS = 10_000_000_000
-DEFAULT_COMM_CTAS = int(os.environ.get("TN5B_AG_COMM_CTAS", "20"))
+# Gatherer CTAs: chosen per shape by parallel/tuning.py (needs the GEMM's N,
+# given at construction) unless TN5B_AG_COMM_CTAS fixes a count.
+DEFAULT_COMM_CTAS = int(os.environ.get("TN5B_AG_COMM_CTAS", "0"))
 PIECE_BYTES = 16384
+READY_STRIDE = 32         # u32 words between two block counters (one 128-byte line)
 
 
 def control_layout(m: int) -> tuple:
@@ -73,7 +76,7 @@ def ag_tile_order(m: int, n: int, world: int, rank: int, bn: int, tile_m: int = 
 class AGGemm:
     def __init__(self, m: int, k: int, group=None, timeout_ns: int = DEFAULT_TIMEOUT_NS,
                  comm_ctas: int | None = None, _emulate: tuple | None = None,
-                 device: torch.device | None = None, tile_kind: int | None = None):
+                 device: torch.device | None = None, tile_kind: int | None = None, n: int | None = None):
         if _emulate is not None:
             self.rank, self.world, self.gather, self.ctrl = _emulate
         else:
@@ -88,7 +91,10 @@ class AGGemm:
         if tile_kind not in (None, 0, 2) or (tile_kind == 2 and (m // self.world) % 256):
             raise ValueError("tile_kind is 0 (single CTA) or 2 (wide CTA pair, rows per rank % 256 == 0)")
         self._kind = tile_kind
-        self.comm_ctas = DEFAULT_COMM_CTAS if comm_ctas is None else int(comm_ctas)
+        if comm_ctas is None:
+            from .tuning import ag_gemm_comm_ctas
+            comm_ctas = DEFAULT_COMM_CTAS or (ag_gemm_comm_ctas(m, n, k, self.world) if n else 20)
+        self.comm_ctas = int(comm_ctas)
         if not 1 <= self.comm_ctas <= 64:
             raise ValueError("comm_ctas must be in [1, 64]")
         # `device` defaults to the current CUDA device; CPU serves host-logic tests.
@@ -100,7 +106,8 @@ class AGGemm:
             self.ctrl = SymmetricBuffer(ctrl_bytes, group)
         self.blocks = (m // self.world) // 128
         self.pieces_per_block = -(-(128 * k * 2) // PIECE_BYTES)
-        self.ready = torch.zeros(self.world * self.blocks, dtype=torch.int32, device=self.device)
+        # arrived-piece counter per (source, 128-row block), one 128-byte line each
+        self.ready = torch.zeros(self.world * self.blocks * READY_STRIDE, dtype=torch.int32, device=self.device)
         self._published_ptrs = torch.tensor([p for p in self.ctrl.peers], dtype=torch.int64, device=self.device)
         self._pulled_ptrs = torch.tensor([p + self.pulled_offset for p in self.ctrl.peers], dtype=torch.int64,
                                          device=self.device)
@@ -137,11 +144,10 @@ class AGGemm:
         return self._orders[key]
 
     def targets(self, epoch: int) -> dict:
-        """Counter targets of call `epoch` (1-based): the peers' gatherer CTAs
-        that finished reading the previous call's own chunk, and the arrived
-        pieces per block."""
-        return dict(pulled_target=(self.world - 1) * self.comm_ctas * (epoch - 1),
-                    ready_target=self.pieces_per_block * epoch)
+        """Targets of call `epoch` (1-based): the peers' gatherer CTAs that
+        finished reading the previous call's own chunk (cumulative counter),
+        and the per-block arrival flag (the epoch)."""
+        return dict(pulled_target=(self.world - 1) * self.comm_ctas * (epoch - 1), ready_target=epoch)
 
     def _check(self, shard, w, b_mn, bias, gelu_aux, gelu_grad_of, out):
         n = w.shape[1] if b_mn else w.shape[0]
@@ -168,12 +174,14 @@ class AGGemm:
                 _stamps: tuple | None = None) -> torch.Tensor:
         """One call (phase 7).  Single-GPU emulation of several ranks runs each
         call as three launches per rank -- phase 1 (own chunk), 2 (pull peers),
-        4 (GEMM) -- over all ranks in turn, so no launch waits on a later one."""
+        4 (GEMM) -- over all ranks in turn, so no launch waits on a later one.
+        Phase 3 then 4 runs the gather and the GEMM of one call as two launches
+        (to time them apart)."""
         if self.failed:
             raise RuntimeError("this AG->GEMM operator previously failed (its counters are out of step)")
         n = self._check(shard, w, b_mn, bias, gelu_aux, gelu_grad_of, out)
-        if phase not in (1, 2, 4, 7):
-            raise ValueError("phase must be 7 (one launch) or 1, 2, 4 (emulation)")
+        if phase not in (1, 2, 3, 4, 7):
+            raise ValueError("phase must be 7 (one launch), 1, 2, 4 (emulation) or 3 then 4 (gather, then GEMM)")
         out = torch.empty((self.m, n), dtype=torch.bfloat16, device=self.device) if out is None else out
         if bn == 0:
             bn = 256 if n >= 256 and (self.m // 128) * ((n + 255) // 256) >= 148 else 128

@@ -52,9 +52,9 @@ from ..utils import tracing
 
 TILE_N = 256
 DEFAULT_TIMEOUT_NS = 10_000_000_000
-# Reducer CTAs of the pull transport (the rest of the SMs run the GEMM); bulk
-# loads from a peer reach the NVLink ceiling with 16-24 CTAs on B200.
-DEFAULT_COMM_CTAS = int(os.environ.get("TN5B_COMM_CTAS", "20"))
+# Reducer CTAs of the pull transport (the rest of the SMs run the GEMM): chosen
+# per shape by parallel/tuning.py unless TN5B_COMM_CTAS fixes a count.
+DEFAULT_COMM_CTAS = int(os.environ.get("TN5B_COMM_CTAS", "0"))
 
 
 class _Lanes:
@@ -149,7 +149,10 @@ class GemmRS:
         self.pull = (transport == "nvlink" and not self.quantized) if pull is None else bool(pull)
         if self.pull and (transport != "nvlink" or self.quantized):
             raise ValueError("the pull transport serves the BF16 arm on NVLink")
-        self.comm_ctas = DEFAULT_COMM_CTAS if comm_ctas is None else int(comm_ctas)
+        if comm_ctas is None:
+            from .tuning import gemm_rs_comm_ctas
+            comm_ctas = DEFAULT_COMM_CTAS if DEFAULT_COMM_CTAS else gemm_rs_comm_ctas(m, n, k, self.world)
+        self.comm_ctas = int(comm_ctas)
         if self.pull and not 1 <= self.comm_ctas <= 64:
             raise ValueError("comm_ctas must be in [1, 64]")
         self._last_operands = None
@@ -221,6 +224,26 @@ class GemmRS:
             self.workspace.epoch = value
         else:
             self._nccl_epoch = value
+
+    @property
+    def flag_tiles(self) -> int:
+        """Flag tiles per destination: 128 rows x tile_n columns of its rows."""
+        return (self.rows // 128) * (self.n // self.tile_n)
+
+    def device_tile_map(self) -> list:
+        """Mapping probe: the (row tile, column tile) pairs this operator's GEMM
+        CTAs decode from the uploaded production table, read back from the
+        device (the counterpart of the reference's mapping_probe,
+        src/gemm/native.cu:230-236)."""
+        mode = 3 if self.pull else (2 if self.quantized else 1)
+        got = lib().gemm_tile_map(self.m, self.n, self.k, mode, self.tile_kind, self.tile_order,
+                                  self.device.index if self.device.index is not None else 0)
+        return [tuple(r) for r in got.cpu().tolist()]
+
+    def host_tile_map(self) -> list:
+        """The production order as (row tile, column tile) pairs, from the host spec."""
+        cols = self.n // self.tile_n
+        return [(t // cols, t % cols) for t in self.production_ids(self.rank)]
 
     @property
     def recv(self):

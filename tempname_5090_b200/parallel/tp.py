@@ -77,10 +77,12 @@ class TensorParallel:
         return x
 
     # ------------------------------------------------------- fused linears
-    def ag_operator(self, site, m: int, k: int):
+    def ag_operator(self, site, m: int, k: int, n: int | None = None):
+        """The AG->GEMM operator of a call site (its gather buffer is the saved
+        input of that site); `n` (the GEMM's N) sizes its communication CTAs."""
         from .ag_gemm import AGGemm
         if site not in self._ag:
-            self._ag[site] = AGGemm(m, k, self.group, timeout_ns=self.timeout_ns)
+            self._ag[site] = AGGemm(m, k, self.group, timeout_ns=self.timeout_ns, n=n)
         return self._ag[site]
 
     def ag_linear(self, site, shard: torch.Tensor, weight: torch.Tensor, *, b_mn: bool = False,
@@ -95,7 +97,8 @@ class TensorParallel:
             y = G.matmul(full, weight, b_t=b_mn, bias=bias, gelu_aux=gelu_aux, gelu_grad_of=gelu_grad_of, out=out)
             return y, full
         if shard.is_cuda:
-            op = self.ag_operator(site, shard.shape[0] * self.world, shard.shape[1])
+            op = self.ag_operator(site, shard.shape[0] * self.world, shard.shape[1],
+                                  weight.shape[1] if b_mn else weight.shape[0])
             y = op.forward(shard, weight, b_mn=b_mn, bias=bias, gelu_aux=gelu_aux,
                            gelu_grad_of=gelu_grad_of, out=out)
             return y, op.gathered

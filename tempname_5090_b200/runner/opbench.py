@@ -6,6 +6,7 @@
     python -m tempname_5090_b200.runner.opbench --op gemm         # 1 GPU: tile kinds vs cuBLAS
     python -m tempname_5090_b200.runner.opbench --op gemm_once --kind 2   # one GEMM (profiler case)
     python -m tempname_5090_b200.runner.opbench --op attn_kernel  # 1 GPU: attention fwd/bwd kernels
+    python -m tempname_5090_b200.runner.opbench --op fused_emulated --world 8   # 1 GPU: fused-op kernels, ranks emulated
     torchrun ... -m tempname_5090_b200.runner.opbench --op nvlink   # SM-issued peer stores vs local copy
 
 Timing: every iteration is bracketed by CUDA events on the launching stream,
@@ -89,6 +90,34 @@ class Timer:
         return float(t.item())
 
 
+def split_phases(op, x, w, timer, iterations=10) -> dict:
+    """Pull GemmRS with its two halves as separate launches: the GEMM CTAs
+    alone (partial tiles stored and published), then the reducer CTAs alone
+    (median device times, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    out = torch.empty((op.rows, op.n), dtype=torch.bfloat16, device="cuda")
+    gemm, red = [], []
+    for _ in range(iterations + 2):
+        timer.flush.fill_(1.0)
+        if op.world > 1:
+            dist.barrier()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        op.begin()
+        e[0].record()
+        op.push(x, w)
+        e[1].record()
+        op.reduce(out)
+        e[2].record()
+        torch.cuda.synchronize()
+        gemm.append(e[0].elapsed_time(e[1]) * 1000)
+        red.append(e[1].elapsed_time(e[2]) * 1000)
+    t = torch.tensor([statistics.median(gemm[2:]), statistics.median(red[2:])], dtype=torch.float64, device="cuda")
+    if op.world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return dict(gemm_phase_us=float(t[0]), reduce_phase_us=float(t[1]))
+
+
 def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True, chunk_rows=128,
                 comm_sweep=(None,), kind_sweep=(None,)):
     import torch
@@ -120,6 +149,7 @@ def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True
                            tflops=flops / us / 1e6, nvlink_bytes_per_rank=wire, peaks=pk["source"])
                 row["back_to_back_us"] = timer.back_to_back(lambda: op.forward(x, w))
                 if op.pull:
+                    row.update(split_phases(op, x, w, timer))
                     row["comm_ctas"] = op.comm_ctas
                     row["tile_kind"] = op.tile_kind
                     prof = op.stage_profile(x, w)
@@ -196,7 +226,7 @@ def attention_case(rank, world, timer, heads=32, hidden=4096, seq=2048, batch=4)
         rows.append(dict(op="attention_stage", stage=name, world=world, us=timer.run(fn),
                          back_to_back_us=timer.back_to_back(fn)))
     if world > 1:
-        prof = tp.ag_operator(("bench_qkv", 0), m, hidden).stage_profile(xs, wqkv, bias=bqkv)
+        prof = tp.ag_operator(("bench_qkv", 0), m, hidden, 3 * hidden // world).stage_profile(xs, wqkv, bias=bqkv)
         rows.append(dict(op="stage_profile", stage="ag_gemm", world=world,
                          **{k: v for k, v in prof.items() if k != "out"}))
         prof = tp.rs_operator(m, hidden, hidden // world, "attn").stage_profile(attn, wo, residual=xs, bias=bo)
@@ -355,9 +385,118 @@ def nvlink_case(rank, world, timer, mib=64):
     return rows
 
 
+def ag_gemm_case(rank, world, timer, m=8192, hidden=4096, ffn=16384):
+    """AG->GEMM at the model's column-parallel shapes (QKV: N = 3h/W, FC1:
+    N = f/W): the fused launch, its two halves launched separately (gather
+    only -- the communication CTAs alone -- then the GEMM alone on the gathered
+    data), the device stage profile, and the library path (NCCL all_gather +
+    cuBLAS)."""
+    import torch
+    import torch.distributed as dist
+    from ..parallel.ag_gemm import AGGemm
+    rows = []
+    g = torch.Generator(device="cuda").manual_seed(41 + rank)
+    shard = torch.randn((m // world, hidden), generator=g, device="cuda").to(torch.bfloat16)
+    for name, n in (("qkv", 3 * hidden // world), ("fc1", ffn // world)):
+        op = AGGemm(m, hidden, n=n)
+        w = (0.02 * torch.randn((n, hidden), generator=g, device="cuda")).to(torch.bfloat16)
+        out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+        fused = timer.run(lambda: op.forward(shard, w, out=out))
+        b2b = timer.back_to_back(lambda: op.forward(shard, w, out=out))
+        gather = timer.run(lambda: op.forward(shard, w, out=out, phase=3))
+        gemm = timer.run(lambda: op.forward(shard, w, out=out, phase=4))
+        prof = op.stage_profile(shard, w, out=out)
+        full = torch.empty((m, hidden), dtype=torch.bfloat16, device="cuda")
+        lib_ag = timer.run(lambda: dist.all_gather_into_tensor(full, shard))
+        lib_mm = timer.run(lambda: torch.mm(full, w.t(), out=out))
+        rows.append(dict(op="ag_gemm", shape=name, m=m, n=n, k=hidden, world=world, fused_us=fused,
+                         back_to_back_us=b2b, gather_only_us=gather, gemm_only_us=gemm,
+                         library_all_gather_us=lib_ag, library_gemm_us=lib_mm, library_us=lib_ag + lib_mm,
+                         tile_kind=op.tile_kind(n, 256), comm_ctas=op.comm_ctas,
+                         gather_gbs=(world - 1) * (m // world) * hidden * 2 / gather / 1e3,
+                         stage={k: v for k, v in prof.items() if k != "out"}))
+        op.close()
+    return rows
+
+
+def fused_emulated_case(m, n, k, world, timer, repeats=3):
+    """The fused operators' kernels with W ranks emulated on ONE GPU (every
+    rank's buffers local; phases launched so that no launch waits on another):
+    the pull GemmRS GEMM phase (partial tiles TMA-stored + flags published) and
+    reducer phase (W sources pulled and reduced), and the AG->GEMM gather and
+    GEMM phases.  A small, self-ending case for a profiler; the times are
+    single-GPU (no NVLink), the kernels and their code paths are the real ones."""
+    import torch
+    from ..parallel.gemm_rs import GemmRS
+    from ..parallel.ag_gemm import AGGemm, control_layout
+    from ..parallel.symmetric import SymmetricBuffer
+    rows = m // world
+    rows_out = []
+    g = torch.Generator(device="cuda").manual_seed(3)
+    data = [SymmetricBuffer.emulated(m * n * 2, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(world * (rows // 128) * (n // 256) * 4, world)
+    ops = [GemmRS(m, n, k, _emulate=(r, world, [b.as_rank(r) for b in data], flags.as_rank(r)))
+           for r in range(world)]
+    xs = [torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16) for _ in range(world)]
+    w = (0.02 * torch.randn((n, k), generator=g, device="cuda")).to(torch.bfloat16)
+    out = torch.empty((rows, n), dtype=torch.bfloat16, device="cuda")
+    events = lambda: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    gemm_us, red_us = [], []
+    for _ in range(repeats):
+        for op in ops:
+            op.begin()
+        s, e = events()
+        s.record()
+        for r, op in enumerate(ops):
+            op.push(xs[r], w)
+        e.record()
+        torch.cuda.synchronize()
+        gemm_us.append(s.elapsed_time(e) * 1000 / world)
+        s, e = events()
+        s.record()
+        for op in ops:
+            op.reduce(out)
+        e.record()
+        torch.cuda.synchronize()
+        red_us.append(s.elapsed_time(e) * 1000 / world)
+    rows_out.append(dict(op="fused_emulated", stage="gemm_rs_pull_gemm_phase", m=m, n=n, k=k, world=world,
+                         tile_kind=ops[0].tile_kind, comm_ctas=ops[0].comm_ctas, us_per_rank=min(gemm_us)))
+    rows_out.append(dict(op="fused_emulated", stage="gemm_rs_pull_reduce_phase", world=world,
+                         us_per_rank=min(red_us), bytes_per_rank=world * rows * n * 2))
+    for b in data + [flags]:
+        b.close()
+    # AG -> GEMM: QKV shape of the attention block (K = n, N = 3 * n / W)
+    kk, nn = n, 3 * n // world
+    gather = SymmetricBuffer.emulated(m * kk * 2, world)
+    pulled_off, ctrl_bytes = control_layout(m)
+    ctrl = SymmetricBuffer.emulated(ctrl_bytes, world)
+    ags = [AGGemm(m, kk, _emulate=(r, world, gather.as_rank(r), ctrl.as_rank(r))) for r in range(world)]
+    shards = [torch.randn((rows, kk), generator=g, device="cuda").to(torch.bfloat16) for _ in range(world)]
+    wq = (0.02 * torch.randn((nn, kk), generator=g, device="cuda")).to(torch.bfloat16)
+    outs = torch.empty((m, nn), dtype=torch.bfloat16, device="cuda")
+    ag_us = []
+    for _ in range(repeats):
+        for phase in (1, 2):
+            for r in range(world):
+                ags[r].forward(shards[r], wq, phase=phase)
+        s, e = events()
+        s.record()
+        for r in range(world):
+            ags[r].forward(shards[r], wq, phase=4, out=outs)
+        e.record()
+        torch.cuda.synchronize()
+        ag_us.append(s.elapsed_time(e) * 1000 / world)
+    rows_out.append(dict(op="fused_emulated", stage="ag_gemm_gemm_phase", m=m, n=nn, k=kk, world=world,
+                         tile_kind=ags[0].tile_kind(nn, 256), us_per_rank=min(ag_us)))
+    gather.close()
+    ctrl.close()
+    return rows_out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep", "gemm", "gemm_once", "attn_kernel", "nvlink"),
+    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep", "gemm", "gemm_once", "attn_kernel", "nvlink",
+                                     "fused_emulated", "ag_gemm"),
                     default="gemmrs")
     ap.add_argument("--kind", default="2", help="gemm_once: tile kind 0/1/2/-1 or 'cublas'")
     ap.add_argument("--m", type=int, default=8192)
@@ -367,6 +506,7 @@ def main(argv=None):
     ap.add_argument("--transports", default="nvlink,nccl")
     ap.add_argument("--comm-ctas", default="", help="gemmrs: comma list of reducer CTA counts (pull transport)")
     ap.add_argument("--tile-kinds", default="", help="gemmrs: comma list of pull GEMM tile kinds (0 single, 2 wide)")
+    ap.add_argument("--world", type=int, default=8, help="fused_emulated: emulated ranks on one GPU")
     ap.add_argument("--out", type=Path)
     args = ap.parse_args(argv)
     import torch
@@ -395,6 +535,10 @@ def main(argv=None):
         rows += attention_kernel_case(timer)
     elif args.op == "nvlink":
         rows += nvlink_case(rank, world, timer)
+    elif args.op == "ag_gemm":
+        rows += ag_gemm_case(rank, world, timer)
+    elif args.op == "fused_emulated":
+        rows += fused_emulated_case(args.m, args.n, args.k, args.world, timer)
     elif args.op == "attention":
         rows += attention_case(rank, world, timer)
     else:

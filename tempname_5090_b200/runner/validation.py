@@ -3,8 +3,10 @@
 * `validate_packet_bytes` (stdlib) / `packet_tensor_valid` (device boolean):
   exact SoA size, finite E4M3 payload, scales in range.
 * `validate_operator_buffers`: after a fused GemmRS call, every tile flag of
-  every source equals the call's epoch, the output is finite and the device
-  status word is clear -- MIN-reduced over ranks so all ranks fail together.
+  every source equals the call's epoch, the device's read-back of the tile map
+  equals the host's production order (mapping probe), the output is finite
+  and the device status word is clear -- MIN-reduced over ranks so all ranks
+  fail together.
 * `projection_reference`: an independent GemmRS result built from a library
   GEMM (test oracle only), a dense all_to_all and the ordered BF16 sum, plus
   the same with an independent FP32 torch statement of the TACO codec.
@@ -79,15 +81,21 @@ def validate_operator_buffers(op, output) -> dict:
     good = bool(torch.isfinite(output).all())
     detail = []
     if op.transport == "nvlink":
-        flags = op.flags.local_view((op.world * op.tiles_per_dest,), torch.int32)
+        flags = op.flags.local_view((op.world * op.flag_tiles,), torch.int32)
         if not bool((flags == op.epoch).all()):
             good = False
             detail.append("tile flags do not all equal the call epoch")
+        # Mapping probe: the device decodes the uploaded production table into
+        # exactly the host's tile order (reference validation.py:96-100).
+        if op.device_tile_map() != op.host_tile_map():
+            good = False
+            detail.append("device tile map differs from the host production order")
     if int(status_tensor(output.device)[0].item()) != 0:
         good = False
         detail.append("device status word set")
     require_all(good, "operator buffer/publication validation failed: " + "; ".join(detail), op.group)
-    return dict(passed=True, tiles_checked=op.tiles_per_dest * op.world, scope="untimed, rank-coordinated")
+    return dict(passed=True, tiles_checked=op.flag_tiles * op.world, mapping_probe=True,
+                scope="untimed, rank-coordinated")
 
 
 def projection_reference(x, w, rank: int, world: int, group, quantized: bool):

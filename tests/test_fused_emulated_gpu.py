@@ -303,3 +303,23 @@ def test_guard_regions_stay_intact_and_detect_an_overrun(arm):
     assert recv[1].check_guards() == []
     for b in recv + [flags]:
         b.close()
+
+
+@pytest.mark.parametrize("arm,kind", [("flux", 0), ("flux", 2), ("flux_taco", 0), ("flux_taco_interleaved", 0)])
+def test_mapping_probe_reads_back_the_host_production_order(arm, kind):
+    """The device decodes each operator's uploaded production table into
+    exactly the host's tile order (every tile once, the rotated / interleaved
+    destination sequence) -- the mapping probe of the validation gate."""
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    world, m, n, k = 4, 2048, 1024, 512
+    data = [SymmetricBuffer.emulated(m * n * 2, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(world * (m // world // 128) * (n // 256) * 4, world)
+    for r in range(world):
+        op = GemmRS(m, n, k, arm=arm, tile_kind=kind if arm == "flux" else None,
+                    _emulate=(r, world, [b.as_rank(r) for b in data], flags.as_rank(r)))
+        host = op.host_tile_map()
+        assert op.device_tile_map() == host
+        assert len(set(host)) == len(host) == (m // op.tile_m) * (n // op.tile_n)
+    for b in data + [flags]:
+        b.close()

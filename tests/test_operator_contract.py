@@ -232,15 +232,15 @@ def test_ag_gemm_launch_contract(monkeypatch, rank, world):
     op.forward(shard, w, gelu_aux=aux)
     op.forward(shard, w.t().contiguous(), b_mn=True, gelu_grad_of=aux)
     c = fake.calls
-    # One launch per call; cumulative counter targets: (W-1) peers x 7 gatherer
-    # CTAs finished reading per previous call, 4 pieces (16 KB) per 128-row
-    # block of K=256 per call.
+    # One launch per call; targets: (W-1) peers x 7 gatherer CTAs finished
+    # reading per previous call (cumulative), and the per-block arrival flag
+    # equal to the call's epoch.
     assert [x["epoch"] for x in c] == [1, 2, 3] and all(x["phase"] == 7 for x in c)
     assert [x["pulled"] for x in c] == [0, 7 * (world - 1), 14 * (world - 1)]
     pulled_offset, _ = ag_gemm.control_layout(m)
     assert pulled_offset % 256 == 0 and pulled_offset >= 4 * m // 128
     assert all(x["pulled_local"] == ctrl.local + pulled_offset for x in c)
-    assert op.pieces_per_block == 4 and [x["ready"] for x in c] == [4, 8, 12]
+    assert [x["ready"] for x in c] == [1, 2, 3]
     assert [x["epi"] for x in c] == [G.EPI_BIAS, G.EPI_GELU, G.EPI_GELU_BWD]
     assert [x["aux"] for x in c] == [False, True, True] and [x["b_mn"] for x in c] == [False, False, True]
     # Own chunk first, then rank+1, ...: the first tiles need no peer data.
