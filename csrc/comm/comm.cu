@@ -151,40 +151,55 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
     }
     return;
   }
-  // Arrival-first: lane = parity of the tile's block-within-destination.  All
-  // threads scan the lane's unclaimed tiles in parallel; the CTA claims (CAS
-  // tagged with the epoch) the first ready tile at or after its own starting
-  // position in the consumer order, cyclically.  The starting positions of the
-  // lane's CTAs are spread evenly over the order, so CTAs do not all race for
-  // the same tile.
+  // Arrival-first: lane = parity of the tile's block-within-destination.  Each
+  // CTA of a lane scans a window of kWindow positions of the consumer order
+  // starting at its low-water mark (every earlier position of its lane is
+  // claimed), and claims (CAS tagged with the epoch) the first ready unclaimed
+  // tile of its lane found from its own offset in the window, cyclically -- the
+  // offsets of a lane's CTAs are spread over the window, so they do not all race
+  // for one tile, and a scan polls at most kWindow tiles' flags instead of all.
+  constexpr int kWindow = 128;
   const int lane_id = blockIdx.x & 1;
-  const int lane_ctas = max(1, int(gridDim.x) >> 1);
-  const int origin = int((int64_t(blockIdx.x >> 1) * tiles) / lane_ctas);
+  const int offset = int((blockIdx.x >> 1) * 37) % kWindow;
   const uint64_t start = globaltimer_ns();
-  __shared__ int s_best;
+  __shared__ int s_best, s_lwm;
+  if (threadIdx.x == 0) s_lwm = 0;
+  __syncthreads();
+  auto lane_of = [&](int i) {
+    const int tile = c.tile_order ? c.tile_order[i] : i;
+    return ((tile / tiles_n) * 128 / c.chunk_rows) & 1;
+  };
+  auto claimed = [&](int i) {
+    const int tile = c.tile_order ? c.tile_order[i] : i;
+    return int32_t(uint32_t(*reinterpret_cast<volatile int*>(c.claims + tile)) - c.epoch) >= 0;
+  };
   for (;;) {
-    if (threadIdx.x == 0) s_best = 0x7fffffff;
+    if (threadIdx.x == 0) {
+      // Advance the low-water mark over other lanes' positions and claimed ones.
+      int lwm = s_lwm;
+      while (lwm < tiles && (lane_of(lwm) != lane_id || claimed(lwm))) ++lwm;
+      s_lwm = lwm;
+      s_best = 0x7fffffff;
+    }
     __syncthreads();
-    int best = 0x7fffffff, open = 0;  // best: cyclic distance from `origin`
-    for (int i = threadIdx.x; i < tiles; i += kThreads) {
+    const int lwm = s_lwm;
+    if (lwm >= tiles) return;  // lane drained
+    const int span = min(kWindow, tiles - lwm);
+    int best = 0x7fffffff;  // cyclic distance from this CTA's offset inside the window
+    for (int w = threadIdx.x; w < span; w += kThreads) {
+      const int i = lwm + w;
+      if (lane_of(i) != lane_id || claimed(i)) continue;
       const int tile = c.tile_order ? c.tile_order[i] : i;
-      const int blk = (tile / tiles_n) * 128 / c.chunk_rows;
-      if ((blk & 1) != lane_id) continue;
-      const int old = *reinterpret_cast<volatile int*>(c.claims + tile);
-      if (int32_t(uint32_t(old) - c.epoch) >= 0) continue;  // already taken this epoch
-      open = 1;
-      const int dist = (i - origin + tiles) % tiles;
+      const int dist = (w - offset % span + span) % span;
       if (dist < best && tile_ready(c, tile, tiles)) best = dist;
     }
     if (best != 0x7fffffff) atomicMin(&s_best, best);
-    const int any_open = __syncthreads_or(open);
+    __syncthreads();
     if (threadIdx.x == 0) {
       int found = -1;
-      if (!any_open) {
-        found = -2;  // lane drained
-      } else if (s_best != 0x7fffffff) {
-        const int pos = (origin + s_best) % tiles;
-        const int tile = c.tile_order ? c.tile_order[pos] : pos;
+      if (s_best != 0x7fffffff) {
+        const int i = lwm + (offset % span + s_best) % span;
+        const int tile = c.tile_order ? c.tile_order[i] : i;
         const int old = *reinterpret_cast<volatile int*>(c.claims + tile);
         // tile_ready is this thread's own acquire of the flags (monotonic epochs:
         // ready for the scanning thread implies ready here).

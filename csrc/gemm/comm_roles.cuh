@@ -77,6 +77,8 @@ __device__ __forceinline__ uint32_t atom_acq_rel_gpu_add(uint32_t* p, uint32_t v
 template <int TILE_CC>
 __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tres) {
   constexpr int TILE_RB = 1;
+  constexpr int kUnit = TILE_CC / 2;                 // pieces per work unit (half a flag tile)
+  constexpr int kUnitsPerTile = TILE_CC / kUnit;
   const PullRsArgs& a = p.pull;
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kCommStages * kPiece);
@@ -108,55 +110,45 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
 #pragma unroll
     for (int s = 0; s < kCommStages; ++s) last_parity[s] = -1;
     bool ok = true;
-    // Work unit: one piece (128 rows x 64 columns of a flag tile), assigned
-    // round-robin over the consumption order, so the last tiles of the GEMM are
-    // spread over all reducer CTAs instead of one CTA per tile.
-    int waited_tile = -1;
-    uint32_t waited = 0;
-    for (int q = cta; q < tiles * TILE_CC && ok; q += ctas) {
-      const int i = q / TILE_CC, pc = q % TILE_CC;
+    // Work unit: half a flag tile (kUnit pieces), assigned round-robin over the
+    // consumption order, so the GEMM's last tiles are spread over twice as many
+    // reducer CTAs as whole tiles would be.  A unit first waits for the flags
+    // of all W sources, then issues one proxy fence (each fence is paid with
+    // the bulk loads in flight) before its loads.
+    for (int q = cta; q < tiles * kUnitsPerTile && ok; q += ctas) {
+      const int i = q / kUnitsPerTile;
       const int lt = a.order ? a.order[i] : i;
       const int ltm = lt / tiles_n, tn = lt % tiles_n;
-      if (i != waited_tile) {
-        waited_tile = i;
-        waited = 0;
-      }
-      {
-        {
-          const int64_t off = piece_offset(rb_base + ltm, tn * TILE_CC + pc, n_chunks);
-          if (a.residual) {
-            const int st = int(seq % kCommStages);
-            const uint32_t ph = (seq / kCommStages) & 1u;
-            if (!mbar_wait(&empty[st], ph ^ 1u, p.timeout_ns, p.status, kTimeoutProducerEmpty, abort_flag)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&full[st], kPiece);
-            tma_load_2d(ring + st * kPiece, tres, &full[st], (tn * TILE_CC + pc) * 64, ltm * 128);
-            last_parity[st] = int(ph);
-            ++seq;
+      for (int s = 0; s < world && ok; ++s)
+        ok = wait_flag_geq(a.my_flags + int64_t(s) * tiles + lt, p.rs.epoch, p.timeout_ns, p.status,
+                           kTimeoutPeerFlag);
+      if (!ok) break;
+      fence_proxy_async_global();  // flag acquires before the bulk engine reads the pieces
+      for (int pc = (q % kUnitsPerTile) * kUnit; pc < (q % kUnitsPerTile + 1) * kUnit && ok; ++pc) {
+        const int64_t off = piece_offset(rb_base + ltm, tn * TILE_CC + pc, n_chunks);
+        if (a.residual) {
+          const int st = int(seq % kCommStages);
+          const uint32_t ph = (seq / kCommStages) & 1u;
+          if (!mbar_wait(&empty[st], ph ^ 1u, p.timeout_ns, p.status, kTimeoutProducerEmpty, abort_flag)) {
+            ok = false;
+            break;
           }
-          for (int s = 0; s < world; ++s) {
-            if (!((waited >> s) & 1u)) {
-              if (!wait_flag_geq(a.my_flags + int64_t(s) * tiles + lt, p.rs.epoch, p.timeout_ns, p.status,
-                                 kTimeoutPeerFlag)) {
-                ok = false;
-                break;
-              }
-              fence_proxy_async_global();  // flag acquire before the bulk engine reads the piece
-              waited |= 1u << s;
-            }
-            const int st = int(seq % kCommStages);
-            const uint32_t ph = (seq / kCommStages) & 1u;
-            if (!mbar_wait(&empty[st], ph ^ 1u, p.timeout_ns, p.status, kTimeoutProducerEmpty, abort_flag)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&full[st], kPiece);
-            bulk_load(ring + st * kPiece, a.partial[s] + off, kPiece, &full[st]);
-            last_parity[st] = int(ph);
-            ++seq;
+          mbar_arrive_expect_tx(&full[st], kPiece);
+          tma_load_2d(ring + st * kPiece, tres, &full[st], (tn * TILE_CC + pc) * 64, ltm * 128);
+          last_parity[st] = int(ph);
+          ++seq;
+        }
+        for (int s = 0; s < world; ++s) {
+          const int st = int(seq % kCommStages);
+          const uint32_t ph = (seq / kCommStages) & 1u;
+          if (!mbar_wait(&empty[st], ph ^ 1u, p.timeout_ns, p.status, kTimeoutProducerEmpty, abort_flag)) {
+            ok = false;
+            break;
           }
+          mbar_arrive_expect_tx(&full[st], kPiece);
+          bulk_load(ring + st * kPiece, a.partial[s] + off, kPiece, &full[st]);
+          last_parity[st] = int(ph);
+          ++seq;
         }
       }
     }
@@ -173,12 +165,12 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
   const int rt = threadIdx.x - 64;  // 0..127
   const uint32_t zero = 0u;         // two +0.0 BF16 values
   uint32_t seq = 0;
-  for (int q = cta; q < tiles * TILE_CC; q += ctas) {
-    const int i = q / TILE_CC, pc = q % TILE_CC;
+  for (int q = cta; q < tiles * kUnitsPerTile; q += ctas) {
+    const int i = q / kUnitsPerTile;
     const int lt = a.order ? a.order[i] : i;
     const int ltm = lt / tiles_n, tn = lt % tiles_n;
     constexpr int pr = 0;
-    {
+    for (int pc = (q % kUnitsPerTile) * kUnit; pc < (q % kUnitsPerTile + 1) * kUnit; ++pc) {
       {
         // This thread's eight 16-byte units: unit rt + 128u is row rt/8 + 16u,
         // columns (rt % 8) * 8 .. +8 of the piece.  The residual tile arrives in

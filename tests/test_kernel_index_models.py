@@ -10,8 +10,9 @@ the kernel relies on:
   pairs the elementwise warp of its half wrote, and each warp writes only inside
   the 64 score columns it alone reads.
 * Arrival-first receiver (`rs_reduce_kernel` in csrc/comm/comm.cu): with tiles
-  becoming ready in any order, the per-lane claim loop (spread origins, cyclic
-  nearest ready tile, CAS) claims every tile exactly once and every CTA exits.
+  becoming ready in any order, the per-lane claim loop (low-water mark, scan
+  window, spread offsets, cyclic nearest ready tile, CAS) claims every tile
+  exactly once and every CTA exits.
 """
 import random
 
@@ -69,13 +70,18 @@ def test_attention_packed_probability_columns():
         assert want == list(range(packed_col(kk), packed_col(kk) + 8))
 
 
-def _simulate_arrival(tiles, chunk_tiles, ctas, ready_order, rng):
-    """One epoch of the claim protocol; returns {tile: claiming CTA}."""
+def _simulate_arrival(tiles, chunk_tiles, ctas, ready_order, rng, window=128):
+    """One epoch of the windowed claim protocol of rs_reduce_kernel (arrival
+    arm); returns {tile: claiming CTA}.  Each CTA keeps a low-water mark (all
+    earlier positions of its lane claimed), scans `window` positions from it
+    and claims the first ready unclaimed tile of its lane found from its own
+    offset in the window, cyclically."""
     claims = {}
     ready = set()
     pending = list(ready_order)
-    lane_ctas = max(1, ctas // 2)
-    origins = [((c >> 1) * tiles) // lane_ctas for c in range(ctas)]
+    lwm = [0] * ctas
+    offsets = [((c >> 1) * 37) % window for c in range(ctas)]
+    lane_of = lambda i: (i // chunk_tiles) % 2
     active = set(range(ctas))
     steps = 0
     while active:
@@ -85,21 +91,24 @@ def _simulate_arrival(tiles, chunk_tiles, ctas, ready_order, rng):
             ready.add(pending.pop(0))
         c = rng.choice(sorted(active))  # any CTA may run next
         lane = c & 1
-        lane_tiles = [i for i in range(tiles) if (i // chunk_tiles) % 2 == lane]
-        open_tiles = [i for i in lane_tiles if i not in claims]
-        if not open_tiles:
+        while lwm[c] < tiles and (lane_of(lwm[c]) != lane or lwm[c] in claims):
+            lwm[c] += 1
+        if lwm[c] >= tiles:
             active.discard(c)  # lane drained: the CTA exits
             continue
-        cands = [(i - origins[c]) % tiles for i in open_tiles if i in ready]
+        span = min(window, tiles - lwm[c])
+        off = offsets[c] % span
+        cands = [((w - off) % span, lwm[c] + w) for w in range(span)
+                 if lane_of(lwm[c] + w) == lane and lwm[c] + w not in claims and lwm[c] + w in ready]
         if not cands:
             continue  # nothing ready: back off and rescan
-        pos = (origins[c] + min(cands)) % tiles
+        pos = min(cands)[1]
         if pos not in claims:  # the CAS
             claims[pos] = c
     return claims
 
 
-@pytest.mark.parametrize("tiles,chunk_tiles,ctas", [(32, 2, 8), (64, 4, 20), (48, 1, 96), (16, 2, 2)])
+@pytest.mark.parametrize("tiles,chunk_tiles,ctas", [(32, 2, 8), (64, 4, 20), (48, 1, 96), (16, 2, 2), (512, 2, 40)])
 def test_arrival_claims_every_tile_once_and_terminates(tiles, chunk_tiles, ctas):
     rng = random.Random(tiles * 131 + ctas)
     for trial in range(5):
