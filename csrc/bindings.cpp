@@ -222,6 +222,9 @@ void ag_gemm(const at::Tensor& shard, const at::Tensor& gather, const at::Tensor
   c.ag = 1;
   c.rank = int(rank); c.world = int(world);
   c.ag_shard = shard.data_ptr();
+  // A shard that already is this rank's chunk of the gather buffer is published in place.
+  c.ag_own_in_place = shard.data_ptr() == static_cast<void*>(static_cast<uint8_t*>(gather.data_ptr()) +
+                                                             rank * shard.numel() * 2);
   c.ag_gather = reinterpret_cast<uint8_t* const*>(gather_ptrs);
   c.ag_published = reinterpret_cast<uint32_t* const*>(published_ptrs);
   c.ag_pulled = reinterpret_cast<uint32_t* const*>(pulled_ptrs);

@@ -88,7 +88,7 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
   if (threadIdx.x == 0) {
     for (int s = 0; s < kCommStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kRedWarps);
+      mbar_init(&empty[s], kRedWarps);  // each stage is consumed by one group of kRedWarps warps
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -162,15 +162,23 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
   }
   if (warp < 2) return;
   // --------------------------------------------------------- reducer warps
-  const int rt = threadIdx.x - 64;  // 0..127
-  const uint32_t zero = 0u;         // two +0.0 BF16 values
-  uint32_t seq = 0;
+  // kRedGroups groups of four warps; group `grp` reduces the pieces whose
+  // position in this CTA's piece sequence is grp modulo kRedGroups.  The loader
+  // issues each piece's stages contiguously (residual, then W sources), so a
+  // group finds its piece's first stage at piece_index * stages_per_piece.
+  const int grp = (warp - 2) / kRedWarps;
+  const int rt = threadIdx.x - 64 - grp * 128;  // 0..127 inside the group
+  const uint32_t zero = 0u;                      // two +0.0 BF16 values
+  const uint32_t stages_per_piece = uint32_t(world + (a.residual ? 1 : 0));
+  uint32_t piece_index = 0;                      // pieces of this CTA seen so far
   for (int q = cta; q < tiles * kUnitsPerTile; q += ctas) {
     const int i = q / kUnitsPerTile;
     const int lt = a.order ? a.order[i] : i;
     const int ltm = lt / tiles_n, tn = lt % tiles_n;
     constexpr int pr = 0;
-    for (int pc = (q % kUnitsPerTile) * kUnit; pc < (q % kUnitsPerTile + 1) * kUnit; ++pc) {
+    for (int pc = (q % kUnitsPerTile) * kUnit; pc < (q % kUnitsPerTile + 1) * kUnit; ++pc, ++piece_index) {
+      if (int(piece_index % kRedGroups) != grp) continue;
+      uint32_t seq = piece_index * stages_per_piece;
       {
         // This thread's eight 16-byte units: unit rt + 128u is row rt/8 + 16u,
         // columns (rt % 8) * 8 .. +8 of the piece.  The residual tile arrives in
@@ -244,7 +252,7 @@ __device__ void rs_reducer(const Params& p, uint8_t* smem, const CUtensorMap* tr
     }
     if (a.stamps) {
       // A flag tile is complete when its last piece is: keep the latest piece time.
-      named_barrier_sync(2, kRedWarps * 32);
+      named_barrier_sync(2 + grp, kRedWarps * 32);
       if (rt == 0) atomicMax(a.stamps + lt, (unsigned long long)globaltimer_ns());
     }
   }
@@ -391,9 +399,20 @@ __device__ void ag_gatherer(const Params& p, uint8_t* smem) {
   };
   // Job sequence: own blocks 0..blocks-1, then peer (rank+step) block b as job
   // blocks + (step-1) * blocks + b; this CTA takes jobs cta, cta + ctas, ...
-  const int own_jobs = (g.phase & 1) ? blocks : 0;
+  if ((g.phase & 1) && g.own_in_place) {
+    // The caller wrote the shard straight into the own chunk (after a bounded
+    // wait for the peers' previous reads, launched before the writer): the
+    // blocks are complete in local memory since the previous kernel -- release
+    // them to every peer.
+    for (int b = cta; b < blocks; b += ctas) {
+      fence_acq_rel_sys();
+      for (int d = 0; d < world; ++d)
+        if (d != rank) st_release_sys(g.published[d] + rank * blocks + b, g.epoch);
+    }
+  }
+  const int own_jobs = ((g.phase & 1) && !g.own_in_place) ? blocks : 0;
   const int total = own_jobs + ((g.phase & 2) ? (world - 1) * blocks : 0);
-  if (g.phase & 1) {
+  if (own_jobs) {
     // Own chunk: overwrite it only once every peer has finished reading the
     // previous call's contents.
     if (!wait_flag_geq(g.pulled_local, g.pulled_target, p.timeout_ns, p.status, kTimeoutPeerFlag)) return;

@@ -87,7 +87,7 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
     if (e != cudaSuccess) return int(e);
     if (dev < 64) configured[dev] = true;
   }
-  const int threads = kThreads;
+  const int threads = kThreadsFor<MODE>;
   if constexpr (PAIR) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(grid), 1, 1);
@@ -328,6 +328,7 @@ int run(const GemmCall& c, cudaStream_t stream) {
     g.ready_target = c.ag_ready_target;
     g.phase = c.phase;
     g.block_stamps = c.ag_block_stamps;
+    g.own_in_place = c.ag_own_in_place;
   }
   CUtensorMap ma, mb;
   const bool ok_a = c.a_mn ? make_map(&ma, c.A, c.M, c.K, c.lda, 64, 64)

@@ -68,6 +68,7 @@ struct GemmCall {
   const uint32_t* ag_pulled_local = nullptr;
   uint32_t* ag_ready = nullptr;                   // local [world][M/world/128]
   uint32_t ag_epoch = 0, ag_pulled_target = 0, ag_ready_target = 0;
+  int ag_own_in_place = 0;                        // shard == own chunk of the gather buffer
   unsigned long long* ag_block_stamps = nullptr;  // optional: arrival time of every gathered block
   unsigned long long* cta_stamps = nullptr;       // optional [grid][2]: start / end of every CTA
   // status / bounded waits

@@ -40,6 +40,11 @@ constexpr int kBM = 128;             // UMMA M (one CTA, cta_group::1)
 constexpr int kBK = 64;              // k-block: 64 bf16 = one 128-byte swizzle row
 constexpr int kUmmaK = 16;           // K per tcgen05.mma for 16-bit inputs
 constexpr int kThreads = 192;
+// Pull reduce-scatter launches carry two more 128-thread groups: in the reducer
+// CTAs they reduce alternate pieces (the GEMM CTAs' extra warps exit at once).
+constexpr int kRedGroups = 2;
+template <int MODE>
+constexpr int kThreadsFor = MODE == 3 ? 64 + kRedGroups * 128 : kThreads;
 constexpr int kEpiWarps = 4;
 constexpr int kEpiFirstWarp = 2;
 
@@ -95,6 +100,7 @@ struct GatherArgs {
   uint32_t pulled_target;          // pulled value once every peer finished reading the previous call
   uint32_t ready_target;           // ready[c][b] once block b of chunk c has arrived (the epoch)
   int phase;                       // communication CTAs: bit0 own chunk + publish, bit1 pull peers
+  int own_in_place;                // the shard already is the own chunk of the gather buffer: publish only
   unsigned long long* block_stamps; // optional [world * rows_per_src / 128]: when each block was stored
 };
 
@@ -307,7 +313,7 @@ namespace gemm {
 // matrix (tile-major pieces the reducer pulls with single bulk loads) and
 // tmap_a2 the residual [M/W, N] that the reducer CTAs load tile by tile.
 template <int BN, int STAGES, int EPI_COLS, int MODE, bool AG, bool PAIR = false, bool WIDE = false>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsFor<MODE>, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_out,
                 const __grid_constant__ CUtensorMap tmap_a2, const __grid_constant__ Params p, int a_mn,

@@ -223,7 +223,8 @@ class GPT:
             with tracing.scope(f"gpt.layer{i}.forward"):
                 x = self._layer_forward(i, x, saved, keep)
         x_final = x
-        lnf, meanf, rstdf = N.layer_norm_fwd(x_final, self.p["final_weight"], self.p["final_bias"], self.eps)
+        buf = tp.ag_input(("head", 0), M, self.h, self.Vl, x.is_cuda)
+        lnf, meanf, rstdf = N.layer_norm_fwd(x_final, self.p["final_weight"], self.p["final_bias"], self.eps, out=buf)
         logits, lnf_full = tp.ag_linear(("head", 0), lnf, self.p["embedding"])
         loss, ce_state = CE.forward(logits, targets, tp.group, self.rank, self.world, scale=loss_scale / M)
         self.forward_calls += 1
@@ -236,12 +237,19 @@ class GPT:
         lh = self.lh
         p = f"layers.{i}."
         x_in = x
-        ln1, mean1, rstd1 = N.layer_norm_fwd(x_in, self.p[p + "ln1_weight"], self.p[p + "ln1_bias"], self.eps)
+        # LayerNorm outputs are written straight into the fused AG->GEMM's gather
+        # buffer (published to the peers without a copy) when TP > 1.
+        h, W = self.h, self.world
+        buf = tp.ag_input(("qkv", i), M, h, 3 * h // W, x.is_cuda)
+        ln1, mean1, rstd1 = N.layer_norm_fwd(x_in, self.p[p + "ln1_weight"], self.p[p + "ln1_bias"], self.eps,
+                                             out=buf)
         qkv, ln1_full = tp.ag_linear(("qkv", i), ln1, self.p[p + "qkv_weight"], bias=self.p[p + "qkv_bias"])
         attn, lse = A.forward(qkv, c["micro_batch"], c["sequence"], lh)
         x2 = tp.linear_rs(attn, self.p[p + "attn_weight"], residual=x_in, bias=self.p[p + "attn_bias"],
                           role="attn")
-        ln2, mean2, rstd2 = N.layer_norm_fwd(x2, self.p[p + "ln2_weight"], self.p[p + "ln2_bias"], self.eps)
+        buf = tp.ag_input(("fc1", i), M, h, self.f // W, x.is_cuda)
+        ln2, mean2, rstd2 = N.layer_norm_fwd(x2, self.p[p + "ln2_weight"], self.p[p + "ln2_bias"], self.eps,
+                                             out=buf)
         pre = torch.empty((M, self.f // self.world), dtype=torch.bfloat16, device=self.device)
         act, ln2_full = tp.ag_linear(("fc1", i), ln2, self.p[p + "fc1_weight"], bias=self.p[p + "fc1_bias"],
                                      gelu_aux=pre)
@@ -265,8 +273,10 @@ class GPT:
         N.column_sum(dpre, out=g[p + "fc1_bias"], workspace=col_ws)
         dln2 = tp.linear_rs(dpre, self.p[p + "fc1_weight"], b_mn=True, role="mlp_bwd")
         G.matmul(dpre, ln2_full, a_t=True, b_t=True, out=g[p + "fc1_weight"])
+        M, h, W = self.M, self.h, self.world
         dx2, dw2, db2 = N.layer_norm_bwd(dln2, x2, self.p[p + "ln2_weight"], mean2, rstd2, dres=dx,
-                                         workspace=ln_ws)
+                                         workspace=ln_ws,
+                                         out=tp.ag_input(("attn_bwd", i % 2), M, h, h // W, dx.is_cuda))
         g[p + "ln2_weight"].copy_(dw2)
         g[p + "ln2_bias"].copy_(db2)
         # attention out-projection (row-parallel): x2 = x_in + RS(attn @ Wattn^T) + b
@@ -278,8 +288,10 @@ class GPT:
         N.column_sum(dqkv, out=g[p + "qkv_bias"], workspace=col_ws)
         dln1 = tp.linear_rs(dqkv, self.p[p + "qkv_weight"], b_mn=True, role="attn_bwd")
         G.matmul(dqkv, ln1_full, a_t=True, b_t=True, out=g[p + "qkv_weight"])
+        # The input gradient feeds the previous layer's FC2-backward AG->GEMM.
+        nxt = tp.ag_input(("fc2_bwd", (i - 1) % 2), M, h, self.f // W, dx2.is_cuda) if i > 0 else None
         dx, dw1, db1 = N.layer_norm_bwd(dln1, x_in, self.p[p + "ln1_weight"], mean1, rstd1, dres=dx2,
-                                        workspace=ln_ws)
+                                        workspace=ln_ws, out=nxt)
         g[p + "ln1_weight"].copy_(dw1)
         g[p + "ln1_bias"].copy_(db1)
         return dx
@@ -312,7 +324,10 @@ class GPT:
         CE.backward(logits, targets, ce_state, loss_scale / M)
         dlnf = tp.linear_rs(logits, self.p["embedding"], b_mn=True, role="head")
         G.matmul(logits, lnf_full, a_t=True, b_t=True, out=g["embedding"])
-        dx, dwf, dbf = N.layer_norm_bwd(dlnf, x_final, self.p["final_weight"], meanf, rstdf, workspace=ln_ws)
+        L = c["layers"]
+        dx, dwf, dbf = N.layer_norm_bwd(dlnf, x_final, self.p["final_weight"], meanf, rstdf, workspace=ln_ws,
+                                        out=tp.ag_input(("fc2_bwd", (L - 1) % 2), M, self.h, self.f // self.world,
+                                                        dlnf.is_cuda))
         g["final_weight"].copy_(dwf)
         g["final_bias"].copy_(dbf)
         for i in reversed(range(c["layers"])):

@@ -32,11 +32,12 @@ def layer_norm_fwd(x, weight, bias, eps, out=None):
     return y, mean, rstd
 
 
-def layer_norm_bwd(dy, x, weight, mean, rstd, dres=None, workspace=None):
-    """Returns (dx, dweight, dbias); dx = bf16(bf16(ln_dx) + dres) when dres is given."""
+def layer_norm_bwd(dy, x, weight, mean, rstd, dres=None, workspace=None, out=None):
+    """Returns (dx, dweight, dbias); dx = bf16(bf16(ln_dx) + dres) when dres is given,
+    written into `out` (contiguous [rows, H]) when given."""
     rows, H = x.shape
     if x.is_cuda:
-        dx = torch.empty_like(x)
+        dx = torch.empty_like(x) if out is None else out
         dw = torch.empty(H, dtype=torch.bfloat16, device=x.device)
         db = torch.empty(H, dtype=torch.bfloat16, device=x.device)
         need = lib().layernorm_bwd_workspace(rows, H)
@@ -53,7 +54,11 @@ def layer_norm_bwd(dy, x, weight, mean, rstd, dres=None, workspace=None):
     dx = rstd[:, None] * (gw - s1 - xhat * s2)
     if dres is not None:
         dx = dx.to(torch.bfloat16).float() + dres.float()
-    return (dx.to(x.dtype), (g * xhat).sum(0).to(x.dtype), g.sum(0).to(x.dtype))
+    dx = dx.to(x.dtype)
+    if out is not None:
+        out.copy_(dx)
+        dx = out
+    return (dx, (g * xhat).sum(0).to(x.dtype), g.sum(0).to(x.dtype))
 
 
 def gelu_bwd(dy, pre):

@@ -123,6 +123,20 @@ class AGGemm:
         """This rank's gathered [M, K] input of the most recent call."""
         return self.gather.local_view((self.m, self.k), torch.bfloat16)
 
+    def input_buffer(self) -> torch.Tensor:
+        """This rank's chunk of the gather buffer as a [M/W, K] tensor, ready to
+        be written with the NEXT call's shard (e.g. by the kernel producing it):
+        a bounded device wait, launched here on the current stream, holds the
+        writer back until every peer has finished reading the previous call's
+        contents.  Passing this view as `shard` skips the own-chunk copy: its
+        blocks are published to the peers as soon as the call starts."""
+        rows = self.m // self.world
+        if self.device.type == "cuda":
+            target = self.targets(self.calls + 1)["pulled_target"]
+            lib().wait_probe(self.ctrl.local + self.pulled_offset, target, self.timeout_ns, self.status)
+            count_launch()
+        return self.gather.local_view((rows, self.k), torch.bfloat16, offset=self.rank * rows * self.k * 2)
+
     def _order(self, n: int, bn: int, kind: int) -> torch.Tensor:
         key = (n, bn, kind)
         if key not in self._orders:

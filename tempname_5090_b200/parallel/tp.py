@@ -85,6 +85,15 @@ class TensorParallel:
             self._ag[site] = AGGemm(m, k, self.group, timeout_ns=self.timeout_ns, n=n)
         return self._ag[site]
 
+    def ag_input(self, site, m: int, k: int, n: int, on_cuda: bool):
+        """Where the producer of `site`'s next AG->GEMM input should write it:
+        this rank's chunk of the fused operator's gather buffer (written in
+        place, it is published to the peers without a copy), or None (one rank,
+        CPU, or an unfused transport)."""
+        if self.world == 1 or not on_cuda or self.transport != "nvlink":
+            return None
+        return self.ag_operator(site, m, k, n).input_buffer()
+
     def ag_linear(self, site, shard: torch.Tensor, weight: torch.Tensor, *, b_mn: bool = False,
                   bias=None, gelu_aux=None, gelu_grad_of=None, out=None):
         """Return (output [M, N], gathered input [M, K])."""

@@ -425,7 +425,10 @@ def fused_emulated_case(m, n, k, world, timer, repeats=3):
     the pull GemmRS GEMM phase (partial tiles TMA-stored + flags published) and
     reducer phase (W sources pulled and reduced), and the AG->GEMM gather and
     GEMM phases.  A small, self-ending case for a profiler; the times are
-    single-GPU (no NVLink), the kernels and their code paths are the real ones."""
+    single-GPU (no NVLink), the kernels and their code paths are the real ones.
+    Launch sequence per repeat (for a profiler's launch skip count): W GemmRS
+    GEMM phases, W reducer phases; after all repeats, per repeat W AG own-chunk
+    phases, W peer-pull phases, W AG GEMM phases."""
     import torch
     from ..parallel.gemm_rs import GemmRS
     from ..parallel.ag_gemm import AGGemm, control_layout
@@ -507,6 +510,7 @@ def main(argv=None):
     ap.add_argument("--comm-ctas", default="", help="gemmrs: comma list of reducer CTA counts (pull transport)")
     ap.add_argument("--tile-kinds", default="", help="gemmrs: comma list of pull GEMM tile kinds (0 single, 2 wide)")
     ap.add_argument("--world", type=int, default=8, help="fused_emulated: emulated ranks on one GPU")
+    ap.add_argument("--repeats", type=int, default=3, help="fused_emulated: calls per stage (1 for a profiler)")
     ap.add_argument("--out", type=Path)
     args = ap.parse_args(argv)
     import torch
@@ -538,7 +542,7 @@ def main(argv=None):
     elif args.op == "ag_gemm":
         rows += ag_gemm_case(rank, world, timer)
     elif args.op == "fused_emulated":
-        rows += fused_emulated_case(args.m, args.n, args.k, args.world, timer)
+        rows += fused_emulated_case(args.m, args.n, args.k, args.world, timer, repeats=args.repeats)
     elif args.op == "attention":
         rows += attention_case(rank, world, timer)
     else:

@@ -77,14 +77,20 @@ def case_ag_gemm(rank, world):
     w = (0.05 * torch.randn((n, k), generator=torch.Generator(device="cuda").manual_seed(1), device="cuda")).to(torch.bfloat16)
     full = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
     dist.all_gather_into_tensor(full, shard)
-    op = AGGemm(m, k)
-    for it in range(4):
+    op = AGGemm(m, k, n=n)
+    kind = op.tile_kind(n, 256)
+    for it in range(6):
         s = (shard * (it + 1)).to(torch.bfloat16)
         f = (full * (it + 1)).to(torch.bfloat16)
-        out = op.forward(s, w, bn=256)
+        if it % 2:  # the producer writes the shard straight into the gather buffer
+            buf = op.input_buffer()
+            buf.copy_(s)
+            s = buf
+        out = op.forward(s, w, bn=256)  # back to back: no host barrier between calls
         torch.cuda.synchronize()
         check_status()
-        require(torch.equal(op.gathered, f) and torch.equal(out, G.matmul(f, w, bn=256)), "AG->GEMM mismatch")
+        require(torch.equal(op.gathered, f) and torch.equal(out, G.matmul(f, w, bn=256, pair=kind)),
+                "AG->GEMM mismatch")
     op.close()
 
 

@@ -96,7 +96,7 @@ def test_gemm_rs_fused_residual_bias():
 
 
 @pytest.mark.parametrize("world,bn,kind", [(2, 128, 0), (4, 256, 0), (8, 256, 0), (2, 256, 2), (8, 256, 2)])
-@pytest.mark.parametrize("epi", ["plain", "bias_gelu", "mn_major"])
+@pytest.mark.parametrize("epi", ["plain", "bias_gelu", "mn_major", "in_place"])
 def test_ag_gemm_emulated(world, bn, kind, epi):
     """Pull all-gather -> GEMM, W ranks emulated on one GPU: every rank's call
     runs as three launches (own chunk + publish, pull peers, GEMM) over all ranks
@@ -124,6 +124,13 @@ def test_ag_gemm_emulated(world, bn, kind, epi):
         kw = dict(b_mn=epi == "mn_major", bn=bn)
         if epi == "bias_gelu":
             kw["bias"] = bias
+        if epi == "in_place":
+            # the shard is written straight into the own chunk (after the bounded
+            # wait input_buffer launches) and published without a copy
+            views = [ops[r].input_buffer() for r in range(world)]
+            for r in range(world):
+                views[r].copy_(shards[r])
+            shards = views
         for phase in (1, 2):
             for r in range(world):
                 ops[r].forward(shards[r], weight, phase=phase, **kw)
