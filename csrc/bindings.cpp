@@ -183,6 +183,36 @@ void gemm_rs_pull(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn
   raise_if(tn5b::gemm::run(c, stream()), "gemm_rs_pull");
 }
 
+// The reducer CTAs of the pull reduce-scatter alone (phase 2), for partials
+// that were packed and published without a GEMM (single-CTA flag tiles).  The
+// GEMM operands of the call are never read: the partial buffer stands in.
+void rs_pull_reduce_only(int64_t partial_local, int64_t partial_ptrs, int64_t flag_ptrs, int64_t my_flags,
+                         int64_t M, int64_t N, int64_t rank, int64_t world, int64_t epoch,
+                         const at::Tensor& consumer_order, at::Tensor& out, const at::Tensor& status,
+                         int64_t timeout_ns, int64_t comm_ctas) {
+  check_bf16(out, "out");
+  TORCH_CHECK(out.is_contiguous() && out.size(0) == M / world && out.size(1) == N, "out must be [M / world, N]");
+  const c10::cuda::CUDAGuard guard(out.device());
+  tn5b::gemm::GemmCall c;
+  c.A = reinterpret_cast<const void*>(partial_local); c.lda = 64;
+  c.B = reinterpret_cast<const void*>(partial_local); c.ldb = 64;
+  c.M = int(M); c.N = int(N); c.K = 64;
+  c.mode = 3; c.phase = 2; c.pair = 0;
+  c.rs_partial_local = reinterpret_cast<void*>(partial_local);
+  c.rs_partials = reinterpret_cast<const uint8_t* const*>(partial_ptrs);
+  c.rs_flags = reinterpret_cast<uint32_t* const*>(flag_ptrs);
+  c.rs_my_flags = reinterpret_cast<const uint32_t*>(my_flags);
+  c.rank = int(rank); c.world = int(world); c.epoch = uint32_t(epoch);
+  check_cuda(consumer_order, "consumer_order");
+  c.rs_consumer_order = consumer_order.data_ptr<int>();
+  c.tile_order = consumer_order.data_ptr<int>();  // not read in the reduce phase
+  c.rs_out = out.data_ptr();
+  c.status = status_ptr(status);
+  c.timeout_ns = uint64_t(timeout_ns);
+  c.comm_ctas = int(comm_ctas);
+  raise_if(tn5b::gemm::run(c, stream()), "rs_pull_reduce_only");
+}
+
 // All-gather -> GEMM, pull transport: out = epilogue(gather(shards) * B^T).
 // `gather` is this rank's symmetric gather buffer [M, K]; its gatherer CTAs
 // pull the peers' chunks into it while the GEMM CTAs consume arrived blocks
@@ -308,6 +338,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 BF16 GEMM with fused epilogue", nogil());
   m.def("gemm_rs_push", &gemm_rs_push, "tcgen05 GEMM whose epilogue pushes tiles to owners", nogil());
   m.def("gemm_rs_pull", &gemm_rs_pull, "tcgen05 GEMM with in-launch pull reduce-scatter", nogil());
+  m.def("rs_pull_reduce_only", &rs_pull_reduce_only, "pull reduce-scatter of packed, published partials", nogil());
   m.def("ag_gemm", &ag_gemm, "all-gather (in-launch pull) fused into a tcgen05 GEMM", nogil());
   m.def("sm_count", &sm_count, "number of SMs of the current device");
   m.def("fused_grid", &fused_grid, "grid of a fused GEMM launch (GEMM + communication CTAs)");

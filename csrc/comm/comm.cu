@@ -299,7 +299,46 @@ __global__ void __launch_bounds__(32) bulk_copy_kernel(uint8_t* __restrict__ dst
   }
   bulk_wait_group_all();
 }
+// Pack a row-major [M, N] BF16 tensor into the pull reduce-scatter's partial
+// layout [M/128][N/64][128][64] (16-byte units; one thread per unit).
+__global__ void __launch_bounds__(256) pack_pieces_kernel(const uint4* __restrict__ src, int64_t ld_units,
+                                                          uint4* __restrict__ dst, int M, int N) {
+  const int units_per_row = N / 8;
+  const int64_t total = int64_t(M) * units_per_row;
+  const int n_chunks = N / 64;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int r = int(i / units_per_row), u = int(i % units_per_row);
+    const int64_t piece = int64_t(r / 128) * n_chunks + u / 8;
+    dst[piece * 1024 + (r % 128) * 8 + (u % 8)] = src[int64_t(r) * ld_units + u];
+  }
+}
+
+// Release flag[source = rank][tile] = epoch on every destination, for all of
+// its flag tiles (128 rows x tile_n), after the preceding pack (stream order).
+__global__ void publish_tiles_kernel(uint32_t* const* flags, int rank, int world, int per_dest, uint32_t epoch) {
+  const int total = world * per_dest;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int d = i / per_dest, t = i % per_dest;
+    fence_acq_rel_sys();
+    st_release_sys(flags[d] + int64_t(rank) * per_dest + t, epoch);
+  }
+}
 }  // namespace
+
+int pack_pieces(const void* src, int64_t ld, void* dst, int M, int N, cudaStream_t stream) {
+  if (M % 128 || N % 64 || ld % 8 || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return -1;
+  const int64_t units = int64_t(M) * (N / 8);
+  const int grid = int(units / 256 < 148 * 8 ? (units + 255) / 256 : 148 * 8);
+  pack_pieces_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(src), ld / 8, static_cast<uint4*>(dst), M, N);
+  return int(cudaGetLastError());
+}
+
+int publish_tiles(uint32_t* const* flags, int rank, int world, int per_dest, uint32_t epoch, cudaStream_t stream) {
+  if (world < 1 || per_dest < 1) return -1;
+  publish_tiles_kernel<<<(world * per_dest + 255) / 256, 256, 0, stream>>>(flags, rank, world, per_dest, epoch);
+  return int(cudaGetLastError());
+}
 
 int bulk_copy(void* dst, const void* src, int64_t bytes, int ctas, int chunk, int stages, uint64_t timeout_ns,
               int* status, cudaStream_t stream) {

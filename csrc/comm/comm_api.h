@@ -46,5 +46,9 @@ int bulk_copy(void* dst, const void* src, int64_t bytes, int ctas, int chunk, in
               int* status, cudaStream_t stream);
 int wait_probe(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status,
                cudaStream_t stream);
+// Pull reduce-scatter of an existing tensor: pack it into the partial buffer's
+// [M/128][N/64][128][64] layout, then release its flag tiles to their owners.
+int pack_pieces(const void* src, int64_t ld, void* dst, int M, int N, cudaStream_t stream);
+int publish_tiles(uint32_t* const* flags, int rank, int world, int per_dest, uint32_t epoch, cudaStream_t stream);
 }  // namespace comm
 }  // namespace tn5b

@@ -113,6 +113,23 @@ void rs_reduce(int64_t recv, int64_t flags, int64_t slot_bytes, int64_t rank, in
   TORCH_CHECK(r == 0, "rs_reduce failed: ", r < 0 ? "bad arguments" : cudaGetErrorString(cudaError_t(r)));
 }
 
+void pack_pieces(const at::Tensor& src, int64_t dst) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16 && src.dim() == 2 && src.stride(1) == 1,
+              "pack_pieces: src must be a CUDA bf16 [M, N] with unit inner stride");
+  const c10::cuda::CUDAGuard guard(src.device());
+  const int r = tn5b::comm::pack_pieces(src.data_ptr(), src.stride(0), reinterpret_cast<void*>(dst), int(src.size(0)),
+                                        int(src.size(1)), at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(r == 0, "pack_pieces failed: ", r < 0 ? "M % 128, N % 64 and 16-byte alignment required"
+                                                    : cudaGetErrorString(cudaError_t(r)));
+}
+
+void publish_tiles(int64_t flag_ptrs, int64_t rank, int64_t world, int64_t per_dest, int64_t epoch, int64_t device) {
+  const c10::cuda::CUDAGuard guard(c10::Device(c10::kCUDA, int(device)));
+  const int r = tn5b::comm::publish_tiles(reinterpret_cast<uint32_t* const*>(flag_ptrs), int(rank), int(world),
+                                          int(per_dest), uint32_t(epoch), at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(r == 0, "publish_tiles failed");
+}
+
 void wait_probe(int64_t flag, int64_t target, int64_t timeout_ns, const at::Tensor& status) {
   const c10::cuda::CUDAGuard guard(status.device());
   const int r = tn5b::comm::wait_probe(reinterpret_cast<const uint32_t*>(flag), uint32_t(target),
@@ -132,6 +149,8 @@ void register_comm(pybind11::module& m) {
   using nogil = pybind11::call_guard<pybind11::gil_scoped_release>;
   m.def("rs_reduce", &rs_reduce, nogil());
   m.def("wait_probe", &wait_probe, nogil());
+  m.def("pack_pieces", &pack_pieces, nogil());
+  m.def("publish_tiles", &publish_tiles, nogil());
   m.def("copy_to_ptr", &copy_to_ptr, nogil());
   m.def("copy_ptr", &copy_ptr, nogil());
   m.def("bulk_copy", &bulk_copy, nogil());

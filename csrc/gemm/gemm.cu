@@ -120,7 +120,13 @@ int auto_kind(int M, int N, int K, double sms) {
   if (K < 1024 || sms < 2) return kSingle;
   const double tiles_s = double((M + 127) / 128) * double((N + 255) / 256);
   const double tiles_w = double((M + 255) / 256) * double((N + 511) / 512);
-  const double waves_s = std::ceil(tiles_s / sms), waves_w = std::ceil(tiles_w / std::floor(sms / 2));
+  const double clusters = std::floor(sms / 2);
+  const double waves_s = std::ceil(tiles_s / sms);
+  double waves_w = std::ceil(tiles_w / clusters);
+  // A partial last wave of at most half the clusters runs as CTA-pair tiles
+  // (run_split): about half a wide wave instead of a full one.
+  const double full = std::floor(tiles_w / clusters), rest = tiles_w - full * clusters;
+  if (full >= 1 && rest > 0 && 2 * rest <= clusters) waves_w = full + 0.55;
   // Per-SM work of one wave: 1 unit (128 x 256 x K) single, 2 units wide.
   const double cost_s = waves_s / kEffSingle;
   const double cost_w = 2.0 * waves_w * (1.0 + kWideEpilogueK / double(K)) / kEffWide;
@@ -134,6 +140,19 @@ int tile_kind(const GemmCall& c, int bn) {
   if (c.tile_order) return kSingle;                            // a table without a kind: single-CTA units
   const bool comm_mode = c.mode == 3 || c.ag;
   return auto_kind(c.M, c.N, c.K, double(sm_count() - (comm_mode ? c.comm_ctas : 0)));
+}
+
+// Split of a wide-tile GEMM: the main launch runs `full` waves of wide tiles,
+// a second launch runs the rest as CTA-pair 256 x 256 tiles (two per wide
+// tile) in one wave.  Returns the number of wide tiles of the main launch, or
+// 0 when the last wave is more than half full (or the shape does not allow it).
+int split_main_tiles(const GemmCall& c, int tiles_m_w, int tiles_n_w) {
+  if (c.tile_order || c.mode != 0 || c.ag || c.N % 512 || c.max_ctas > 0) return 0;
+  const int clusters = sm_count() / 2;
+  const int tiles = tiles_m_w * tiles_n_w;
+  const int full = tiles / clusters, rest = tiles - full * clusters;
+  if (full < 1 || rest == 0 || 2 * rest > clusters) return 0;
+  return full * clusters;
 }
 
 int pick_bn(const GemmCall& c) {
@@ -170,6 +189,7 @@ int tile_map(const GemmCall& c, int* out, cudaStream_t stream) {
   const bool pair = kind != kSingle;
   const int tile_n = kind == kWide ? 2 * bn : bn;
   Params p{};
+  p.tail_from = -1;
   p.M = c.M; p.N = c.N; p.K = c.K;
   p.tiles_m = (c.M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.tiles_n = (c.N + tile_n - 1) / tile_n;
@@ -242,6 +262,7 @@ int run(const GemmCall& c, cudaStream_t stream) {
   const bool pair = kind != kSingle;
   const int tile_n = kind == kWide ? 2 * bn : bn;
   Params p{};
+  p.tail_from = -1;  // only a split GEMM's tail launch decodes tiles from the main grid
   p.M = c.M; p.N = c.N; p.K = c.K;
   p.tiles_m = (c.M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.tiles_n = (c.N + tile_n - 1) / tile_n;
@@ -366,7 +387,33 @@ int run(const GemmCall& c, cudaStream_t stream) {
   }
   switch (c.mode) {
     case 0:
-      if (kind == kWide) return launch<256, 4, 64, kModeLocal, false, true, true>(c, p, ma, mb, mo, ma2, grid, stream);
+      if (kind == kWide) {
+        const int main_tiles = split_main_tiles(c, p.tiles_m, p.tiles_n);
+        if (main_tiles > 0) {
+          // Main launch: whole waves of wide tiles; tail launch: the remaining
+          // wide tiles as pairs of 256 x 256 CTA-pair tiles, one wave.
+          const int wide_m = p.tiles_m, wide_n = p.tiles_n;
+          Params main = p;
+          main.num_tiles = main_tiles;
+          main.gemm_ctas = 2 * (sm_count() / 2);
+          int r = launch<256, 4, 64, kModeLocal, false, true, true>(c, main, ma, mb, mo, ma2, main.gemm_ctas,
+                                                                    stream);
+          if (r) return r;
+          Params tail = p;
+          tail.debug = nullptr;
+          tail.cta_stamps = nullptr;
+          tail.tail_from = main_tiles;
+          tail.tail_tiles_m = wide_m;
+          tail.tail_tiles_n = wide_n;
+          tail.tiles_m = wide_m;
+          tail.tiles_n = 2 * wide_n;
+          tail.num_tiles = 2 * (wide_m * wide_n - main_tiles);
+          const int clusters = tail.num_tiles < sm_count() / 2 ? tail.num_tiles : sm_count() / 2;
+          tail.gemm_ctas = 2 * clusters;
+          return launch<256, 6, 64, kModeLocal, false, true>(c, tail, ma, mb, mo, ma2, tail.gemm_ctas, stream);
+        }
+        return launch<256, 4, 64, kModeLocal, false, true, true>(c, p, ma, mb, mo, ma2, grid, stream);
+      }
       if (pair) return launch<256, 6, 64, kModeLocal, false, true>(c, p, ma, mb, mo, ma2, grid, stream);
       if (bn == 256) return launch<256, 4, 64, kModeLocal, false>(c, p, ma, mb, mo, ma2, grid, stream);
       return launch<128, 6, 64, kModeLocal, false>(c, p, ma, mb, mo, ma2, grid, stream);

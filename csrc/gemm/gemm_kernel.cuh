@@ -122,6 +122,10 @@ struct Params {
   int M, N, K;
   int tiles_m, tiles_n, num_tiles, k_blocks;
   int group_m;                   // raster group (plain GEMMs)
+  // Tail launch of a split GEMM: linear tile t is half (t % 2) of tile
+  // tail_from + t / 2 of the main launch's grouped raster over a grid of
+  // tail_tiles_m x tail_tiles_n wide (256 x 2*BN) tiles; tail_from < 0 otherwise.
+  int tail_from, tail_tiles_m, tail_tiles_n;
   const int* tile_order;         // optional: linear tile ids (tm * tiles_n + tn)
   // epilogue
   int epi;
@@ -170,13 +174,18 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& tm, int
     tn = id % p.tiles_n;
     return;
   }
-  const int group_size = p.group_m * p.tiles_n;
-  const int group = t / group_size;
+  const bool tail = p.tail_from >= 0;
+  const int tiles_m = tail ? p.tail_tiles_m : p.tiles_m;
+  const int tiles_n = tail ? p.tail_tiles_n : p.tiles_n;
+  const int u = tail ? p.tail_from + (t >> 1) : t;
+  const int group_size = p.group_m * tiles_n;
+  const int group = u / group_size;
   const int first_m = group * p.group_m;
-  const int size_m = min(p.tiles_m - first_m, p.group_m);
-  const int r = t % group_size;
+  const int size_m = min(tiles_m - first_m, p.group_m);
+  const int r = u % group_size;
   tm = first_m + r % size_m;
   tn = r / size_m;
+  if (tail) tn = 2 * tn + (t & 1);  // the wide tile's two 256-column halves
 }
 
 __device__ __forceinline__ float bf16_round_f(float x) {

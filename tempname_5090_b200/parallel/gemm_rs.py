@@ -156,6 +156,7 @@ class GemmRS:
         if self.pull and not 1 <= self.comm_ctas <= 64:
             raise ValueError("comm_ctas must be in [1, 64]")
         self._last_operands = None
+        self._scatter_order = None
         # `device` defaults to the current CUDA device; CPU is for host-logic tests
         # (NCCL transport on Gloo ranks, or a recording stand-in for the kernels).
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -289,6 +290,56 @@ class GemmRS:
                     ws.failed = True
                 raise
             self.calls += 1
+        return out
+
+    def scatter(self, x: torch.Tensor, out=None, phase: int = 3) -> torch.Tensor:
+        """Reduce-scatter of an existing [M, N] BF16 tensor over the pull
+        transport (no GEMM): the tensor is packed into this rank's partial
+        buffer, its tiles are released to their owners, and a launch of the
+        reducer CTAs alone pulls and sums every source's rows of this rank in
+        source order (BF16 after every source).  Used for the vocab-parallel
+        embedding's SumScatter (TempName-5090 python/flux_5090/model.py:100-108).
+        phase 3: the whole call; single-GPU emulation of several ranks runs
+        phase 1 (pack + publish, opens the epoch) on every rank, then phase 2."""
+        if not self.pull:
+            raise RuntimeError("scatter needs the pull transport")
+        if x.dtype != torch.bfloat16 or tuple(x.shape) != (self.m, self.n) or x.stride(-1) != 1 \
+                or x.device != self.device:
+            raise ValueError(f"x must be a bf16 [{self.m}, {self.n}] tensor on {self.device}")
+        ws = self.workspace
+        if self.failed or ws.failed:
+            raise RuntimeError("this GemmRS operator (or one sharing its receive workspace) previously failed")
+        out = torch.empty((self.rows, self.n), dtype=torch.bfloat16, device=self.device) if out is None else out
+        per_dest = (self.rows // 128) * (self.n // TILE_N)
+        if self._scatter_order is None:
+            self._scatter_order = torch.arange(per_dest, dtype=torch.int32, device=self.device)
+        if phase not in (1, 2, 3):
+            raise ValueError("phase is 3 (one call) or 1 then 2 (emulation)")
+        with ws.lock:
+            if phase & 1:
+                if self.epoch + 2 >= 2 ** 31:
+                    raise RuntimeError("epoch exhausted; create a new operator")
+                self.epoch += 1
+            try:
+                part = ws.partials()[self.epoch & 1]
+                dev = self.device.index if self.device.index is not None else 0
+                with tracing.scope("gemm_rs.scatter"):
+                    if phase & 1:
+                        lib().pack_pieces(x, part.local)
+                        lib().publish_tiles(self.flags.ptrs.data_ptr(), self.rank, self.world, per_dest,
+                                            self.epoch, dev)
+                        count_launch(2)
+                    if phase & 2:
+                        lib().rs_pull_reduce_only(part.local, part.ptrs.data_ptr(), self.flags.ptrs.data_ptr(),
+                                                  self.flags.local, self.m, self.n, self.rank, self.world,
+                                                  self.epoch, self._scatter_order, out, self.status,
+                                                  self.timeout_ns, self.comm_ctas)
+                        count_launch()
+            except BaseException:
+                self.failed = ws.failed = True
+                raise
+            if phase & 2:
+                self.calls += 1
         return out
 
     def _check_operands(self, x, w, b_mn, residual=None, bias=None, out=None):

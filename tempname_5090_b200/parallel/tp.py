@@ -60,9 +60,14 @@ class TensorParallel:
         return out
 
     def scatter_sum(self, x: torch.Tensor) -> torch.Tensor:
-        """Plain reduce-scatter by rows (embedding SumScatter)."""
+        """Reduce-scatter by rows (the embedding's SumScatter): the pull
+        transport's reducer CTAs over NVLink, NCCL for the unfused transports."""
         if self.world == 1:
             return x.contiguous()
+        M, N = x.shape
+        if x.is_cuda and self.transport == "nvlink" and self.arm == "flux" and M % (128 * self.world) == 0 \
+                and N % 256 == 0:
+            return self.rs_operator(M, N, 8, "embed").scatter(x.contiguous())
         if x.is_cuda:
             out = torch.empty((x.shape[0] // self.world, *x.shape[1:]), dtype=x.dtype, device=x.device)
             dist.reduce_scatter_tensor(out, x.contiguous(), group=self.group)

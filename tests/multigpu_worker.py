@@ -67,6 +67,28 @@ def case_gemm_rs(rank, world):
             "TACO arms are not bitwise equal")
 
 
+def case_scatter(rank, world):
+    """TensorParallel.scatter_sum (the embedding's SumScatter) over the pull
+    transport equals NCCL reduce_scatter on embedding-like inputs (one non-zero
+    source per row), bitwise, back to back."""
+    from tempname_5090_b200.parallel.tp import TensorParallel
+    from tempname_5090_b200._native import check_status
+    tp = TensorParallel(None)
+    m, n = world * 512, 1024
+    for it in range(3):
+        g = torch.Generator(device="cuda").manual_seed(50 + it)
+        owner = torch.randint(0, world, (m,), generator=g, device="cuda")
+        x = torch.randn((m, n), generator=torch.Generator(device="cuda").manual_seed(60 + rank + 10 * it),
+                        device="cuda").to(torch.bfloat16) * (owner == rank)[:, None].to(torch.bfloat16)
+        got = tp.scatter_sum(x)
+        want = torch.empty_like(got)
+        dist.reduce_scatter_tensor(want, x)
+        torch.cuda.synchronize()
+        check_status()
+        require(torch.equal(got, want), "pull scatter differs from NCCL reduce_scatter")
+    tp.close()
+
+
 def case_ag_gemm(rank, world):
     from tempname_5090_b200.parallel.ag_gemm import AGGemm
     from tempname_5090_b200.ops import gemm as G
@@ -166,7 +188,8 @@ def case_missing_peer(rank, world):
     dist.barrier()
 
 
-CASES = dict(gemm_rs=case_gemm_rs, ag_gemm=case_ag_gemm, model=case_model, missing_peer=case_missing_peer)
+CASES = dict(gemm_rs=case_gemm_rs, ag_gemm=case_ag_gemm, model=case_model, missing_peer=case_missing_peer,
+             scatter=case_scatter)
 
 
 def main():

@@ -330,3 +330,39 @@ def test_mapping_probe_reads_back_the_host_production_order(arm, kind):
         assert len(set(host)) == len(host) == (m // op.tile_m) * (n // op.tile_n)
     for b in data + [flags]:
         b.close()
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_pull_scatter_of_an_existing_tensor(world):
+    """The embedding's SumScatter over the pull transport (pack, publish,
+    reducer-only launch): bitwise the ordered BF16 sum of the sources' rows,
+    over calls of both buffer parities."""
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    from tempname_5090_b200.ops import taco
+    from tempname_5090_b200._native import check_status
+    m, n = world * 256, 768
+    rows = m // world
+    data = [SymmetricBuffer.emulated(m * n * 2, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(world * (rows // 128) * (n // 256) * 4, world)
+    ops = [GemmRS(m, n, 8, comm_ctas=6, _emulate=(r, world, [b.as_rank(r) for b in data], flags.as_rank(r)))
+           for r in range(world)]
+    for call in range(3):
+        xs = [torch.randn((m, n), generator=_gen(9 * call + r), device="cuda").to(torch.bfloat16)
+              for r in range(world)]
+        if call == 1:  # embedding-like: each row non-zero on exactly one source
+            owner = torch.randint(0, world, (m,), generator=torch.Generator().manual_seed(5))
+            xs = [x * (owner == r).to(x.device)[:, None].to(torch.bfloat16) for r, x in enumerate(xs)]
+        for r, op in enumerate(ops):
+            op.scatter(xs[r], phase=1)
+        outs = [op.scatter(xs[r], phase=2) for r, op in enumerate(ops)]
+        torch.cuda.synchronize()
+        check_status()
+        for r in range(world):
+            local = xs[r][r * rows:(r + 1) * rows].contiguous()
+            remote = torch.cat([xs[s][r * rows:(r + 1) * rows] for s in range(world) if s != r])
+            assert torch.equal(outs[r], taco.ordered_reduce(local, remote, r, world)), (call, r)
+            if call == 1:
+                assert torch.equal(outs[r], sum(x.float() for x in xs)[r * rows:(r + 1) * rows].to(torch.bfloat16))
+    for b in data + [flags]:
+        b.close()

@@ -83,3 +83,28 @@ def test_pair_tiles_bitwise_equal_single_cta(kind):
     x = matmul(a, b, bn=256, pair=0)
     y = matmul(a, b, bn=256, pair=kind)
     assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("M,N,K", [(8192, 4096, 1024), (12288, 4096, 512), (4096, 8192, 768)])
+def test_split_wide_gemm_tail_runs_as_pair_tiles(M, N, K):
+    """A wide-tile GEMM whose last wave is at most half full runs that wave as
+    CTA-pair 256 x 256 tiles in a second launch (8192 x 4096: 3 wide waves + a
+    pair wave instead of 4 wide waves); every tile kind accumulates K in the
+    same order, so the result is bitwise the single-CTA one, with epilogues."""
+    from tempname_5090_b200.ops.gemm import matmul
+    from tempname_5090_b200._native import check_status
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+    b = (0.05 * torch.randn((N, K), generator=g, device="cuda")).to(torch.bfloat16)
+    bias = torch.randn((N,), generator=g, device="cuda").to(torch.bfloat16)
+    single = matmul(a, b, bn=256, pair=0)
+    split = matmul(a, b, bn=256, pair=2)
+    torch.cuda.synchronize()
+    check_status()
+    assert torch.equal(single, split)
+    assert _rel(split, a.float() @ b.float().t()) < 1e-2
+    aux_s = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    aux_w = torch.empty_like(aux_s)
+    assert torch.equal(matmul(a, b, bias=bias, gelu_aux=aux_s, bn=256, pair=0),
+                       matmul(a, b, bias=bias, gelu_aux=aux_w, bn=256, pair=2))
+    assert torch.equal(aux_s, aux_w)

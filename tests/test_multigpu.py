@@ -49,5 +49,10 @@ def test_tp_model_matches_single_rank(world):
     _run("model", world)
 
 
+@pytest.mark.parametrize("world", [2, 8])
+def test_pull_scatter_matches_nccl(world):
+    _run("scatter", world)
+
+
 def test_missing_peer_times_out_cleanly():
     _run("missing_peer", 2)
