@@ -8,6 +8,7 @@
 #include "gemm/gemm_api.h"
 #include "kernels/kernels_api.h"
 #include "comm/comm_api.h"
+#include "common/push_lanes.h"
 
 namespace {
 
@@ -332,6 +333,21 @@ int64_t sm_count() {
 void register_kernels(pybind11::module& m);
 void register_comm(pybind11::module& m);
 
+// The push transport's lane layout as the kernels compute it (push_lanes.h):
+// (lane_slot_bytes, recv_bytes, flag_words, flag index of every (source, local tile)).
+std::tuple<int64_t, int64_t, int64_t, at::Tensor> push_lanes_layout(int64_t rows, int64_t n, int64_t chunk_rows,
+                                                                    int64_t world, int64_t tile_n) {
+  TORCH_CHECK(chunk_rows > 0 && chunk_rows % 128 == 0 && rows % chunk_rows == 0 && n % tile_n == 0,
+              "push lanes: 128 | chunk_rows, chunk_rows | rows, tile_n | n");
+  const tn5b::PushLanes L{int(rows), int(n), int(chunk_rows), int(world), int(tile_n)};
+  const int tiles_n = int(n / tile_n), tiles = int(rows / 128) * tiles_n;
+  at::Tensor idx = at::empty({world, tiles}, at::kLong);
+  auto a = idx.accessor<int64_t, 2>();
+  for (int s = 0; s < world; ++s)
+    for (int t = 0; t < tiles; ++t) a[s][t] = L.flag_index(s, (t / tiles_n) * 128, t % tiles_n);
+  return {L.lane_slot_bytes(), L.recv_bytes(), L.flag_words(), idx};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "tempname_5090_b200 native sm_100a kernels";
   using nogil = pybind11::call_guard<pybind11::gil_scoped_release>;
@@ -341,6 +357,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rs_pull_reduce_only", &rs_pull_reduce_only, "pull reduce-scatter of packed, published partials", nogil());
   m.def("ag_gemm", &ag_gemm, "all-gather (in-launch pull) fused into a tcgen05 GEMM", nogil());
   m.def("sm_count", &sm_count, "number of SMs of the current device");
+  m.def("push_lanes_layout", &push_lanes_layout, "push transport lane layout as the kernels compute it");
   m.def("fused_grid", &fused_grid, "grid of a fused GEMM launch (GEMM + communication CTAs)");
   m.def("fused_tile_kind", &fused_tile_kind, "tile kind the wave model picks for a fused launch");
   m.def("gemm_tile_map", &gemm_tile_map, "device read-back of the GEMM tile order (mapping probe)");

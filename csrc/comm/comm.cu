@@ -1,7 +1,9 @@
 // Receiver side of the fused GEMM -> reduce-scatter and the bounded-wait probe.
 //
-// Each rank's producer GEMM pushes tile (source=s) of destination d into d's
-// slot region and release-stores flag[s][tile] = epoch on d.  This kernel runs
+// Each rank's producer GEMM pushes tile (source=s) of destination d into the
+// receive region of the tile's lane on d (lane = parity of its block within the
+// destination; push_lanes.h) and release-stores that lane's flag[s][tile] =
+// epoch on d.  This kernel runs
 // on d after its own GEMM (same stream), waits (bounded) for every source's
 // tile flag and reduces in the fixed source order 0..W-1, rounding to BF16
 // after every source ("bf16_after_each_source", src/taco/codec.cu:155-196 of
@@ -11,11 +13,12 @@
 //
 // Consumption policies:
 //   ordered   CTA c takes tiles order[c], order[c+grid], ... and blocks on each.
-//   arrival   CTAs are split over two lanes (block-within-destination parity);
-//             each scans its lane's tiles and claims whichever is fully ready
+//   arrival   CTAs are split over the two lanes; each scans its lane's tiles
+//             (its lane's flag array) and claims whichever is fully ready
 //             first (per-tile claim words tagged with the epoch).
 #include "comm_api.h"
 #include "../common/ptx.cuh"
+#include "../common/push_lanes.h"
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -65,9 +68,18 @@ __device__ __forceinline__ void decode4(uint32_t raw, float quant, float adaptiv
   for (int j = 0; j < 4; ++j) o[j] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(x[j], kNorm) / adaptive));
 }
 
-__device__ __forceinline__ bool tile_ready(const RsReduceCall& c, int tile, int tiles) {
+__device__ __forceinline__ PushLanes lanes_of(const RsReduceCall& c) {
+  return PushLanes{c.rows, c.n, c.chunk_rows, c.world, c.tile_n};
+}
+
+// Flag of source s for local tile `tile` (in its lane's flag array).
+__device__ __forceinline__ const uint32_t* tile_flag(const RsReduceCall& c, int s, int tile, int tiles_n) {
+  return c.flags + lanes_of(c).flag_index(s, (tile / tiles_n) * 128, tile % tiles_n);
+}
+
+__device__ __forceinline__ bool tile_ready(const RsReduceCall& c, int tile, int tiles_n) {
   for (int s = 0; s < c.world; ++s)
-    if (int32_t(ld_acquire_sys(c.flags + int64_t(s) * tiles + tile) - c.epoch) < 0) return false;
+    if (int32_t(ld_acquire_sys(tile_flag(c, s, tile, tiles_n)) - c.epoch) < 0) return false;
   return true;
 }
 
@@ -80,23 +92,26 @@ __device__ void reduce_tile(const RsReduceCall& c, int tile, int tiles_n) {
   const int total = 128 * groups_per_row;
   const int64_t elems = int64_t(c.chunk_rows) * c.n;
   const int64_t block_groups = elems / 128;
+  const PushLanes L = lanes_of(c);
+  const int tile_lane = L.lane_of(tm * 128);  // a tile lies inside one block
   for (int gi = warp; gi < total; gi += kWarps) {
     const int r = tm * 128 + gi / groups_per_row;
     const int col = tn * c.tile_n + (gi % groups_per_row) * 128 + lane * 4;
-    const int64_t idx = int64_t(r) * c.n + col;
+    const int64_t idx = int64_t(r) * c.n + col;                // output element
+    const int64_t lidx = int64_t(L.lane_row(r)) * c.n + col;   // element in the lane's BF16 blocks
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int s = 0; s < c.world; ++s) {
       float v[4];
-      const uint8_t* slot = c.recv + int64_t(s) * c.slot_bytes;
+      const uint8_t* slot = c.recv + L.slot_offset(tile_lane, s);
       if (s == c.rank || !c.quantized) {
-        const uint2 raw = ld_cg_v2(slot + idx * 2);
+        const uint2 raw = ld_cg_v2(slot + lidx * 2);
         const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] = __bfloat162float(h[j]);
       } else {
         const int blk = r / c.chunk_rows;
         const int64_t g = (int64_t(r % c.chunk_rows) * c.n + (col - lane * 4)) / 128;
-        const uint8_t* pkt = slot + int64_t(blk) * (elems + 8 * block_groups);
+        const uint8_t* pkt = slot + int64_t(blk >> 1) * (elems + 8 * block_groups);
         const uint32_t raw = ld_cg_u32(pkt + g * 128 + lane * 4);
         const float quant = ld_cg_f32(pkt + elems + 4 * g);
         const float adaptive = ld_cg_f32(pkt + elems + 4 * block_groups + 4 * g);
@@ -139,7 +154,7 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
       if (threadIdx.x == 0) {
         int ok = 1;
         for (int s = 0; s < c.world && ok; ++s)
-          ok = wait_flag_geq(c.flags + int64_t(s) * tiles + tile, c.epoch, c.timeout_ns, c.status,
+          ok = wait_flag_geq(tile_flag(c, s, tile, tiles_n), c.epoch, c.timeout_ns, c.status,
                              kTimeoutPeerFlag);
         s_ok = ok;
       }
@@ -191,7 +206,7 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
       if (lane_of(i) != lane_id || claimed(i)) continue;
       const int tile = c.tile_order ? c.tile_order[i] : i;
       const int dist = (w - offset % span + span) % span;
-      if (dist < best && tile_ready(c, tile, tiles)) best = dist;
+      if (dist < best && tile_ready(c, tile, tiles_n)) best = dist;
     }
     if (best != 0x7fffffff) atomicMin(&s_best, best);
     __syncthreads();
@@ -203,7 +218,7 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_kernel(const __grid_consta
         const int old = *reinterpret_cast<volatile int*>(c.claims + tile);
         // tile_ready is this thread's own acquire of the flags (monotonic epochs:
         // ready for the scanning thread implies ready here).
-        if (int32_t(uint32_t(old) - c.epoch) < 0 && tile_ready(c, tile, tiles) &&
+        if (int32_t(uint32_t(old) - c.epoch) < 0 && tile_ready(c, tile, tiles_n) &&
             atomicCAS(c.claims + tile, old, int(c.epoch)) == old)
           found = tile;
       }
@@ -375,8 +390,9 @@ int copy16(void* dst, const void* src, int64_t bytes, int ctas, cudaStream_t str
 }
 
 int rs_reduce(const RsReduceCall& c, cudaStream_t stream) {
-  if (c.rows % 128 || c.n % 128 || c.tile_n % 128 || !c.recv || !c.flags || !c.out) return -1;
-  if (c.quantized && (c.rows % c.chunk_rows)) return -1;
+  if (c.rows % 128 || c.n % c.tile_n || c.tile_n % 128 || !c.recv || !c.flags || !c.out) return -1;
+  if (c.chunk_rows <= 0 || c.chunk_rows % 128 || c.rows % c.chunk_rows) return -1;
+  if (c.slot_bytes != PushLanes{c.rows, c.n, c.chunk_rows, c.world, c.tile_n}.lane_slot_bytes()) return -1;
   if (c.arrival && !c.claims) return -1;
   const int tiles = (c.rows / 128) * ((c.n + c.tile_n - 1) / c.tile_n);
   int sms = 148;

@@ -10,9 +10,9 @@ namespace tn5b {
 namespace comm {
 
 struct RsReduceCall {
-  const uint8_t* recv = nullptr;   // this rank's slot region [world][slot_bytes]
-  const uint32_t* flags = nullptr; // this rank's flags [world][tiles]
-  int64_t slot_bytes = 0;
+  const uint8_t* recv = nullptr;   // this rank's receive regions [lane][world][slot_bytes] (push_lanes.h)
+  const uint32_t* flags = nullptr; // this rank's flags [lane][world][lane tiles]
+  int64_t slot_bytes = 0;          // one lane region of one source (PushLanes::lane_slot_bytes)
   int rank = 0, world = 1;
   int rows = 0, n = 0;             // output [rows, n] (rows = M / world)
   int tile_n = 256;                // producer tile width (flag granularity)

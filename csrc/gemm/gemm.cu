@@ -316,12 +316,15 @@ int run(const GemmCall& c, cudaStream_t stream) {
     if (!c.rs_recv || !c.rs_flags || c.world < 1 || c.M % c.world) return fail("gemm-rs: bad args");
     const int rows = c.M / c.world;
     if (rows % kBM) return fail("gemm-rs: rows per destination must be a multiple of 128");
-    if (c.mode == 2 && (rows % c.chunk_rows || c.chunk_rows % kBM || c.N % 128))
-      return fail("gemm-rs: TACO needs chunk_rows | rows, 128 | chunk_rows, 128 | N");
+    if (c.chunk_rows <= 0 || rows % c.chunk_rows || c.chunk_rows % kBM || c.N % 256)
+      return fail("gemm-rs: the push lanes need chunk_rows | rows, 128 | chunk_rows, 256 | N");
     p.rs.recv = c.rs_recv; p.rs.flags = c.rs_flags;
     p.rs.rank = c.rank; p.rs.world = c.world;
     p.rs.rows_per_dest = rows; p.rs.chunk_rows = c.chunk_rows;
-    p.rs.epoch = c.epoch; p.rs.slot_bytes = c.slot_bytes;
+    p.rs.epoch = c.epoch;
+    p.rs.lanes = PushLanes{rows, c.N, c.chunk_rows, c.world, 256};
+    if (c.slot_bytes != p.rs.lanes.lane_slot_bytes())
+      return fail("gemm-rs: slot_bytes must be one lane region of one source (push_lanes.h)");
     if (c.delay_ns > 100000000ull) return fail("gemm-rs: diagnostic delay above 100 ms");
     p.rs.delay_tile = c.delay_tile; p.rs.delay_ns = c.delay_ns;
   }

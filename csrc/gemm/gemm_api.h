@@ -38,7 +38,7 @@ struct GemmCall {
   int rank = 0, world = 1;
   int chunk_rows = 128;
   uint32_t epoch = 0;
-  int64_t slot_bytes = 0;
+  int64_t slot_bytes = 0;      // push: one lane region of one source (PushLanes::lane_slot_bytes)
   int delay_tile = -1;         // diagnostic: bounded publication delay of one tile
   uint64_t delay_ns = 0;
   // Communication role (pull transports): CTAs [gemm_ctas, grid) move data over

@@ -32,6 +32,7 @@
 #include <cstdint>
 #include "../common/ptx.cuh"
 #include "gemm_api.h"
+#include "../common/push_lanes.h"
 
 namespace tn5b {
 namespace gemm {
@@ -66,15 +67,17 @@ enum Mode : int {
 };
 
 struct RsArgs {
-  // Peer base pointers of every rank's receive slots (index = rank), each slot
-  // region laid out [source][M/W rows][N] (bf16) or [source][blocks][packet].
+  // Peer base pointers of every rank's receive regions and flags (index =
+  // rank).  Push transport: two lanes per owner (block parity), each with its
+  // own receive region [source][lane blocks] and flag array [source][lane
+  // tiles] (PushLanes, push_lanes.h).  Pull transport: flag[source * tiles_per_dest + t].
   uint8_t* const* recv;          // device array [world]
-  uint32_t* const* flags;        // device array [world]; flag[source * tiles_per_dest + t]
+  uint32_t* const* flags;        // device array [world]
   int rank, world;
   int rows_per_dest;             // M / world
-  int chunk_rows;                // TACO packet block rows (reference macroblock)
+  int chunk_rows;                // block rows (reference macroblock; lane = block parity)
   uint32_t epoch;
-  int64_t slot_bytes;            // bytes of one source slot on a receiver
+  PushLanes lanes;               // push transport layout of every owner's regions
   // Diagnostic only (never in timed paths): delay the flag publication of one
   // tile (linear id) by a bounded `delay_ns` to create artificial lane skew.
   int delay_tile;
@@ -764,12 +767,13 @@ __global__ void __launch_bounds__(kThreadsFor<MODE>, 1)
             }
             __syncwarp();
             // Receiver packet of source `rank`, block = chunk_rows x N (reference SoA layout).
+            // Packets of a lane's blocks sit back to back in its region.
             const int row_local0 = row_w - dest * p.rs.rows_per_dest;
             const int blk = row_local0 / p.rs.chunk_rows;
             const int64_t elems = int64_t(p.rs.chunk_rows) * p.N;
             const int64_t groups = elems / 128;
-            uint8_t* pkt = p.rs.recv[dest] + int64_t(p.rs.rank) * p.rs.slot_bytes +
-                           int64_t(blk) * (elems + 8 * groups);
+            uint8_t* pkt = p.rs.recv[dest] + p.rs.lanes.slot_offset(blk & 1, p.rs.rank) +
+                           int64_t(blk >> 1) * (elems + 8 * groups);
             const int rib0 = row_local0 % p.rs.chunk_rows;  // row in block of lane 0
 #pragma unroll 4
             for (int idx = lane; idx < 32 * 8; idx += 32) {
@@ -828,10 +832,12 @@ __global__ void __launch_bounds__(kThreadsFor<MODE>, 1)
             ld = p.ldo;
             row_base = row_w;
           } else {
-            base = reinterpret_cast<__nv_bfloat16*>(p.rs.recv[dest] +
-                                                    int64_t(p.rs.rank) * p.rs.slot_bytes);
+            // A 128-row tile lies inside one block (128 | chunk_rows): one lane.
+            const int row_local = row_w - dest * p.rs.rows_per_dest;
+            base = reinterpret_cast<__nv_bfloat16*>(
+                p.rs.recv[dest] + p.rs.lanes.slot_offset(p.rs.lanes.lane_of(row_local), p.rs.rank));
             ld = p.N;
-            row_base = row_w - dest * p.rs.rows_per_dest;
+            row_base = p.rs.lanes.lane_row(row_local);
           }
 #pragma unroll 4
           for (int idx = lane; idx < 32 * kUnits; idx += 32) {
@@ -877,16 +883,13 @@ __global__ void __launch_bounds__(kThreadsFor<MODE>, 1)
         // one system-scope release of flag[source][tile] = epoch on the owner.
         named_barrier_sync(1, kEpiWarps * 32);
         if (warp == kEpiFirstWarp && lane == 0) {
-          const int tiles_per_dest_m = p.rs.rows_per_dest / kBM;
-          const int local_tile = (tm - dest * tiles_per_dest_m) * p.tiles_n + tn;
+          const int row_local = tm * kBM - dest * p.rs.rows_per_dest;
           if (p.rs.delay_ns && tm * p.tiles_n + tn == p.rs.delay_tile) {
             const uint64_t t0 = globaltimer_ns();
             while (globaltimer_ns() - t0 < p.rs.delay_ns) __nanosleep(1000);
           }
           fence_acq_rel_sys();
-          st_release_sys(p.rs.flags[dest] + int64_t(p.rs.rank) * tiles_per_dest_m * p.tiles_n +
-                             local_tile,
-                         p.rs.epoch);
+          st_release_sys(p.rs.flags[dest] + p.rs.lanes.flag_index(p.rs.rank, row_local, tn), p.rs.epoch);
         }
       }
     }

@@ -4,9 +4,12 @@
 
 Transport `nvlink` (default): ONE persistent tcgen05 GEMM launch whose
 epilogue pushes every finished 128x256 tile straight into its owner's receive
-slot over NVLink (BF16, or a TACO H128/E4M3 packet for remote tiles in the
+region over NVLink (BF16, or a TACO H128/E4M3 packet for remote tiles in the
 quantized arms) and release-stores a per-(source, tile) epoch flag on the
-owner; then the owner's receiver kernel waits (bounded) on each tile's W flags
+owner.  Each owner has two lanes (block-within-destination parity, as the
+reference's two lane communicators), each with its own receive region and
+flag array (`mapping.PushLanes`, csrc/common/push_lanes.h).  Then the owner's
+receiver kernel waits (bounded) on each tile's W flags
 and reduces in source order 0..W-1 with BF16 rounding after every source,
 fusing the TACO decode and an optional residual + bias epilogue.
 Arms A/B produce tiles destination-major, C/D interleave destinations at
@@ -77,19 +80,24 @@ class _Lanes:
 class RSWorkspace:
     """Exchange buffers shared by every GemmRS operator of one (M, N) on one
     group: the tile flags and the epoch sequence, plus (allocated on first use)
-    the push transport's receive slots (2 parities x W sources) and the pull
-    transport's partial buffers (2 parities x [M, N]).  Any number of operators
-    may share it: each call is a full exchange, so the parity chain argument
-    holds across operators."""
+    the push transport's receive regions (2 parities x 2 lanes x W sources,
+    `mapping.PushLanes`) and the pull transport's partial buffers (2 parities x
+    [M, N]).  Any number of operators may share it: each call is a full
+    exchange, so the parity chain argument holds across operators.  The flag
+    array serves both transports: the pull transport's [source][flag tile] and
+    the push transport's [lane][source][lane tile] views."""
 
     def __init__(self, m: int, n: int, world: int, group=None, *, recv=None, flags=None, partial=None,
-                 device=None):
+                 device=None, chunk_rows: int = 128):
         self.m, self.n, self.world, self.group = m, n, world, group
         self.rows = m // world
-        self.slot_bytes = self.rows * n * 2
+        self.chunk_rows = chunk_rows
+        self.lanes = mapping.PushLanes(self.rows, n, chunk_rows, world, TILE_N)
+        self.slot_bytes = self.lanes.lane_slot_bytes
         self.tiles_per_dest = (self.rows // 128) * (n // TILE_N)
+        self.flag_words = max(world * self.tiles_per_dest, self.lanes.flag_words)
         if flags is None:
-            flags = SymmetricBuffer(world * self.tiles_per_dest * 4, group)
+            flags = SymmetricBuffer(self.flag_words * 4, group)
         self.recv, self.flags, self.partial = recv, flags, partial
         # A failed exchange leaves slots and flags of an unfinished epoch: every
         # operator sharing this workspace refuses further calls.  The lock keeps
@@ -104,7 +112,7 @@ class RSWorkspace:
     def slots(self):
         """Receive slots of the push transport (allocated on first use, collectively)."""
         if self.recv is None:
-            self.recv = [SymmetricBuffer(self.world * self.slot_bytes, self.group) for _ in range(2)]
+            self.recv = [SymmetricBuffer(self.lanes.recv_bytes, self.group) for _ in range(2)]
         return self.recv
 
     def partials(self):
@@ -179,7 +187,8 @@ class GemmRS:
                                           self.tile_m)
         self.consumer_order = torch.tensor(local, dtype=torch.int32, device=self.device)
         self.tiles_per_dest = (self.rows // 128) * (n // TILE_N)
-        self.slot_bytes = self.rows * n * 2
+        self.lanes = mapping.PushLanes(self.rows, n, chunk_rows, self.world, TILE_N)
+        self.slot_bytes = self.lanes.lane_slot_bytes
         self._nccl_epoch = 0
         self.calls = 0
         self.failed = False
@@ -190,8 +199,12 @@ class GemmRS:
             if _emulate is not None:
                 # (rank, world, receive slots or partial buffers [2 parities], flags)
                 bufs = dict(partial=_emulate[2]) if self.pull else dict(recv=_emulate[2])
-                workspace = RSWorkspace(m, n, self.world, flags=_emulate[3], device=self.device, **bufs)
-            self.workspace = workspace if workspace is not None else RSWorkspace(m, n, self.world, group)
+                workspace = RSWorkspace(m, n, self.world, flags=_emulate[3], device=self.device,
+                                        chunk_rows=chunk_rows, **bufs)
+            if workspace is not None and workspace.chunk_rows != chunk_rows:
+                raise ValueError("a shared RSWorkspace serves one chunk_rows (its push lanes are cut in blocks)")
+            self.workspace = workspace if workspace is not None else RSWorkspace(m, n, self.world, group,
+                                                                                 chunk_rows=chunk_rows)
         else:
             self.lanes, self.lane_streams = _Lanes.get(group)
             self.partial = torch.empty((m, n), dtype=torch.bfloat16, device=self.device)
@@ -230,6 +243,16 @@ class GemmRS:
     def flag_tiles(self) -> int:
         """Flag tiles per destination: 128 rows x tile_n columns of its rows."""
         return (self.rows // 128) * (self.n // self.tile_n)
+
+    def published_flags(self) -> torch.Tensor:
+        """This rank's flag words that a complete exchange sets, as int32: the
+        pull transport's [source][flag tile], or the push transport's two lane
+        arrays at `PushLanes.flag_indices` (padding words of a shorter lane excluded)."""
+        words = self.flags.local_view((self.workspace.flag_words,), torch.int32)
+        if self.pull:
+            return words[: self.world * self.flag_tiles]
+        idx = torch.tensor(self.lanes.flag_indices(), dtype=torch.long, device=words.device)
+        return words[idx]
 
     def device_tile_map(self) -> list:
         """Mapping probe: the (row tile, column tile) pairs this operator's GEMM

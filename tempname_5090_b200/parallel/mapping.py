@@ -183,6 +183,48 @@ def consumer_tile_order(m, n, k, world, chunk_rows, arm, rank, plan=None, tile_n
     return out
 
 
+class PushLanes:
+    """Lane layout of the push transport on each owner (the host statement of
+    `csrc/common/push_lanes.h`).  Block b of a destination (chunk_rows rows)
+    travels on lane b % 2, as the reference's per-block exchange alternates
+    between two lane communicators (python/flux_5090/runtime.py:50-56).  Every
+    lane has its own receive region [source][lane block] and flag array
+    [source][lane tile]; both lanes are sized for ceil(blocks / 2) blocks."""
+
+    def __init__(self, rows_per_dest: int, n: int, chunk_rows: int, world: int, tile_n: int = 256):
+        if chunk_rows % TILE_M or rows_per_dest % chunk_rows or n % tile_n:
+            raise ValueError("push lanes need 128 | chunk_rows, chunk_rows | rows, tile_n | N")
+        self.rows, self.n, self.chunk_rows, self.world, self.tile_n = rows_per_dest, n, chunk_rows, world, tile_n
+        self.blocks = rows_per_dest // chunk_rows
+        self.lane_blocks = (self.blocks + 1) // 2
+        self.tiles_n = n // tile_n
+        self.lane_tiles = self.lane_blocks * (chunk_rows // TILE_M) * self.tiles_n
+        self.lane_slot_bytes = self.lane_blocks * chunk_rows * n * 2
+        self.recv_bytes = 2 * world * self.lane_slot_bytes
+        self.flag_words = 2 * world * self.lane_tiles
+
+    def lane_of(self, row_local: int) -> int:
+        return (row_local // self.chunk_rows) % 2
+
+    def lane_row(self, row_local: int) -> int:
+        return (row_local // self.chunk_rows // 2) * self.chunk_rows + row_local % self.chunk_rows
+
+    def slot_offset(self, lane: int, source: int) -> int:
+        """Byte offset of `source`'s region of `lane` in a receive buffer."""
+        return (lane * self.world + source) * self.lane_slot_bytes
+
+    def flag_index(self, source: int, local_tile: int) -> int:
+        """Word of `source`'s flag for local tile (row tile * tiles_n + column tile)."""
+        row_local, tn = (local_tile // self.tiles_n) * TILE_M, local_tile % self.tiles_n
+        lane = self.lane_of(row_local)
+        return (lane * self.world + source) * self.lane_tiles + (self.lane_row(row_local) // TILE_M) * self.tiles_n + tn
+
+    def flag_indices(self) -> list:
+        """Every flag word a complete exchange sets (sources x local tiles)."""
+        tiles = (self.rows // TILE_M) * self.tiles_n
+        return [self.flag_index(s, t) for s in range(self.world) for t in range(tiles)]
+
+
 def wire_bytes(m, n, world, quantized):
     """Bytes each source sends to remote owners per projection."""
     elements = (world - 1) * (m // world) * n

@@ -81,7 +81,7 @@ def validate_operator_buffers(op, output) -> dict:
     good = bool(torch.isfinite(output).all())
     detail = []
     if op.transport == "nvlink":
-        flags = op.flags.local_view((op.world * op.flag_tiles,), torch.int32)
+        flags = op.published_flags()
         if not bool((flags == op.epoch).all()):
             good = False
             detail.append("tile flags do not all equal the call epoch")
@@ -94,7 +94,8 @@ def validate_operator_buffers(op, output) -> dict:
         good = False
         detail.append("device status word set")
     require_all(good, "operator buffer/publication validation failed: " + "; ".join(detail), op.group)
-    return dict(passed=True, tiles_checked=op.flag_tiles * op.world, mapping_probe=True,
+    return dict(passed=True, tiles_checked=op.world * (op.flag_tiles if op.pull else op.tiles_per_dest),
+                mapping_probe=True,
                 scope="untimed, rank-coordinated")
 
 

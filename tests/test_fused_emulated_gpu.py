@@ -15,21 +15,23 @@ def _gen(seed):
     return torch.Generator(device="cuda").manual_seed(seed)
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world,blocks", [(2, 2), (4, 2), (8, 2), (2, 3), (8, 3)])
 @pytest.mark.parametrize("arm", ["flux", "flux_taco", "flux_taco_interleaved", "flux_taco_interleaved_arrival"])
-def test_gemm_rs_emulated_bitwise(world, arm):
+def test_gemm_rs_emulated_bitwise(world, blocks, arm):
+    """Every arm against an ordered reduce / decode_reduce of the partials.
+    An odd block count per destination leaves lane 1 one block shorter than
+    lane 0 (push transport)."""
     from tempname_5090_b200.parallel.gemm_rs import GemmRS
     from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
-    from tempname_5090_b200.parallel import planning
+    from tempname_5090_b200.parallel import planning, mapping
     from tempname_5090_b200.ops import gemm as G, taco
     from tempname_5090_b200._native import check_status
     chunk = 128
-    m, n, k = world * 256, 512, 320
+    m, n, k = world * blocks * chunk, 512, 320
     rows = m // world
-    slot = rows * n * 2
-    tiles = (rows // 128) * (n // 256)
-    recv = [SymmetricBuffer.emulated(world * slot, world) for _ in range(2)]
-    flags = SymmetricBuffer.emulated(world * tiles * 4, world)
+    lanes = mapping.PushLanes(rows, n, chunk, world)
+    recv = [SymmetricBuffer.emulated(lanes.recv_bytes, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(max(lanes.flag_words, world * (rows // 128) * (n // 256)) * 4, world)
     plan = None
     if arm.endswith("arrival"):
         order = planning.candidates(m, n, k, world, chunk)[1]["arrival_order"]
@@ -68,14 +70,62 @@ def test_gemm_rs_emulated_bitwise(world, arm):
         xs = [(x * 0.5 + 0.25).to(torch.bfloat16) for x in xs]
 
 
+@pytest.mark.parametrize("blocks", [2, 3])
+def test_push_lanes_have_their_own_regions_and_flags(blocks):
+    """Push transport, W=2 emulated, BF16 arm: after both producers ran (no
+    receiver yet), each owner's lane l holds exactly the rows of its blocks
+    2j + l from each source (lane region [source][lane block]) and that lane's
+    flag array has the epoch at the lane's tiles; padding of a shorter lane
+    stays untouched."""
+    from tempname_5090_b200.parallel.gemm_rs import GemmRS
+    from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
+    from tempname_5090_b200.parallel.mapping import PushLanes
+    from tempname_5090_b200.ops import gemm as G
+    from tempname_5090_b200._native import check_status
+    world, chunk, n, k = 2, 128, 512, 192
+    m = world * blocks * chunk
+    rows = m // world
+    lanes = PushLanes(rows, n, chunk, world)
+    recv = [SymmetricBuffer.emulated(lanes.recv_bytes, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(lanes.flag_words * 4, world)
+    ops = [GemmRS(m, n, k, arm="flux", pull=False, chunk_rows=chunk,
+                  _emulate=(r, world, [b.as_rank(r) for b in recv], flags.as_rank(r))) for r in range(world)]
+    xs = [torch.randn((m, k), generator=_gen(30 + r), device="cuda").to(torch.bfloat16) for r in range(world)]
+    ws = [torch.randn((n, k), generator=_gen(40 + r), device="cuda").to(torch.bfloat16) for r in range(world)]
+    for op in ops:
+        op.begin()
+    for r, op in enumerate(ops):
+        op.push(xs[r], ws[r])
+    torch.cuda.synchronize()
+    check_status()
+    parts = [G.matmul(xs[s], ws[s], bn=256) for s in range(world)]
+    parity = ops[0].epoch & 1
+    for r in range(world):
+        region = recv[parity].as_rank(r).local_view((lanes.recv_bytes // 2,), torch.bfloat16)
+        words = flags.as_rank(r).local_view((lanes.flag_words,), torch.int32)
+        expect_flags = torch.zeros_like(words)
+        expect_flags[torch.tensor(lanes.flag_indices(), device=words.device)] = ops[r].epoch
+        assert torch.equal(words, expect_flags), (blocks, r)
+        for lane in range(2):
+            for s in range(world):
+                off = lanes.slot_offset(lane, s)
+                slot = region[off // 2: off // 2 + lanes.lane_slot_bytes // 2].view(-1, n)
+                for j, b in enumerate(range(lane, blocks, 2)):
+                    got = slot[j * chunk:(j + 1) * chunk]
+                    want = parts[s][r * rows + b * chunk: r * rows + (b + 1) * chunk]
+                    assert torch.equal(got, want), (blocks, r, lane, s, b)
+
+
 def test_gemm_rs_fused_residual_bias():
     from tempname_5090_b200.parallel.gemm_rs import GemmRS
     from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
     from tempname_5090_b200.ops import gemm as G, taco
+    from tempname_5090_b200.parallel.mapping import PushLanes
     world, m, n, k = 2, 512, 256, 128
     rows = m // world
-    recv = [SymmetricBuffer.emulated(world * rows * n * 2, world) for _ in range(2)]
-    flags = SymmetricBuffer.emulated(world * (rows // 128) * (n // 256) * 4, world)
+    lanes = PushLanes(rows, n, 128, world)
+    recv = [SymmetricBuffer.emulated(lanes.recv_bytes, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(lanes.flag_words * 4, world)
     ops = [GemmRS(m, n, k, _emulate=(r, world, [b.as_rank(r) for b in recv], flags.as_rank(r))) for r in range(world)]
     xs = [torch.randn((m, k), generator=_gen(r), device="cuda").to(torch.bfloat16) for r in range(world)]
     ws = [torch.randn((n, k), generator=_gen(9 + r), device="cuda").to(torch.bfloat16) for r in range(world)]
@@ -283,11 +333,13 @@ def test_guard_regions_stay_intact_and_detect_an_overrun(arm):
     from tempname_5090_b200.parallel.gemm_rs import GemmRS
     from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
     from tempname_5090_b200._native import check_status, lib
+    from tempname_5090_b200.parallel.mapping import PushLanes
     world, m, n, k = 4, 1024, 512, 256
     rows = m // world
     g = 4096
-    recv = [SymmetricBuffer(world * rows * n * 2, guard_bytes=g, _emulate_world=world) for _ in range(2)]
-    flags = SymmetricBuffer(world * (rows // 128) * (n // 256) * 4, guard_bytes=g, _emulate_world=world)
+    lanes = PushLanes(rows, n, 128, world)
+    recv = [SymmetricBuffer(lanes.recv_bytes, guard_bytes=g, _emulate_world=world) for _ in range(2)]
+    flags = SymmetricBuffer(lanes.flag_words * 4, guard_bytes=g, _emulate_world=world)
     ops = [GemmRS(m, n, k, arm=arm, _emulate=(r, world, [b.as_rank(r) for b in recv], flags.as_rank(r)))
            for r in range(world)]
     xs = [torch.randn((m, k), generator=_gen(r), device="cuda").to(torch.bfloat16) for r in range(world)]

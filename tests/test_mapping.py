@@ -105,3 +105,43 @@ def test_rotated_push_order_is_a_permutation_keeping_within_destination_order(ar
         if arm == "flux":
             assert rot[-1] // cols // per_dest == rank  # own rows last
     assert len(firsts) == world  # every rank starts on a different destination
+
+
+@pytest.mark.parametrize("rows,n,chunk,world", [(256, 512, 128, 2), (384, 512, 128, 2), (1024, 4096, 256, 8),
+                                                (640, 768, 128, 4), (128, 256, 128, 8)])
+def test_push_lanes_layout(rows, n, chunk, world):
+    """Block b of a destination travels on lane b % 2; each lane's flag array
+    holds its own tiles only, every (source, tile) has its own word, and lane
+    rows pack the lane's blocks in block order."""
+    lanes = mp.PushLanes(rows, n, chunk, world)
+    tiles_n = n // 256
+    tiles = (rows // 128) * tiles_n
+    idx = lanes.flag_indices()
+    assert len(set(idx)) == world * tiles and max(idx) < lanes.flag_words
+    for s in range(world):
+        for t in range(tiles):
+            row = (t // tiles_n) * 128
+            lane = (row // chunk) % 2
+            word = lanes.flag_index(s, t)
+            assert (lane * world + s) * lanes.lane_tiles <= word < (lane * world + s + 1) * lanes.lane_tiles
+    seen = {0: [], 1: []}
+    for row in range(0, rows, 128):
+        seen[lanes.lane_of(row)].append(lanes.lane_row(row))
+    for lane in (0, 1):
+        assert seen[lane] == list(range(0, 128 * len(seen[lane]), 128))
+        assert len(seen[lane]) * 128 * n * 2 <= lanes.lane_slot_bytes
+    assert lanes.recv_bytes == 2 * world * lanes.lane_slot_bytes >= world * rows * n * 2
+
+
+@pytest.mark.parametrize("rows,n,chunk,world", [(256, 512, 128, 2), (384, 512, 128, 2), (1024, 4096, 256, 8),
+                                                (640, 768, 128, 4)])
+def test_push_lanes_host_statement_matches_kernel_arithmetic(rows, n, chunk, world):
+    """The host's PushLanes and the header the kernels compile (push_lanes.h,
+    evaluated on the host through the extension) agree word for word."""
+    from tempname_5090_b200 import _native
+    if not _native.available():
+        pytest.skip("native extension not built")
+    slot, recv, words, idx = _native.lib().push_lanes_layout(rows, n, chunk, world, 256)
+    lanes = mp.PushLanes(rows, n, chunk, world)
+    assert (slot, recv, words) == (lanes.lane_slot_bytes, lanes.recv_bytes, lanes.flag_words)
+    assert idx.flatten().tolist() == lanes.flag_indices()

@@ -91,10 +91,12 @@ def test_fused_gemm_epilogue_packets_match_reference_encoder(ref):
     from tempname_5090_b200.parallel.gemm_rs import GemmRS
     from tempname_5090_b200.parallel.symmetric import SymmetricBuffer
     from tempname_5090_b200.ops import gemm as G
-    world, m, n, k, chunk = 2, 512, 512, 384, 128
+    from tempname_5090_b200.parallel.mapping import PushLanes
+    world, m, n, k, chunk = 2, 768, 512, 384, 128
     rows = m // world
-    recv = [SymmetricBuffer.emulated(world * rows * n * 2, world) for _ in range(2)]
-    flags = SymmetricBuffer.emulated(world * (rows // 128) * (n // 256) * 4, world)
+    lanes = PushLanes(rows, n, chunk, world)
+    recv = [SymmetricBuffer.emulated(lanes.recv_bytes, world) for _ in range(2)]
+    flags = SymmetricBuffer.emulated(lanes.flag_words * 4, world)
     op = GemmRS(m, n, k, arm="flux_taco", chunk_rows=chunk,
                 _emulate=(0, world, [b.as_rank(0) for b in recv], flags.as_rank(0)))
     g = torch.Generator(device="cuda").manual_seed(5)
@@ -106,10 +108,12 @@ def test_fused_gemm_epilogue_packets_match_reference_encoder(ref):
     partial = G.matmul(x, w, bn=256)
     pbytes = chunk * n // 128 * 136
     parity = op.epoch & 1
-    slot = recv[parity].view(1, (rows * n * 2,), torch.uint8)  # rank 1's slot of source 0
+    region = recv[parity].view(1, (lanes.recv_bytes,), torch.uint8)  # rank 1's receive regions
     for blk in range(rows // chunk):
+        # block blk of source 0 sits in lane blk % 2, packet blk // 2 of that lane
+        start = lanes.slot_offset(blk % 2, 0) + (blk // 2) * pbytes
         block = partial[rows + blk * chunk: rows + (blk + 1) * chunk].contiguous()
         theirs = torch.empty(pbytes, dtype=torch.uint8, device="cuda")
         assert ref.flux_5090_encode(block.data_ptr(), theirs.data_ptr(), block.numel(), _stream()) == 0
         torch.cuda.synchronize()
-        assert torch.equal(slot[blk * pbytes:(blk + 1) * pbytes], theirs)
+        assert torch.equal(region[start:start + pbytes], theirs)
