@@ -2,26 +2,28 @@
 // head_dim 128, BF16 in/out, FP32 softmax statistics.
 //
 // One CTA per (128-query tile, batch*head); heavy (late) query tiles first.
-//   warp 0     TMA producer: the Q tile once, then K_j and V_j (128 keys each)
-//              through a 2-stage ring.  Q/K/V are read in place from the fused
-//              QKV buffer [tokens, 3*heads*128] with one 2-D tensor map.
+//   warp 0     TMA producer: the Q tile once, then K_j (3-stage ring, up to two
+//              blocks ahead) and V_j (2-stage ring), 128 keys each.  Q/K/V are
+//              read in place from the fused QKV buffer [tokens, 3*heads*128]
+//              with one 2-D tensor map.
 //   warp 1     MMA issuer: S_j = Q K_j^T into one of two TMEM buffers
-//              (M=128, N=128, K=16 x 8), then O += P_{j-1} V_{j-1} with the
-//              A operand (P, BF16) read from TMEM and V as an MN-major smem
-//              operand -- S_{j} is issued before PV_{j-1} so the softmax of
+//              (M=128, N=128, K=16 x 8), then O_h += P_{j-1,h} V_{j-1,h} for the
+//              two key halves h (A operand P, BF16, read from TMEM; V as an
+//              MN-major smem operand), each half issued as soon as its softmax
+//              warps are done -- S_j is issued before PV_{j-1} so the softmax of
 //              block j overlaps the tensor work of block j-1.
-//   warps 2-9  softmax: two warps per TMEM lane quarter, each owning 64 of the
-//              128 score columns of its rows (row = TMEM lane); loads its scores,
-//              applies the causal mask on the diagonal block, exchanges
-//              half-row maxima (and at the end the partial row sums) with its
-//              partner warp through a bounded mbarrier handshake, keeps a
-//              running max in the log2 domain and rescales O in TMEM only when the
-//              max grows by more than 2^8 (otherwise the stale max is exact:
-//              numerator and denominator share it), writes P = exp2(s - m) as
-//              packed BF16 into the first half of its own 64 score columns
-//              (the PV MMA addresses those chunks), and finally normalises O
-//              and writes O (BF16) and the row LSE (natural log).
-// TMEM: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+//   warps 2-9  softmax: two warps per TMEM lane quarter, warp `half` owning key
+//              columns [64*half, +64) of every block with its own running max
+//              (log2 domain), row sum and accumulator O_half, so the two never
+//              synchronise inside the loop; O_half is rescaled in TMEM only when
+//              its max grows by more than 2^8 (a stale max is exact: numerator
+//              and denominator share it); P = exp2(s - m) is written as packed
+//              BF16 into the first half of the warp's own 64 score columns (the
+//              PV MMA addresses those chunks).  At the end the two warps swap
+//              (m, l) once and each writes 64 columns of
+//              O = (O_0 2^(m_0-m) + O_1 2^(m_1-m)) / (l_0 2^(m_0-m) + l_1 2^(m_1-m))
+//              (BF16) plus the row LSE (natural log).
+// TMEM: S0 [0,128), S1 [128,256), O_0 [256,384), O_1 [384,512) of 512 columns.
 // Every wait is bounded; on a timeout the status word is set and the CTA exits.
 // Semantics: causal scaled_dot_product_attention (TempName-5090 model.py:255).
 #include "kernels_api.h"
@@ -38,13 +40,19 @@ constexpr int kD = 128;
 constexpr int kBlk = 128;
 constexpr int kThreads = 320;    // warp 0 TMA, warp 1 MMA, warps 2-9 elementwise (2 per TMEM lane quarter)
 constexpr int kEwWarps = 8;
+// Backward: no running max to share, so four elementwise warps per TMEM lane
+// quarter, one per 32-column quarter of the score block (more warps to hide
+// the TMEM-load, exp2 and shared-memory latencies of the elementwise pass).
+constexpr int kBwdEwWarps = 16;
+constexpr int kBwdThreads = 64 + 32 * kBwdEwWarps;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;
 
 constexpr int kSmQ = 0;               // 2 x 16 KB (d chunks)
-constexpr int kSmK = 32768;           // 2 stages x 32 KB
-constexpr int kSmV = 32768 * 3;       // 2 stages x 32 KB
-constexpr int kSmBar = 32768 * 5;
+constexpr int kKStages = 3;
+constexpr int kSmK = 32768;           // kKStages stages x 32 KB
+constexpr int kSmV = 32768 * 4;       // 2 stages x 32 KB
+constexpr int kSmBar = 32768 * 6;
 constexpr int kSmTotal = kSmBar + 256 + 1024;
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -110,14 +118,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kSmBar);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = bars + 3;
-  uint64_t* k_empty = bars + 5;
-  uint64_t* v_empty = bars + 7;
-  uint64_t* s_full = bars + 9;
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* k_full = bars + 1;   // kKStages
+  uint64_t* v_full = bars + 4;
+  uint64_t* k_empty = bars + 6;  // kKStages
+  uint64_t* v_empty = bars + 9;
+  uint64_t* s_full = bars + 11;
+  uint64_t* p_full = bars + 13;  // [score buffer][half]
+  uint64_t* o_done = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   __shared__ uint64_t xbar[4];  // per lane quarter: the two softmax warps' handshake
 
@@ -138,13 +146,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKStages; ++i) {
       mbar_init(k_full + i, 1);
-      mbar_init(v_full + i, 1);
       mbar_init(k_empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(v_full + i, 1);
       mbar_init(v_empty + i, 1);
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, kEwWarps);
+      mbar_init(p_full + 2 * i, kEwWarps / 2);
+      mbar_init(p_full + 2 * i + 1, kEwWarps / 2);
     }
     mbar_init(o_done, 1);
     for (int i = 0; i < 4; ++i) mbar_init(xbar + i, 2);
@@ -168,15 +179,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(q_full, 32768);
       tma_load_2d(sm + kSmQ, &tq, q_full, h * kD, row0 + q0);
       tma_load_2d(sm + kSmQ + 16384, &tq, q_full, h * kD + 64, row0 + q0);
-      for (int j = 0; j < nkb; ++j) {
+      // K runs up to two blocks ahead of V: K_{j+2} only waits for S_{j-1}
+      // (early), V_j waits for PV_{j-2} (after the softmax of block j-2), so a
+      // K load is never queued behind a V wait.
+      int kn = 0;  // next K block to load
+      bool ok = true;
+      for (int j = 0; j < nkb && ok; ++j) {
+        for (; kn < nkb && kn <= j + kKStages - 1; ++kn) {
+          const int ks = kn % kKStages;
+          if (!mbar_wait(k_empty + ks, ((kn / kKStages) & 1) ^ 1, timeout_ns, status, kTimeoutProducerEmpty,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          trace_put(tr, 1, kn + 1);
+          mbar_arrive_expect_tx(k_full + ks, 32768);
+          uint8_t* kdst = sm + kSmK + ks * 32768;
+          tma_load_2d(kdst, &tq, k_full + ks, (H + h) * kD, row0 + kn * kBlk);
+          tma_load_2d(kdst + 16384, &tq, k_full + ks, (H + h) * kD + 64, row0 + kn * kBlk);
+        }
+        if (!ok) break;
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(k_empty + st, ph ^ 1, timeout_ns, status, kTimeoutProducerEmpty, abort_flag)) break;
-        trace_put(tr, 1, j + 1);
-        mbar_arrive_expect_tx(k_full + st, 32768);
-        uint8_t* kdst = sm + kSmK + st * 32768;
-        tma_load_2d(kdst, &tq, k_full + st, (H + h) * kD, row0 + j * kBlk);
-        tma_load_2d(kdst + 16384, &tq, k_full + st, (H + h) * kD + 64, row0 + j * kBlk);
         if (!mbar_wait(v_empty + st, ph ^ 1, timeout_ns, status, kTimeoutProducerEmpty, abort_flag)) break;
         mbar_arrive_expect_tx(v_full + st, 32768);
         uint8_t* vdst = sm + kSmV + st * 32768;
@@ -189,34 +213,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
       const uint32_t idesc_o = make_idesc_bf16(128, 128, 0, 1);
       bool ok = mbar_wait(q_full, 0, timeout_ns, status, kTimeoutMmaFull, abort_flag);
+      // PV of block i, one half of the keys at a time: O_h += P_h V_h, issued
+      // as soon as the four softmax warps of half h have written P_h.
       auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(p_full + (i & 1), (i >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) return false;
         if (!mbar_wait(v_full + (i & 1), (i >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) return false;
-        tc_fence_after();
         const uint32_t vb = smem_u32(sm + kSmV + (i & 1) * 32768);
         const uint32_t p_tmem = tmem + uint32_t((i & 1) * 128);
+        for (int hh = 0; hh < 2; ++hh) {
+          if (!mbar_wait(p_full + 2 * (i & 1) + hh, (i >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag))
+            return false;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 256, p_tmem + packed_col(kk), mnmajor_desc(vb, kk), idesc_o,
-                          (i > 0 || kk > 0) ? 1u : 0u);
+          for (int k4 = 0; k4 < 4; ++k4)
+            umma_f16_tmem_a(tmem + 256 + hh * 128, p_tmem + packed_col(hh * 4 + k4), mnmajor_desc(vb, hh * 4 + k4),
+                            idesc_o, (i > 0 || k4 > 0) ? 1u : 0u);
+        }
         umma_commit(v_empty + (i & 1));
         umma_commit(o_done);
         return true;
       };
       for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(k_full + st, (j >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
+        const int st = j & 1, ks = j % kKStages;
+        if (!mbar_wait(k_full + ks, (j / kKStages) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // S_j overwrites the buffer whose P_{j-2} the PV MMAs of block j-2 read
+        // from TMEM.  MMAs with different accumulators may overlap in the
+        // tensor pipe, and an MMA's TMEM A-operand reads are not ordered with a
+        // later MMA's accumulator writes, so wait until PV_{j-2} has completed.
+        if (j >= 2 && !mbar_wait(o_done, (j - 2) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         trace_put(tr, 2, j + 1);
-        const uint32_t kb = smem_u32(sm + kSmK + st * 32768);
+        const uint32_t kb = smem_u32(sm + kSmK + ks * 32768);
         const uint32_t d = tmem + uint32_t(st * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_f16(d, kmajor_desc(sQ, kk), kmajor_desc(kb, kk), idesc_s, kk > 0 ? 1u : 0u);
-        umma_commit(k_empty + st);
+        umma_commit(k_empty + ks);
         umma_commit(s_full + st);
         if (j >= 1) ok = issue_pv(j - 1);
       }
@@ -226,24 +263,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------- softmax
-    // Two warps per TMEM lane quarter: `half` selects columns [64*half, 64*half+64).
+    // Two warps per TMEM lane quarter: `half` owns score columns [64*half, +64)
+    // -- half of each key block -- with its own running max, row sum and
+    // accumulator O_half (TMEM columns 256 + 128*half), so the two warps never
+    // wait for each other inside the loop.  They combine once at the end:
+    //   O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)).
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
+    const uint32_t o_col = uint32_t(256 + half * 128);
     const float sl2 = scale * kLog2e;
-    // Partner handshake per lane quarter: double-buffered slots, bounded waits.
-    __shared__ float xchg[2][2][128];  // [slot][half][row]
-    float m_run = -INFINITY, l = 0.f;  // m_run in log2 units; l = this half's partial row sum
+    __shared__ float xchg[2][2][128];  // [m, l][half][row]
+    float m_run = -INFINITY, l = 0.f;  // m_run in log2 units (-inf: no unmasked score yet)
     bool ok = true;
-    auto exchange = [&](int step, float mine, float& other) -> bool {
-      xchg[step & 1][half][row] = mine;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(xbar + q);
-      if (!warp_wait(xbar + q, step & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) return false;
-      other = xchg[step & 1][half ^ 1][row];
-      return true;
-    };
     for (int j = 0; j < nkb; ++j) {
       if (!warp_wait(s_full + (j & 1), (j >> 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
         ok = false;
@@ -272,22 +305,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (diag && half * 64 + c > row) x[c] = -INFINITY;  // raw-score max: scale > 0 keeps the order
         mxa[c & 7] = fmaxf(mxa[c & 7], x[c]);
       }
-      float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                       fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-      // Exchange the half-row maxima with the partner warp of this lane quarter.
-      float other_mx;
-      if (!exchange(j, mx, other_mx)) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(mx, other_mx) * sl2;
+      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7]))) * sl2;
       // Lazy rescale, decided per row but executed by the whole warp (the TMEM
       // load/store are warp-collective): rows that keep their max scale by 1.
       const bool grow = mx > m_run + kRescale;
       if (__any_sync(0xffffffffu, grow)) {
         const float m_new = grow ? mx : m_run;
         if (j > 0) {
-          const float factor = grow ? ex2(m_run - m_new) : 1.f;
+          const float factor = grow ? ex2(m_run - m_new) : 1.f;  // 0 while m_run = -inf (O_h row is 0)
           l *= factor;
           if (!warp_wait(o_done, (j - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
             ok = false;
@@ -296,8 +322,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           uint32_t r[32];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const uint32_t addr = tmem + lane_base + uint32_t(256 + half * 64 + c * 32);
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t addr = tmem + lane_base + o_col + uint32_t(c * 32);
             tmem_ld_32x32b_x32(addr, r);
             tmem_wait_ld();
 #pragma unroll
@@ -308,14 +334,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         m_run = m_new;
       }
+      // A half-row with every score masked so far (the diagonal block's upper
+      // half of the first query tile) keeps m_run = -inf: its P is 0.
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;
       float suma[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) suma[a] = 0.f;
       uint32_t w[32];
 #pragma unroll
       for (int c = 0; c < 64; c += 2) {
-        const float p0 = ex2(fmaf(x[c], sl2, -m_run));
-        const float p1 = ex2(fmaf(x[c + 1], sl2, -m_run));
+        const float p0 = ex2(fmaf(x[c], sl2, -m_use));
+        const float p1 = ex2(fmaf(x[c + 1], sl2, -m_use));
         suma[c & 7] += p0;
         suma[(c + 1) & 7] += p1;
         w[c / 2] = pack2(p0, p1);
@@ -327,33 +356,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(p_full + (j & 1));
+        mbar_arrive(p_full + 2 * (j & 1) + half);
         trace_put(tr, 1 + warp, j + 1);
       }
     }
-    // Final: combine the two half-row sums, normalise this half's O columns.
-    float other_l = 0.f;
-    if (ok) ok = exchange(nkb, l, other_l);
-    const float ltot = l + other_l;
+    // Final: exchange (m, l) with the partner warp of this lane quarter, then
+    // each warp writes d columns [64*half, +64) from both accumulators.
+    float other_m = -INFINITY, other_l = 0.f;
+    if (ok) {
+      xchg[0][half][row] = m_run;
+      xchg[1][half][row] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xbar + q);
+      ok = warp_wait(xbar + q, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag);
+      if (ok) {
+        other_m = xchg[0][half ^ 1][row];
+        other_l = xchg[1][half ^ 1][row];
+      }
+    }
     if (ok && warp_wait(o_done, (nkb - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
       tc_fence_after();
-      const float inv = 1.f / ltot;
+      const float m_tot = fmaxf(m_run, other_m);  // finite: column 0 of every row is unmasked
+      const float w_me = ex2(m_run - m_tot), w_other = ex2(other_m - m_tot);
+      const float l_tot = l * w_me + other_l * w_other;
+      const float inv = 1.f / l_tot;
+      const float w0 = (half == 0 ? w_me : w_other) * inv, w1 = (half == 0 ? w_other : w_me) * inv;
       const int qidx = q0 + row;
-      if (half == 0) lse[int64_t(bh) * S + qidx] = (m_run + log2f(ltot)) / kLog2e;
+      if (half == 0) lse[int64_t(bh) * S + qidx] = (m_tot + log2f(l_tot)) / kLog2e;
       // Stage 32 rows x 64 columns (128 B per row) of this warp through smem (Q tile is dead).
       uint8_t* stg = sm + kSmQ + (q * 2 + half) * 4096;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + uint32_t(256 + half * 64 + c * 32), r);
+        uint32_t r0[32], r1[32];
+        const uint32_t col = uint32_t(half * 64 + c * 32);
+        tmem_ld_32x32b_x32(tmem + lane_base + 256 + col, r0);
+        tmem_ld_32x32b_x32(tmem + lane_base + 384 + col, r1);
         tmem_wait_ld();
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = fmaf(__uint_as_float(r0[i]), w0, __uint_as_float(r1[i]) * w1);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint4 pk;
-          pk.x = pack2(__uint_as_float(r[8 * u + 0]) * inv, __uint_as_float(r[8 * u + 1]) * inv);
-          pk.y = pack2(__uint_as_float(r[8 * u + 2]) * inv, __uint_as_float(r[8 * u + 3]) * inv);
-          pk.z = pack2(__uint_as_float(r[8 * u + 4]) * inv, __uint_as_float(r[8 * u + 5]) * inv);
-          pk.w = pack2(__uint_as_float(r[8 * u + 6]) * inv, __uint_as_float(r[8 * u + 7]) * inv);
+          pk.x = pack2(o[8 * u + 0], o[8 * u + 1]);
+          pk.y = pack2(o[8 * u + 2], o[8 * u + 3]);
+          pk.z = pack2(o[8 * u + 4], o[8 * u + 5]);
+          pk.w = pack2(o[8 * u + 6], o[8 * u + 7]);
           const int unit = c * 4 + u;  // 8 units of 16 B per 64-column row
           *reinterpret_cast<uint4*>(stg + lane * 128 + ((unit ^ (lane & 7)) << 4)) = pk;
         }
@@ -399,18 +447,19 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
-// Elementwise pass over half (`half`) of one 128-column score row pair held in
-// TMEM: reads S (cols s_col+64*half..+64) and dP (dp_col+64*half..+64) and
-// writes P / dS as packed BF16 into the first 32 of those same 64 columns, so
-// the two warps sharing a lane quarter never touch each other's columns.  The
-// MMA reads packed chunk kk (16 BF16 values) at column packed_col(kk).
+// Elementwise pass over one 32-column quarter (`quarter`) of a 128-column
+// score row held in TMEM: reads S (cols s_col+32*quarter..+32) and dP
+// (dp_col+32*quarter..+32) and writes P / dS as packed BF16 into the first 16
+// of those same 32 columns, so the four warps sharing a lane quarter never
+// touch each other's columns.  The MMA reads packed chunk kk (16 BF16 values)
+// at column bwd_packed_col(kk).
 // kColumnStats: per-column LSE/D from smem (dK/dV kernel) or per-row values.
+__device__ __forceinline__ uint32_t bwd_packed_col(int kk) { return uint32_t((kk >> 1) * 32 + (kk & 1) * 8); }
 template <bool kColumnStats>
 __device__ __forceinline__ void softmax_grad_row(uint32_t tmem, uint32_t lane_base, uint32_t s_col, uint32_t dp_col,
                                                  float sl2, const float* lse_s, const float* d_s, float lse_row2,
-                                                 float d_row, int row, bool diag, bool write_p, int half) {
-#pragma unroll 1
-  for (int quarter = 2 * half; quarter < 2 * half + 2; ++quarter) {
+                                                 float d_row, int row, bool diag, bool write_p, int quarter) {
+  {
     uint32_t rs[32], rd[32];
     tmem_ld_32x32b_x32(tmem + lane_base + s_col + quarter * 32, rs);
     tmem_ld_32x32b_x32(tmem + lane_base + dp_col + quarter * 32, rd);
@@ -434,7 +483,7 @@ __device__ __forceinline__ void softmax_grad_row(uint32_t tmem, uint32_t lane_ba
       wp[i / 2] = pack2(pp[0], pp[1]);
       wd[i / 2] = pack2(dd[0], dd[1]);
     }
-    const uint32_t packed = uint32_t(half * 64 + (quarter & 1) * 16);
+    const uint32_t packed = uint32_t(quarter * 32);
     if (write_p) tmem_st_32x32b_x16(tmem + lane_base + s_col + packed, wp);
     tmem_st_32x32b_x16(tmem + lane_base + dp_col + packed, wd);
   }
@@ -470,7 +519,7 @@ __device__ __forceinline__ void store_tmem_rows(uint32_t tmem_row, float mul, ui
   __syncwarp();
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                             const float* __restrict__ lse, const float* __restrict__ Dvec,
                             __nv_bfloat16* __restrict__ dqkv, int64_t ld_dqkv, int S, int H, float scale,
@@ -490,7 +539,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 5;
   uint64_t* p_full = bars + 6;
   uint64_t* done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* mma_done = bars + 8;  // dV/dK MMAs of a block completed (they read P^T, dS^T in TMEM)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -511,8 +561,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(q_empty + i, 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, kEwWarps);
+    mbar_init(p_full, kBwdEwWarps);
     mbar_init(done, 1);
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -558,6 +609,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < nblk && ok; ++t) {
         const int st = t & 1;
         if (!mbar_wait(q_full + st, (t >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        // S^T_t / dP^T_t overwrite the P^T / dS^T that block t-1's dV/dK MMAs
+        // read from TMEM; an MMA's TMEM A-operand reads are not ordered with a
+        // later MMA's accumulator writes, so wait for those MMAs to complete.
+        if (t > 0 && !mbar_wait(mma_done, (t - 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t qb = smem_u32(sQ + st * 32768), ob = smem_u32(sO + st * 32768);
 #pragma unroll
@@ -570,21 +628,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 256, tmem + packed_col(kk), mnmajor_desc(ob, kk), idesc_tm, (t > 0 || kk > 0));
+          umma_f16_tmem_a(tmem + 256, tmem + bwd_packed_col(kk), mnmajor_desc(ob, kk), idesc_tm, (t > 0 || kk > 0));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 384, tmem + 128 + packed_col(kk), mnmajor_desc(qb, kk), idesc_tm, (t > 0 || kk > 0));
+          umma_f16_tmem_a(tmem + 384, tmem + 128 + bwd_packed_col(kk), mnmajor_desc(qb, kk), idesc_tm,
+                          (t > 0 || kk > 0));
         umma_commit(q_empty + st);
+        umma_commit(mma_done);
       }
       umma_commit(done);
       mbar_wait(done, 0, timeout_ns, status, kTimeoutDrain, nullptr);
     }
   } else {
-    const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int q = warp & 3;            // TMEM lane quarter (key rows)
+    const int cq = (warp - 2) >> 2;    // 32-column quarter of the query block
+    const int half = cq;               // readout: warps of column quarters 0, 1 write 64 columns each
     const int row = q * 32 + lane;  // key row within the block
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     const float sl2 = scale * kLog2e;
+    __shared__ float lse_l2[kBwdEwWarps][128];
+    const int ew = warp - 2;
     bool ok = true;
     for (int t = 0; t < nblk; ++t) {
       const int st = t & 1;
@@ -593,19 +656,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float* ls = sStat + st * 256;
       const float* ds = sStat + st * 256 + 128;
-      // Per-column LSE in log2 units computed on the fly (ls[c] * log2e).
-      __shared__ float lse_l2[kEwWarps][128];
-      const int ew = warp - 2;
-      // Each warp converts its own copy (no cross-warp sync needed).
-#pragma unroll
-      for (int c = lane; c < 128; c += 32) lse_l2[ew][c] = ls[c] * kLog2e;
+      // Per-column LSE in log2 units for this warp's 32 columns (its own copy).
+      lse_l2[ew][cq * 32 + lane] = ls[cq * 32 + lane] * kLog2e;
       __syncwarp();
-      softmax_grad_row<true>(tmem, lane_base, 0, 128, sl2, lse_l2[ew], ds, 0.f, 0.f, row, t == 0, true, half);
+      softmax_grad_row<true>(tmem, lane_base, 0, 128, sl2, lse_l2[ew], ds, 0.f, 0.f, row, t == 0, true, cq);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && warp_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+    if (cq < 2 && ok && warp_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
       tc_fence_after();
       uint8_t* stg = sQ + (q * 2 + half) * 4096;  // Q stage 0 is dead after the last MMA
       __nv_bfloat16* dK = dqkv + int64_t(row0 + k0 + q * 32) * ld_dqkv + (H + h) * kD + half * 64;
@@ -622,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                           const float* __restrict__ lse, const float* __restrict__ Dvec,
                           __nv_bfloat16* __restrict__ dqkv, int64_t ld_dqkv, int S, int H, float scale,
@@ -641,7 +700,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 5;
   uint64_t* p_full = bars + 6;
   uint64_t* done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* mma_done = bars + 8;  // dQ MMAs of a block completed (they read dS in TMEM)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -659,8 +719,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_empty + i, 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, kEwWarps);
+    mbar_init(p_full, kBwdEwWarps);
     mbar_init(done, 1);
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -704,6 +765,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < nkb && ok; ++j) {
         const int st = j & 1;
         if (!mbar_wait(kv_full + st, (j >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        // dP_j overwrites the dS that block j-1's dQ MMAs read from TMEM: wait
+        // for them (TMEM A-operand reads are not ordered with later writes).
+        if (j > 0 && !mbar_wait(mma_done, (j - 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t kbase = smem_u32(sK + st * 32768), vbase = smem_u32(sV + st * 32768);
 #pragma unroll
@@ -716,16 +783,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 256, tmem + 128 + packed_col(kk), mnmajor_desc(kbase, kk), idesc_tm,
+          umma_f16_tmem_a(tmem + 256, tmem + 128 + bwd_packed_col(kk), mnmajor_desc(kbase, kk), idesc_tm,
                           (j > 0 || kk > 0));
         umma_commit(kv_empty + st);
+        umma_commit(mma_done);
       }
       umma_commit(done);
       mbar_wait(done, 0, timeout_ns, status, kTimeoutDrain, nullptr);
     }
   } else {
-    const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int q = warp & 3;            // TMEM lane quarter (query rows)
+    const int cq = (warp - 2) >> 2;    // 32-column quarter of the key block
+    const int half = cq;               // readout: warps of column quarters 0, 1 write 64 columns each
     const int row = q * 32 + lane;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     const float sl2 = scale * kLog2e;
@@ -736,12 +805,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!warp_wait(s_full, j & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
       tc_fence_after();
       softmax_grad_row<false>(tmem, lane_base, 0, 128, sl2, nullptr, nullptr, lse2, drow, row, j == nkb - 1, false,
-                              half);
+                              cq);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && warp_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+    if (cq < 2 && ok && warp_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
       tc_fence_after();
       uint8_t* stg = sK + (q * 2 + half) * 4096;
       __nv_bfloat16* dQ = dqkv + int64_t(row0 + q0 + q * 32) * ld_dqkv + h * kD + half * 64;
@@ -792,9 +861,9 @@ int attention_bwd_tc(const void* qkv, int64_t ld_qkv, const void* dout, int64_t 
     configured[dev] = true;
   }
   dim3 grid(B * H, S / kBlk);
-  attn_bwd_dkdv_tc_kernel<<<grid, kThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
+  attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
                                                              ld_dqkv, S, H, scale, status, timeout_ns);
-  attn_bwd_dq_tc_kernel<<<grid, kThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
+  attn_bwd_dq_tc_kernel<<<grid, kBwdThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
                                                            ld_dqkv, S, H, scale, status, timeout_ns);
   return int(cudaGetLastError());
 }

@@ -242,26 +242,30 @@ GEMM_SHAPES = ((8192, 8192, 8192), (8192, 12288, 4096), (8192, 16384, 4096), (81
 
 def gemm_case(shapes, timer):
     """Tile kinds (0 single CTA, 1 CTA pair, 2 wide pair, -1 auto) against cuBLAS,
-    with the kernel's own cycle counters (MMA-role cycles and wait fractions)."""
+    with the kernel's own cycle counters (MMA-role cycles and wait fractions).
+    Kind "2u" is the wide tile without the tail split (a grid cap of all SMs
+    turns the split off)."""
     import torch
     from ..ops.gemm import matmul
-    from .._native import check_status
+    from .._native import check_status, lib
     rows = []
+    sms = lib().sm_count()
     for (m, n, k) in shapes:
         a = torch.randn((m, k), device="cuda").to(torch.bfloat16)
         b = torch.randn((n, k), device="cuda").to(torch.bfloat16)
         out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
         ref = torch.mm(a, b.t())
         flops = 2.0 * m * n * k
-        for kind in (0, 1, 2, -1):
-            fn = (lambda kind=kind: matmul(a, b, out=out, bn=256 if kind else 0, pair=kind))
+        for kind in (0, 1, 2, "2u", -1):
+            pair, cap = (2, sms) if kind == "2u" else (kind, 0)
+            fn = (lambda pair=pair, cap=cap: matmul(a, b, out=out, bn=256 if pair else 0, pair=pair, max_ctas=cap))
             fn()
             torch.cuda.synchronize()
             check_status()
             exact = bool(torch.equal(out, ref))
             us = timer.run(fn)
             dbg = torch.zeros(148 * 8, dtype=torch.int64, device="cuda")
-            matmul(a, b, out=out, bn=256 if kind else 0, pair=kind, debug=dbg)
+            matmul(a, b, out=out, bn=256 if pair else 0, pair=pair, max_ctas=cap, debug=dbg)
             torch.cuda.synchronize()
             d = dbg.view(-1, 8).double()
             lead = d[d[:, 1] > 0]
@@ -288,6 +292,19 @@ def gemm_once(m, n, k, kind):
             matmul(a, b, out=out, bn=256 if int(kind) else 0, pair=int(kind))
     torch.cuda.synchronize()
     return [dict(op="gemm_once", kind=kind, m=m, n=n, k=k)]
+
+
+def attention_once(B, S, H):
+    """Three forward + backward calls at one shape (a small, self-ending case for a profiler)."""
+    import torch
+    from ..ops import attention as A
+    qkv = torch.randn((B * S, 3 * H * 128), device="cuda").to(torch.bfloat16)
+    dout = torch.randn((B * S, H * 128), device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        out, lse = A.forward(qkv, B, S, H)
+        A.backward(qkv, out, dout, lse, B, S, H)
+    torch.cuda.synchronize()
+    return [dict(op="attn_once", B=B, S=S, H=H)]
 
 
 def attention_kernel_case(timer, shapes=((4, 2048, 4), (1, 2048, 32), (4, 2048, 32))):
@@ -498,10 +515,13 @@ def fused_emulated_case(m, n, k, world, timer, repeats=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep", "gemm", "gemm_once", "attn_kernel", "nvlink",
-                                     "fused_emulated", "ag_gemm"),
+    ap.add_argument("--op", choices=("gemmrs", "attention", "sweep", "gemm", "gemm_once", "attn_kernel", "attn_once",
+                                     "nvlink", "fused_emulated", "ag_gemm"),
                     default="gemmrs")
     ap.add_argument("--kind", default="2", help="gemm_once: tile kind 0/1/2/-1 or 'cublas'")
+    ap.add_argument("--heads", type=int, default=32, help="attn_once: heads (batch from --batch, length from --seq)")
+    ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=2048)
@@ -535,6 +555,8 @@ def main(argv=None):
         rows += gemm_case(GEMM_SHAPES, timer)
     elif args.op == "gemm_once":
         rows += gemm_once(args.m, args.n, args.k, args.kind)
+    elif args.op == "attn_once":
+        rows += attention_once(args.batch, args.seq, args.heads)
     elif args.op == "attn_kernel":
         rows += attention_kernel_case(timer)
     elif args.op == "nvlink":
