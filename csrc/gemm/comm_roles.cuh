@@ -426,11 +426,21 @@ __device__ void ag_gatherer(const Params& p, uint8_t* smem) {
   if (g.phase & 2)
     for (int step = 1; step < world; ++step)
       if (last_of_step[step] < 0) red_release_sys_add(g.pulled[(rank + step) % world], 1u);  // reads nothing
+  bool own_published = own_jobs == 0;
   for (int j = cta; j < total && ok; j += ctas) {
     if (j < own_jobs) {
       const int64_t off = int64_t(j) * block_bytes;
       ok = stream_block(g.shard + off, local + int64_t(rank) * g.chunk_bytes + off, rank * blocks + j, nullptr);
       continue;
+    }
+    if (!own_published) {
+      // The stream publishes a block only once its stores are kLag groups old.
+      // Before this CTA waits for a peer's block, every own block it copied
+      // must be published: the peer's CTA may be waiting for one of ours the
+      // same way (with few blocks per rank that wait is circular).
+      ok = bs.finish();
+      own_published = true;
+      if (!ok) break;
     }
     const int step = 1 + (j - own_jobs) / blocks, b = (j - own_jobs) % blocks;
     const int c = (rank + step) % world;

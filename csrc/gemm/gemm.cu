@@ -115,6 +115,11 @@ int launch(const GemmCall& c, const Params& p, const CUtensorMap& ma, const CUte
 // not overlapped and its 4x larger tiles quantise into fewer, coarser waves.
 enum TileKind { kSingle = 0, kPair = 1, kWide = 2 };
 
+// The split tail (below) pays only on long K: measured at M=8192, N=4096 it
+// took 5 % off K=16384, nothing at K=4096 and added 5-15 % at K=2048 (the
+// CTA-pair tail launch runs at a lower tensor-pipe occupancy than wide tiles).
+constexpr int kSplitMinK = 8192;
+
 // Wave-model choice between the single-CTA and the wide tile on `sms` SMs.
 int auto_kind(int M, int N, int K, double sms) {
   if (K < 1024 || sms < 2) return kSingle;
@@ -126,7 +131,7 @@ int auto_kind(int M, int N, int K, double sms) {
   // A partial last wave of at most half the clusters runs as CTA-pair tiles
   // (run_split): about half a wide wave instead of a full one.
   const double full = std::floor(tiles_w / clusters), rest = tiles_w - full * clusters;
-  if (full >= 1 && rest > 0 && 2 * rest <= clusters) waves_w = full + 0.55;
+  if (K >= kSplitMinK && full >= 1 && rest > 0 && 2 * rest <= clusters) waves_w = full + 0.55;
   // Per-SM work of one wave: 1 unit (128 x 256 x K) single, 2 units wide.
   const double cost_s = waves_s / kEffSingle;
   const double cost_w = 2.0 * waves_w * (1.0 + kWideEpilogueK / double(K)) / kEffWide;
@@ -147,7 +152,7 @@ int tile_kind(const GemmCall& c, int bn) {
 // tile) in one wave.  Returns the number of wide tiles of the main launch, or
 // 0 when the last wave is more than half full (or the shape does not allow it).
 int split_main_tiles(const GemmCall& c, int tiles_m_w, int tiles_n_w) {
-  if (c.tile_order || c.mode != 0 || c.ag || c.N % 512 || c.max_ctas > 0) return 0;
+  if (c.tile_order || c.mode != 0 || c.ag || c.N % 512 || c.max_ctas > 0 || c.K < kSplitMinK) return 0;
   const int clusters = sm_count() / 2;
   const int tiles = tiles_m_w * tiles_n_w;
   const int full = tiles / clusters, rest = tiles - full * clusters;

@@ -125,6 +125,7 @@ def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True
     from ..parallel.gemm_rs import GemmRS
     from ..parallel import planning
     from ..ops import gemm as G
+    from .._native import check_status
     pk = peaks()
     g = torch.Generator(device="cuda").manual_seed(17 + rank)
     x = torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16)
@@ -156,6 +157,7 @@ def gemmrs_case(m, n, k, rank, world, timer, arms, transports, with_library=True
                     row["stage"] = {key: prof[key] for key in ("producer_last_ns", "consumer_first_ns",
                                                                 "consumer_last_ns", "consumer_tiles",
                                                                 "consumer_tiles_completed_before_producer_end")}
+                check_status()
                 rows.append(row)
                 op.close()
     # GEMM alone (no communication) and the library-only baseline
@@ -411,6 +413,7 @@ def ag_gemm_case(rank, world, timer, m=8192, hidden=4096, ffn=16384):
     import torch
     import torch.distributed as dist
     from ..parallel.ag_gemm import AGGemm
+    from .._native import check_status
     rows = []
     g = torch.Generator(device="cuda").manual_seed(41 + rank)
     shard = torch.randn((m // world, hidden), generator=g, device="cuda").to(torch.bfloat16)
@@ -423,6 +426,7 @@ def ag_gemm_case(rank, world, timer, m=8192, hidden=4096, ffn=16384):
         gather = timer.run(lambda: op.forward(shard, w, out=out, phase=3))
         gemm = timer.run(lambda: op.forward(shard, w, out=out, phase=4))
         prof = op.stage_profile(shard, w, out=out)
+        check_status()  # a timed-out wait would make every later wait return at once: fail here instead
         full = torch.empty((m, hidden), dtype=torch.bfloat16, device="cuda")
         lib_ag = timer.run(lambda: dist.all_gather_into_tensor(full, shard))
         lib_mm = timer.run(lambda: torch.mm(full, w.t(), out=out))

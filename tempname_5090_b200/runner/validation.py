@@ -132,6 +132,7 @@ def fused_operator_check(m: int, hidden: int, ffn: int, group=None, seed: int = 
     import torch.distributed as dist
     from ..ops import gemm as G
     from ..ops import taco
+    from .._native import check_status
     from ..parallel.ag_gemm import AGGemm
     from ..parallel.gemm_rs import GemmRS
     rank, world = dist.get_rank(group), dist.get_world_size(group)
@@ -149,6 +150,7 @@ def fused_operator_check(m: int, hidden: int, ffn: int, group=None, seed: int = 
         kind = ag.tile_kind(ffn // world, 256)
         want = G.matmul(full, w1, bn=256, pair=kind)
         torch.cuda.synchronize()
+        check_status()  # a timed-out device wait raises with its code instead of reading as a mismatch
         ag_ok = bool(torch.equal(ag.gathered, full)) and bool(torch.equal(got, want))
         result["ag_tile_kind"] = kind
     finally:
@@ -170,6 +172,7 @@ def fused_operator_check(m: int, hidden: int, ffn: int, group=None, seed: int = 
         y = taco.ordered_reduce(sources[rank].contiguous(), remote, rank, world)
         want = ((res.float() + y.float()).to(torch.bfloat16).float() + bias.float()).to(torch.bfloat16)
         torch.cuda.synchronize()
+        check_status()
         rs_ok = bool(torch.equal(got, want))
         result["rs_tile_kind"] = rs.tile_kind
         result["rs_transport"] = "nvlink-pull" if rs.pull else "nvlink-push"

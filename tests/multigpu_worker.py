@@ -114,6 +114,24 @@ def case_ag_gemm(rank, world):
         require(torch.equal(op.gathered, f) and torch.equal(out, G.matmul(f, w, bn=256, pair=kind)),
                 "AG->GEMM mismatch")
     op.close()
+    # Eight 128-row blocks per rank on 20 communication CTAs, shard copied by
+    # the gatherers: a CTA copies one own block and then waits for a peer's
+    # block whose owner CTA is in the same position, so own blocks must be
+    # published before that wait (a lazily published own block deadlocked here).
+    m2, k2, n2 = world * 1024, 256, 512
+    shard2 = torch.randn((m2 // world, k2), generator=g, device="cuda").to(torch.bfloat16)
+    w2 = (0.05 * torch.randn((n2, k2), generator=g, device="cuda")).to(torch.bfloat16)
+    full2 = torch.empty((m2, k2), dtype=torch.bfloat16, device="cuda")
+    dist.all_gather_into_tensor(full2, shard2)
+    op = AGGemm(m2, k2, comm_ctas=20, n=n2)
+    for _ in range(2):
+        out = op.forward(shard2, w2, bn=256)
+        torch.cuda.synchronize()
+        check_status()
+        require(torch.equal(op.gathered, full2) and
+                torch.equal(out, G.matmul(full2, w2, bn=256, pair=op.tile_kind(n2, 256))),
+                "AG->GEMM mismatch (copied shard, eight blocks per rank)")
+    op.close()
 
 
 def case_model(rank, world):

@@ -85,12 +85,12 @@ def test_pair_tiles_bitwise_equal_single_cta(kind):
     assert torch.equal(x, y)
 
 
-@pytest.mark.parametrize("M,N,K", [(8192, 4096, 1024), (12288, 4096, 512), (4096, 8192, 768)])
+@pytest.mark.parametrize("M,N,K", [(8192, 4096, 8192), (12288, 4096, 8192)])
 def test_split_wide_gemm_tail_runs_as_pair_tiles(M, N, K):
-    """A wide-tile GEMM whose last wave is at most half full runs that wave as
-    CTA-pair 256 x 256 tiles in a second launch (8192 x 4096: 3 wide waves + a
-    pair wave instead of 4 wide waves); every tile kind accumulates K in the
-    same order, so the result is bitwise the single-CTA one, with epilogues."""
+    """A long-K wide-tile GEMM whose last wave is at most half full runs that
+    wave as CTA-pair 256 x 256 tiles in a second launch (8192 x 4096: 3 wide
+    waves + a pair wave instead of 4 wide waves); every tile kind accumulates K
+    in the same order, so the result is bitwise the single-CTA one, with epilogues."""
     from tempname_5090_b200.ops.gemm import matmul
     from tempname_5090_b200._native import check_status
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
