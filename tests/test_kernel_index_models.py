@@ -5,10 +5,15 @@ the kernel relies on:
 
 * GEMM grouped raster (`tile_coords` in csrc/gemm/gemm_kernel.cuh): a bijection
   from linear tile ids to (tile_m, tile_n) for every tile kind's tile counts.
-* Attention packed probabilities (`packed_col` / `softmax_grad_row` in
+* Attention packed probabilities (`packed_col` for the forward softmax,
+  `bwd_packed_col` / `softmax_grad_row` for the backward, in
   csrc/kernels/attention_tc.cu): the MMA's K-chunk kk finds exactly the BF16
-  pairs the elementwise warp of its half wrote, and each warp writes only inside
-  the 64 score columns it alone reads.
+  pairs the elementwise warp of its half (forward) or column quarter (backward)
+  wrote, and each warp writes only inside the score columns it alone reads.
+* AG gatherer job schedule (`ag_gatherer` in csrc/gemm/comm_roles.cuh): with
+  own blocks published before a CTA's first wait on a peer's block, every
+  rank's CTAs finish for every shape; with the publication lagging behind later
+  stores only, the eight-blocks-per-rank shape of the bench deadlocks.
 * Arrival-first receiver (`rs_reduce_kernel` in csrc/comm/comm.cu): with tiles
   becoming ready in any order, the per-lane claim loop (low-water mark, scan
   window, spread offsets, cyclic nearest ready tile, CAS) claims every tile
@@ -68,6 +73,96 @@ def test_attention_packed_probability_columns():
     for kk in range(8):
         want = [location[16 * kk + 2 * j] for j in range(8)]
         assert want == list(range(packed_col(kk), packed_col(kk) + 8))
+
+
+def bwd_packed_col(kk):
+    return (kk >> 1) * 32 + (kk & 1) * 8
+
+
+def test_attention_backward_packed_columns_per_quarter():
+    # Backward: one warp per 32-column quarter q of a lane quarter; it reads
+    # score columns [32q, 32q+32) and packs pair p (columns 32q+2p, +1) at 32q+p.
+    location = {}
+    for q in range(4):
+        for p in range(16):
+            location[32 * q + 2 * p] = 32 * q + p
+        written = {32 * q + p for p in range(16)}
+        assert written <= set(range(32 * q, 32 * q + 32))
+    for kk in range(8):
+        want = [location[16 * kk + 2 * j] for j in range(8)]
+        assert want == list(range(bwd_packed_col(kk), bwd_packed_col(kk) + 8))
+
+
+def _gatherer_finishes(world, blocks, ctas, pieces, lag=24, publish_before_peer_wait=True):
+    """Every rank's gatherer CTAs run their jobs (own blocks first, then peer
+    blocks in rank+1.. order, job j on CTA j % ctas).  An own block becomes
+    visible to peers once `lag` later pieces were stored by its CTA, when the
+    CTA finishes, or -- with the fix -- before the CTA's first wait on a peer.
+    Returns False if every unfinished CTA waits for a block nobody can publish."""
+    total = blocks + (world - 1) * blocks
+    published = set()           # (rank, block)
+    state = {}
+    for r in range(world):
+        for c in range(ctas):
+            jobs = list(range(c, total, ctas))
+            state[(r, c)] = dict(jobs=jobs, i=0, stored=0, pending=[], flushed=False)
+
+    def retire(r, st, everything=False):
+        keep = []
+        for blk, last in st["pending"]:
+            if everything or last + lag < st["stored"]:
+                published.add((r, blk))
+            else:
+                keep.append((blk, last))
+        st["pending"] = keep
+
+    while True:
+        progress, left = False, False
+        for (r, c), st in state.items():
+            while st["i"] < len(st["jobs"]):
+                j = st["jobs"][st["i"]]
+                if j < blocks:
+                    st["stored"] += pieces
+                    st["pending"].append((j, st["stored"] - 1))
+                    retire(r, st)
+                else:
+                    if publish_before_peer_wait and not st["flushed"]:
+                        retire(r, st, everything=True)
+                        st["flushed"] = True
+                    step, b = 1 + (j - blocks) // blocks, (j - blocks) % blocks
+                    if ((r + step) % world, b) not in published:
+                        break
+                    for _ in range(pieces):  # the stream retires after every store
+                        st["stored"] += 1
+                        retire(r, st)
+                st["i"] += 1
+                progress = True
+            if st["i"] == len(st["jobs"]):
+                if st["pending"]:
+                    retire(r, st, everything=True)
+                    progress = True
+            else:
+                left = True
+        if not left:
+            return True
+        if not progress:
+            return False
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("blocks", [1, 2, 8, 32])
+@pytest.mark.parametrize("ctas", [3, 16, 20, 32])
+@pytest.mark.parametrize("pieces", [4, 64])
+def test_gatherer_schedule_always_finishes(world, blocks, ctas, pieces):
+    assert _gatherer_finishes(world, blocks, ctas, pieces)
+
+
+def test_lagged_own_block_publication_deadlocks_at_the_bench_shape():
+    # M=8192 at TP8: eight 128-row blocks per rank, 20 communication CTAs,
+    # K=4096 (64 pieces of 16 KB per block): the schedule without the fix.
+    assert not _gatherer_finishes(8, 8, 20, 64, publish_before_peer_wait=False)
+    assert not _gatherer_finishes(4, 16, 20, 64, publish_before_peer_wait=False)
+    assert _gatherer_finishes(2, 32, 20, 64, publish_before_peer_wait=False)
 
 
 def _simulate_arrival(tiles, chunk_tiles, ctas, ready_order, rng, window=128):
