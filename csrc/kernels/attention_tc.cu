@@ -437,6 +437,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   dQ:    CTA per 128-query block; for each key block j <= the query block:
 //          S = Q K_j^T, dP = dO V_j^T; dS = P (dP - D); dQ += dS K_j.
 // ============================================================================
+// Optional per-CTA cycle counters of the backward kernels (8 words per CTA,
+// CTA id blockIdx.y * gridDim.x + blockIdx.x; each word has one writer):
+// [0] MMA thread waiting for Q/dO or K/V tiles, [1] waiting for the
+// elementwise warps, [2] waiting for the previous block's MMAs, [3] MMA thread
+// total; [4] elementwise warp 2 waiting for S/dP, [5] its elementwise work,
+// [6] blocks.
+// The counters compile away in the kernels launched without them (kOn false).
+template <bool kOn>
+struct BwdTrace {
+  unsigned long long* w;
+  __device__ long long now() const {
+    if constexpr (kOn) return clock64();
+    return 0;
+  }
+  __device__ void add(int i, long long since) const {
+    if constexpr (kOn) w[i] += (unsigned long long)(clock64() - since);
+  }
+  __device__ void count(int i) const {
+    if constexpr (kOn) w[i] += 1;
+  }
+};
+
 constexpr int kBwdSmTotal = 6 * 32768 + 2048 + 256 + 1024;
 
 // cp.async.bulk (non-tensor) global -> shared, completion counted on `bar`.
@@ -519,11 +541,13 @@ __device__ __forceinline__ void store_tmem_rows(uint32_t tmem_row, float mul, ui
   __syncwarp();
 }
 
+template <bool kTrace>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                             const float* __restrict__ lse, const float* __restrict__ Dvec,
                             __nv_bfloat16* __restrict__ dqkv, int64_t ld_dqkv, int S, int H, float scale,
-                            int* status, uint64_t timeout_ns) {
+                            int* status, uint64_t timeout_ns,
+                            unsigned long long* dbg) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // [K 32K][V 32K][Q st0 32K][Q st1 32K][dO st0 32K][dO st1 32K][LSE/D 2 x 1K][bars]
@@ -544,6 +568,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const BwdTrace<kTrace> trc{kTrace ? dbg + 8 * (size_t(blockIdx.y) * gridDim.x + blockIdx.x) : nullptr};
   // Grid (B*H, S/128), x-fastest: small key blocks carry the most query blocks
   // and run first for every head.
   const int bh = blockIdx.x;
@@ -603,12 +628,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
       const uint32_t idesc_tm = make_idesc_bf16(128, 128, 0, 1);
+      const long long t_start = trc.now();
+      long long tw = trc.now();
       bool ok = mbar_wait(kv_full, 0, timeout_ns, status, kTimeoutMmaFull, abort_flag);
+      trc.add(0, tw);
       tc_fence_after();
       const uint32_t kbase = smem_u32(sK), vbase = smem_u32(sV);
       for (int t = 0; t < nblk && ok; ++t) {
         const int st = t & 1;
+        tw = trc.now();
         if (!mbar_wait(q_full + st, (t >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        trc.add(0, tw);
+        tw = trc.now();
         // S^T_t / dP^T_t overwrite the P^T / dS^T that block t-1's dV/dK MMAs
         // read from TMEM; an MMA's TMEM A-operand reads are not ordered with a
         // later MMA's accumulator writes, so wait for those MMAs to complete.
@@ -616,6 +647,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           ok = false;
           break;
         }
+        trc.add(2, tw);
         tc_fence_after();
         const uint32_t qb = smem_u32(sQ + st * 32768), ob = smem_u32(sO + st * 32768);
 #pragma unroll
@@ -624,7 +656,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int kk = 0; kk < 8; ++kk)
           umma_f16(tmem + 128, kmajor_desc(vbase, kk), kmajor_desc(ob, kk), idesc_kk, kk > 0);
         umma_commit(s_full);
+        tw = trc.now();
         if (!mbar_wait(p_full, t & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        trc.add(1, tw);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -638,6 +672,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       umma_commit(done);
       mbar_wait(done, 0, timeout_ns, status, kTimeoutDrain, nullptr);
+      trc.add(3, t_start);
     }
   } else {
     const int q = warp & 3;            // TMEM lane quarter (key rows)
@@ -649,9 +684,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     __shared__ float lse_l2[kBwdEwWarps][128];
     const int ew = warp - 2;
     bool ok = true;
+    const bool tracer = warp == 2 && lane == 0;
     for (int t = 0; t < nblk; ++t) {
       const int st = t & 1;
+      const long long tw = tracer ? trc.now() : 0;
       if (!warp_wait(s_full, t & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
+      if (tracer) trc.add(4, tw);
+      const long long tk = tracer ? trc.now() : 0;
       // q_full(t) has completed before the MMA warp issued S^T(t): the stats are in smem.
       tc_fence_after();
       const float* ls = sStat + st * 256;
@@ -663,6 +702,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (tracer) {
+        trc.add(5, tk);
+        trc.count(6);
+      }
     }
     if (cq < 2 && ok && warp_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
       tc_fence_after();
@@ -681,11 +724,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+template <bool kTrace>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                           const float* __restrict__ lse, const float* __restrict__ Dvec,
                           __nv_bfloat16* __restrict__ dqkv, int64_t ld_dqkv, int S, int H, float scale,
-                          int* status, uint64_t timeout_ns) {
+                          int* status, uint64_t timeout_ns,
+                          unsigned long long* dbg) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // [Q 32K][dO 32K][K st0 32K][K st1 32K][V st0 32K][V st1 32K][bars]
@@ -705,6 +750,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const BwdTrace<kTrace> trc{kTrace ? dbg + 8 * (size_t(blockIdx.y) * gridDim.x + blockIdx.x) : nullptr};
   const int bh = blockIdx.x;  // grid (B*H, S/128), x-fastest: heavy query tiles first
   const int qt = int(gridDim.y) - 1 - int(blockIdx.y);
   const int b = bh / H, h = bh % H;
@@ -759,18 +805,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
       const uint32_t idesc_tm = make_idesc_bf16(128, 128, 0, 1);
+      const long long t_start = trc.now();
+      long long tw = trc.now();
       bool ok = mbar_wait(q_full, 0, timeout_ns, status, kTimeoutMmaFull, abort_flag);
+      trc.add(0, tw);
       tc_fence_after();
       const uint32_t qbase = smem_u32(sQ), obase = smem_u32(sO);
       for (int j = 0; j < nkb && ok; ++j) {
         const int st = j & 1;
+        tw = trc.now();
         if (!mbar_wait(kv_full + st, (j >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        trc.add(0, tw);
+        tw = trc.now();
         // dP_j overwrites the dS that block j-1's dQ MMAs read from TMEM: wait
         // for them (TMEM A-operand reads are not ordered with later writes).
         if (j > 0 && !mbar_wait(mma_done, (j - 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
           ok = false;
           break;
         }
+        trc.add(2, tw);
         tc_fence_after();
         const uint32_t kbase = smem_u32(sK + st * 32768), vbase = smem_u32(sV + st * 32768);
 #pragma unroll
@@ -779,7 +832,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int kk = 0; kk < 8; ++kk)
           umma_f16(tmem + 128, kmajor_desc(obase, kk), kmajor_desc(vbase, kk), idesc_kk, kk > 0);
         umma_commit(s_full);
+        tw = trc.now();
         if (!mbar_wait(p_full, j & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+        trc.add(1, tw);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -790,6 +845,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       umma_commit(done);
       mbar_wait(done, 0, timeout_ns, status, kTimeoutDrain, nullptr);
+      trc.add(3, t_start);
     }
   } else {
     const int q = warp & 3;            // TMEM lane quarter (query rows)
@@ -801,14 +857,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float lse2 = lse[int64_t(bh) * S + q0 + row] * kLog2e;
     const float drow = Dvec[int64_t(bh) * S + q0 + row];
     bool ok = true;
+    const bool tracer = warp == 2 && lane == 0;
     for (int j = 0; j < nkb; ++j) {
+      const long long tw = tracer ? trc.now() : 0;
       if (!warp_wait(s_full, j & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) { ok = false; break; }
+      if (tracer) trc.add(4, tw);
+      const long long tk = tracer ? trc.now() : 0;
       tc_fence_after();
       softmax_grad_row<false>(tmem, lane_base, 0, 128, sl2, nullptr, nullptr, lse2, drow, row, j == nkb - 1, false,
                               cq);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (tracer) {
+        trc.add(5, tk);
+        trc.count(6);
+      }
     }
     if (cq < 2 && ok && warp_wait(done, 0, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
       tc_fence_after();
@@ -847,7 +911,8 @@ int attention_fwd_tc(const void* qkv, int64_t ld_qkv, void* out, int64_t ld_out,
 
 int attention_bwd_tc(const void* qkv, int64_t ld_qkv, const void* dout, int64_t ld_dout, const float* lse,
                      const float* Dvec, void* dqkv, int64_t ld_dqkv, int B, int S, int H, float scale, int* status,
-                     uint64_t timeout_ns, cudaStream_t s) {
+                     uint64_t timeout_ns, cudaStream_t s, unsigned long long* dbg_dkdv,
+                     unsigned long long* dbg_dq) {
   if (S % kBlk || ld_qkv % 8 || ld_dout % 8 || ld_dqkv % 8) return -1;
   CUtensorMap mq, mo;
   if (!make_map(&mq, qkv, uint64_t(3) * H * kD, uint64_t(B) * S, uint64_t(ld_qkv))) return -1;
@@ -856,15 +921,25 @@ int attention_bwd_tc(const void* qkv, int64_t ld_qkv, const void* dout, int64_t 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
-    cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
+    cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
+    cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
+    cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
+    cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmTotal);
     configured[dev] = true;
   }
   dim3 grid(B * H, S / kBlk);
-  attn_bwd_dkdv_tc_kernel<<<grid, kBwdThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
-                                                             ld_dqkv, S, H, scale, status, timeout_ns);
-  attn_bwd_dq_tc_kernel<<<grid, kBwdThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, static_cast<__nv_bfloat16*>(dqkv),
-                                                           ld_dqkv, S, H, scale, status, timeout_ns);
+  __nv_bfloat16* dq = static_cast<__nv_bfloat16*>(dqkv);
+  if (dbg_dkdv && dbg_dq) {
+    attn_bwd_dkdv_tc_kernel<true><<<grid, kBwdThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, dq, ld_dqkv, S, H, scale,
+                                                                        status, timeout_ns, dbg_dkdv);
+    attn_bwd_dq_tc_kernel<true><<<grid, kBwdThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, dq, ld_dqkv, S, H, scale,
+                                                                      status, timeout_ns, dbg_dq);
+  } else {
+    attn_bwd_dkdv_tc_kernel<false><<<grid, kBwdThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, dq, ld_dqkv, S, H, scale,
+                                                                         status, timeout_ns, nullptr);
+    attn_bwd_dq_tc_kernel<false><<<grid, kBwdThreads, kBwdSmTotal, s>>>(mq, mo, lse, Dvec, dq, ld_dqkv, S, H, scale,
+                                                                       status, timeout_ns, nullptr);
+  }
   return int(cudaGetLastError());
 }
 

@@ -58,6 +58,7 @@ int attention_bwd_pre(const void* out, int64_t ld_out, const void* dout, int64_t
                       int S, int H, cudaStream_t s);
 int attention_bwd_tc(const void* qkv, int64_t ld_qkv, const void* dout, int64_t ld_dout, const float* lse,
                      const float* Dvec, void* dqkv, int64_t ld_dqkv, int B, int S, int H, float scale, int* status,
-                     uint64_t timeout_ns, cudaStream_t s);
+                     uint64_t timeout_ns, cudaStream_t s, unsigned long long* dbg_dkdv = nullptr,
+                     unsigned long long* dbg_dq = nullptr);
 }  // namespace kernels
 }  // namespace tn5b

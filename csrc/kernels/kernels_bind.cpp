@@ -182,9 +182,17 @@ void attention_fwd_tc(const at::Tensor& qkv, at::Tensor& out, at::Tensor& lse, i
                          reinterpret_cast<unsigned long long*>(trace)),
      "attention_fwd_tc");
 }
+// Optional [2, CTAs, 8] int64 cycle counters of the backward kernels (dK/dV, dQ).
+unsigned long long* dbg_words(const c10::optional<at::Tensor>& dbg, int kernel, int64_t ctas) {
+  if (!dbg) return nullptr;
+  TORCH_CHECK(dbg->is_cuda() && dbg->scalar_type() == at::kLong && dbg->is_contiguous() &&
+                  dbg->numel() == 2 * ctas * 8,
+              "attention debug counters must be a contiguous int64 [2, B*H*S/128, 8] CUDA tensor");
+  return reinterpret_cast<unsigned long long*>(dbg->data_ptr<int64_t>()) + kernel * ctas * 8;
+}
 void attention_bwd_tc(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
                       at::Tensor& Dvec, at::Tensor& dqkv, int64_t B, int64_t S, int64_t H, double scale,
-                      const at::Tensor& status, int64_t timeout_ns) {
+                      const at::Tensor& status, int64_t timeout_ns, const c10::optional<at::Tensor>& dbg) {
   need(qkv, at::kBFloat16, "qkv", false); need(out, at::kBFloat16, "out", false);
   need(dout, at::kBFloat16, "dout", false); need(dqkv, at::kBFloat16, "dqkv", false);
   need(lse, at::kFloat, "lse"); need(Dvec, at::kFloat, "D");
@@ -194,7 +202,9 @@ void attention_bwd_tc(const at::Tensor& qkv, const at::Tensor& out, const at::Te
                           int(B), int(S), int(H), cur()), "attention_bwd_pre");
   ok(k::attention_bwd_tc(qkv.data_ptr(), qkv.stride(0), dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(),
                          Dvec.data_ptr<float>(), dqkv.data_ptr(), dqkv.stride(0), int(B), int(S), int(H), float(scale),
-                         status.data_ptr<int>(), uint64_t(timeout_ns), cur()), "attention_bwd_tc");
+                         status.data_ptr<int>(), uint64_t(timeout_ns), cur(), dbg_words(dbg, 0, B * H * (S / 128)),
+                         dbg_words(dbg, 1, B * H * (S / 128))),
+     "attention_bwd_tc");
 }
 }  // namespace
 

@@ -49,14 +49,19 @@ def forward(qkv: torch.Tensor, B: int, S: int, H: int, out: torch.Tensor | None 
     return o, lse.reshape(B * H, S)
 
 
-def backward(qkv, out, dout, lse, B: int, S: int, H: int, dqkv: torch.Tensor | None = None):
+def backward(qkv, out, dout, lse, B: int, S: int, H: int, dqkv: torch.Tensor | None = None,
+             debug: torch.Tensor | None = None):
+    """`debug`: optional zeroed int64 [2, B*H*S/128, 8] CUDA tensor that receives
+    the dK/dV and dQ kernels' per-CTA cycle counters (MMA thread waiting for
+    tiles / for the elementwise warps / for the previous block's MMAs, MMA total;
+    one elementwise warp waiting for S and dP / working; blocks)."""
     d = qkv.shape[1] // (3 * H)
     scale = 1.0 / math.sqrt(d)
     if qkv.is_cuda:
         dqkv = torch.empty_like(qkv) if dqkv is None else dqkv
         Dvec = torch.empty((B * H, S), dtype=torch.float32, device=qkv.device)
         lib().attention_bwd_tc(qkv, out, dout, lse, Dvec, dqkv, B, S, H, scale, status_tensor(qkv.device),
-                               TIMEOUT_NS)
+                               TIMEOUT_NS, debug)
         count_launch(3)
         return dqkv
     q, k, v = _split(qkv, B, S, H, d)

@@ -328,6 +328,18 @@ def attention_kernel_case(timer, shapes=((4, 2048, 4), (1, 2048, 32), (4, 2048, 
         g = dqkv.float().reshape(B, S, 3, H, d).permute(2, 0, 3, 1, 4)
         rel = lambda x, y: ((x - y).norm() / y.norm()).item()
         again = A.backward(qkv, out, dout, lse, B, S, H)
+        dbg = torch.zeros((2, B * H * (S // 128), 8), dtype=torch.int64, device="cuda")
+        A.backward(qkv, out, dout, lse, B, S, H, debug=dbg)
+        torch.cuda.synchronize()
+        phases = {}
+        for name, c in zip(("dkdv", "dq"), dbg.double().cpu()):
+            blocks = c[:, 6].sum().item()
+            mma = c[:, 3].sum().item()
+            phases[name] = dict(mma_wait_tiles=c[:, 0].sum().item() / mma, mma_wait_elementwise=c[:, 1].sum().item() / mma,
+                                mma_wait_prev_mma=c[:, 2].sum().item() / mma,
+                                ew_wait_cycles_per_block=c[:, 4].sum().item() / blocks,
+                                ew_work_cycles_per_block=c[:, 5].sum().item() / blocks,
+                                mma_cycles_per_block=mma / blocks)
         flops = 4.0 * B * H * S * S * d / 2
         fwd_us = timer.run(lambda: A.forward(qkv, B, S, H, out=out))
         bwd_us = timer.run(lambda: A.backward(qkv, out, dout, lse, B, S, H, dqkv=dqkv))
@@ -335,7 +347,7 @@ def attention_kernel_case(timer, shapes=((4, 2048, 4), (1, 2048, 32), (4, 2048, 
                          fwd_tflops=flops / fwd_us / 1e6, bwd_tflops=2.5 * flops / bwd_us / 1e6,
                          out_rel_err=rel(out.float(), o.detach()), dq_rel_err=rel(g[0], q.grad),
                          dk_rel_err=rel(g[1], k.grad), dv_rel_err=rel(g[2], v.grad),
-                         backward_deterministic=bool(torch.equal(again, dqkv))))
+                         backward_deterministic=bool(torch.equal(again, dqkv)), backward_phases=phases))
     return rows
 
 
