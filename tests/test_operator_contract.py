@@ -42,7 +42,7 @@ class _FakeLib:
             raise RuntimeError("injected launch failure")
         self.calls.append(("push", dict(mode=mode, recv=recv_ptrs, flags=flag_ptrs, epoch=epoch,
                                         order=tile_order.tolist(), rank=rank, world=world,
-                                        delay=(delay_tile, delay_ns))))
+                                        delay=(delay_tile, delay_ns), slot=slot_bytes, chunk=chunk_rows)))
 
     def gemm_rs_pull(self, x, a_mn, w, b_mn, partial_local, partial_ptrs, flag_ptrs, my_flags, rank, world, epoch,
                      tile_order, consumer_order, out, residual, bias, status, timeout_ns, comm_ctas, phase, stamps,
@@ -59,7 +59,8 @@ class _FakeLib:
                   out, residual, bias, order, arrival, claims, status, timeout_ns, max_ctas, stamps):
         self.calls.append(("reduce", dict(recv=recv, flags=flags, epoch=epoch, quantized=quantized,
                                           arrival=arrival, claims=claims is not None, order=order.tolist(),
-                                          residual=residual is not None, bias=bias is not None)))
+                                          residual=residual is not None, bias=bias is not None,
+                                          slot=slot_bytes, chunk=chunk_rows)))
 
 
 @pytest.mark.parametrize("arm", ["flux", "flux_taco", "flux_taco_interleaved", "flux_taco_interleaved_arrival"])
@@ -116,6 +117,9 @@ def test_nvlink_transport_launch_contract(monkeypatch, arm, rank, world):
         assert p["recv"] == recv[call & 1].ptrs.data_ptr() and r["recv"] == recv[call & 1].local
         assert p["flags"] == flags.ptrs.data_ptr() and r["flags"] == flags.local
         assert p["mode"] == (2 if quantized else 1) and r["quantized"] == quantized
+        # both sides address the owner's two lane regions with the same layout
+        lanes = mapping.PushLanes(M // world, N, CHUNK, world)
+        assert p["slot"] == r["slot"] == lanes.lane_slot_bytes and p["chunk"] == r["chunk"] == CHUNK
         assert r["arrival"] == arm.endswith("arrival") and r["claims"] == arm.endswith("arrival")
         assert p["order"] == production and r["order"] == consumer
         assert r["residual"] and not r["bias"]
