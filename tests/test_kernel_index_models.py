@@ -10,6 +10,9 @@ the kernel relies on:
   csrc/kernels/attention_tc.cu): the MMA's K-chunk kk finds exactly the BF16
   pairs the elementwise warp of its half (forward) or column quarter (backward)
   wrote, and each warp writes only inside the score columns it alone reads.
+* Pull GemmRS buffer reuse (`GemmRS` parity buffers, `rs_reducer`): with ranks
+  at arbitrary relative speeds, no reducer reads a source's partial buffer
+  after that source overwrote it with a later call's partial.
 * AG gatherer job schedule (`ag_gatherer` in csrc/gemm/comm_roles.cuh): with
   own blocks published before a CTA's first wait on a peer's block, every
   rank's CTAs finish for every shape; with the publication lagging behind later
@@ -213,3 +216,50 @@ def test_arrival_claims_every_tile_once_and_terminates(tiles, chunk_tiles, ctas)
         assert sorted(claims) == list(range(tiles))
         for tile, cta in claims.items():
             assert (tile // chunk_tiles) % 2 == cta & 1  # claimed by a CTA of its lane
+
+
+def _pull_rs_reuse_is_safe(world, calls, rng):
+    """Pull GemmRS across calls with ranks at arbitrary relative speeds.  Each
+    rank's call t runs as one launch: its GEMM writes partial buffer t % 2 and
+    publishes the flag (epoch t) to every owner; its reducer waits for every
+    source's epoch-t flag and reads that source's buffer t % 2.  A rank's call
+    t+1 starts only after its call t ended (stream order).  Returns False if a
+    reader ever finds a buffer already overwritten by a later call."""
+    buf = [[0, 0] for _ in range(world)]          # call id held by each rank's two buffers
+    flags = [0] * world                           # latest epoch each rank published
+    # per rank: (call, stage) with stage 0 = GEMM pending, 1.. = reading source stage-1
+    state = [[1, 0] for _ in range(world)]
+    done = 0
+    while done < world:
+        r = rng.randrange(world)
+        call, stage = state[r]
+        if call > calls:
+            continue
+        if stage == 0:
+            buf[r][call % 2] = call
+            flags[r] = call
+            state[r][1] = 1
+            continue
+        s = stage - 1
+        if flags[s] < call:
+            # wait: is anyone able to move?  (no deadlock: every rank's flags only rise)
+            if all(state[q][0] > calls or (state[q][1] >= 1 and flags[state[q][1] - 1] < state[q][0])
+                   for q in range(world)):
+                return False  # everyone waits
+            continue
+        if buf[s][call % 2] != call:
+            return False      # the source already overwrote the data of this call
+        if s == world - 1:
+            state[r] = [call + 1, 0]
+            if call + 1 > calls:
+                done += 1
+        else:
+            state[r][1] = stage + 1
+    return True
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_pull_rs_parity_buffers_are_never_overwritten_while_read(world):
+    rng = random.Random(world)
+    for _ in range(200):
+        assert _pull_rs_reuse_is_safe(world, 6, rng)
