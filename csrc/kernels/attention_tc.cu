@@ -742,11 +742,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = bars + 3;
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* done = bars + 7;
-  uint64_t* mma_done = bars + 8;  // dQ MMAs of a block completed (they read dS in TMEM)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* s_full = bars + 5;    // S_j and dP_j in TMEM
+  uint64_t* consumed = bars + 6;  // every elementwise warp holds its S_j, dP_j in registers
+  uint64_t* p_full = bars + 7;    // dS_j written (packed BF16, columns of its own)
+  uint64_t* dq_done = bars + 8;   // dQ += dS_j K_j finished reading dS_j
+  uint64_t* done = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -765,9 +766,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(kv_empty + i, 1);
     }
     mbar_init(s_full, 1);
+    mbar_init(consumed, kBwdEwWarps);
     mbar_init(p_full, kBwdEwWarps);
+    mbar_init(dq_done, 1);
     mbar_init(done, 1);
-    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -803,6 +805,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // TMEM: S [0,128), dP [128,256), dQ [256,384), dS packed BF16 [384,448).
+      // dS has columns of its own, so S_j and dP_j are issued as soon as every
+      // elementwise warp holds S_{j-1}, dP_{j-1} in registers (`consumed`) and
+      // run while the warps compute dS_{j-1}; dQ += dS_{j-1} K_{j-1} follows.
+      // No MMA writes columns that an earlier MMA reads as its A operand.
       const uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);
       const uint32_t idesc_tm = make_idesc_bf16(128, 128, 0, 1);
       const long long t_start = trc.now();
@@ -811,37 +818,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       trc.add(0, tw);
       tc_fence_after();
       const uint32_t qbase = smem_u32(sQ), obase = smem_u32(sO);
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        tw = trc.now();
-        if (!mbar_wait(kv_full + st, (j >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
-        trc.add(0, tw);
-        tw = trc.now();
-        // dP_j overwrites the dS that block j-1's dQ MMAs read from TMEM: wait
-        // for them (TMEM A-operand reads are not ordered with later writes).
-        if (j > 0 && !mbar_wait(mma_done, (j - 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
-          ok = false;
-          break;
+      for (int j = 0; j <= nkb && ok; ++j) {
+        if (j < nkb) {
+          const int st = j & 1;
+          tw = trc.now();
+          if (!mbar_wait(kv_full + st, (j >> 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+          trc.add(0, tw);
+          tw = trc.now();
+          if (j > 0 && !mbar_wait(consumed, (j - 1) & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          trc.add(1, tw);
+          tc_fence_after();
+          const uint32_t kbase = smem_u32(sK + st * 32768), vbase = smem_u32(sV + st * 32768);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) umma_f16(tmem, kmajor_desc(qbase, kk), kmajor_desc(kbase, kk), idesc_kk, kk > 0);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tmem + 128, kmajor_desc(obase, kk), kmajor_desc(vbase, kk), idesc_kk, kk > 0);
+          umma_commit(s_full);
         }
-        trc.add(2, tw);
-        tc_fence_after();
-        const uint32_t kbase = smem_u32(sK + st * 32768), vbase = smem_u32(sV + st * 32768);
+        if (j > 0) {
+          const int pj = j - 1, pst = pj & 1;
+          tw = trc.now();
+          if (!mbar_wait(p_full, pj & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
+          trc.add(1, tw);
+          tc_fence_after();
+          const uint32_t kbase = smem_u32(sK + pst * 32768);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) umma_f16(tmem, kmajor_desc(qbase, kk), kmajor_desc(kbase, kk), idesc_kk, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16(tmem + 128, kmajor_desc(obase, kk), kmajor_desc(vbase, kk), idesc_kk, kk > 0);
-        umma_commit(s_full);
-        tw = trc.now();
-        if (!mbar_wait(p_full, j & 1, timeout_ns, status, kTimeoutMmaFull, abort_flag)) { ok = false; break; }
-        trc.add(1, tw);
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16_tmem_a(tmem + 256, tmem + 128 + bwd_packed_col(kk), mnmajor_desc(kbase, kk), idesc_tm,
-                          (j > 0 || kk > 0));
-        umma_commit(kv_empty + st);
-        umma_commit(mma_done);
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16_tmem_a(tmem + 256, tmem + 384 + uint32_t(8 * kk), mnmajor_desc(kbase, kk), idesc_tm,
+                            (pj > 0 || kk > 0));
+          umma_commit(kv_empty + pst);
+          umma_commit(dq_done);
+        }
       }
       umma_commit(done);
       mbar_wait(done, 0, timeout_ns, status, kTimeoutDrain, nullptr);
@@ -864,8 +875,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (tracer) trc.add(4, tw);
       const long long tk = tracer ? trc.now() : 0;
       tc_fence_after();
-      softmax_grad_row<false>(tmem, lane_base, 0, 128, sl2, nullptr, nullptr, lse2, drow, row, j == nkb - 1, false,
-                              cq);
+      uint32_t rs[32], rd[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + uint32_t(cq * 32), rs);
+      tmem_ld_32x32b_x32(tmem + lane_base + uint32_t(128 + cq * 32), rd);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(consumed);
+      // dS = P (dP - D), P = exp2(S * scale * log2e - LSE * log2e); keys > query masked.
+      const bool diag = j == nkb - 1;
+      uint32_t wd[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        float dd[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int c = cq * 32 + i + e;
+          const bool masked = diag && (c > row);
+          const float p = masked ? 0.f : ex2(fmaf(__uint_as_float(rs[i + e]), sl2, -lse2));
+          dd[e] = p * (__uint_as_float(rd[i + e]) - drow);
+        }
+        wd[i / 2] = pack2(dd[0], dd[1]);
+      }
+      // dQ += dS_{j-1} K_{j-1} must have read the dS columns before they are rewritten.
+      if (j > 0 && !warp_wait(dq_done, (j - 1) & 1, timeout_ns, status, kTimeoutEpiTmemFull, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      tmem_st_32x32b_x16(tmem + lane_base + uint32_t(384 + cq * 16), wd);  // key chunks 2cq, 2cq+1
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
