@@ -96,6 +96,17 @@ def test_attention_backward_packed_columns_per_quarter():
         assert want == list(range(bwd_packed_col(kk), bwd_packed_col(kk) + 8))
 
 
+def test_attention_dq_ds_columns_of_their_own():
+    # dQ kernel: warp of column quarter q packs dS pair p (keys 32q+2p, +1) at
+    # 384 + 16q + p; the dQ MMA reads key chunk kk at [384 + 8kk, +8), outside
+    # the S / dP / dQ columns [0, 384).
+    location = {32 * q + 2 * p: 384 + 16 * q + p for q in range(4) for p in range(16)}
+    for kk in range(8):
+        want = [location[16 * kk + 2 * j] for j in range(8)]
+        assert want == list(range(384 + 8 * kk, 384 + 8 * kk + 8))
+    assert min(location.values()) >= 384 and max(location.values()) < 448
+
+
 def _gatherer_finishes(world, blocks, ctas, pieces, lag=24, publish_before_peer_wait=True):
     """Every rank's gatherer CTAs run their jobs (own blocks first, then peer
     blocks in rank+1.. order, job j on CTA j % ctas).  An own block becomes
